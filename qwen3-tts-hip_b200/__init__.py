@@ -1,0 +1,13 @@
+"""B200-native Qwen3-TTS token loop (talker decode step + CodePredictor pass).
+
+Import name ``qwen3_tts_hip_b200`` (the directory is ``qwen3-tts-hip_b200/``;
+``__graft_entry__.load_package()`` registers it). Compute lives in
+``libqtts_b200.so`` built from ``csrc/`` for sm_100a; this package is the
+host-side mirror of the reference's ``HipTtsEngine`` API over its C ABI.
+"""
+from .engine import (  # noqa: F401
+    SAMPLE_RATE, EngineOptions, Error, Finished, GenerateOptions, GeneratedCodes,
+    GeneratedCodesChunk, HipTextStream, HipTtsEngine, HipTtsStream, InvalidInput,
+    NeedMoreText, PollingTextStream, StreamOptions, TextStreamInput, TextStreamOptions,
+    TtsPreparedInputs, lib, library_path, start_text_stream, SIGNATURES,
+)

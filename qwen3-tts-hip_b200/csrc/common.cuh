@@ -1,0 +1,75 @@
+// Shared device helpers for the sm_100a Qwen3-TTS token-loop kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qtts {
+
+constexpr int kHeadDim = 128;  // Qwen3-TTS talker and CodePredictor head_dim
+
+// ---- programmatic dependent launch (PDL) --------------------------------
+// Every kernel calls pdl_wait() before it touches memory written by the
+// previous kernel on the stream; weights may be fetched before it.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// 16-byte streaming load of constant weights: non-coherent path, no L1 allocation.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+__device__ __forceinline__ void unpack8(uint4 u, float f[8]) {
+  f[0] = bf16lo(u.x); f[1] = bf16hi(u.x);
+  f[2] = bf16lo(u.y); f[3] = bf16hi(u.y);
+  f[4] = bf16lo(u.z); f[5] = bf16hi(u.z);
+  f[6] = bf16lo(u.w); f[7] = bf16hi(u.w);
+}
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// Paged bf16 KV cache view. A physical page holds `1 << page_shift` positions
+// of every layer: [layer][k|v][kv_head][page_pos][head_dim].
+struct KvView {
+  __nv_bfloat16* pool;
+  const int* page_table;  // logical page -> physical page
+  int page_shift;
+  int kv_heads;
+  long long page_stride;   // elements per physical page
+  long long layer_stride;  // elements per layer inside a page
+};
+
+__device__ __forceinline__ __nv_bfloat16* kv_ptr(const KvView& v, int layer, int kind,
+                                                 int head, int pos) {
+  const int page = v.page_table[pos >> v.page_shift];
+  const int inpage = pos & ((1 << v.page_shift) - 1);
+  return v.pool + (long long)page * v.page_stride + (long long)layer * v.layer_stride +
+         ((long long)((kind * v.kv_heads + head) << v.page_shift) + inpage) * kHeadDim;
+}
+
+}  // namespace qtts

@@ -1,0 +1,1476 @@
+// Host engine for the B200 Qwen3-TTS token loop, and the C ABI of qtts_b200.h.
+//
+// Mirrors piedshag/qwen3-tts-hip's HipTtsEngine (src/generation.rs) around
+// the sm_100a kernels of kernels.cu:
+//   load                 HipTtsEngine::load_with_options   generation.rs:284-315
+//   text prep on device  TtsTextPrep::prepare_*            text.rs:348-382,516-603
+//   talker prefill       HipTalker::prefill_token*         talker.rs:207-233
+//   frame loop           HipTtsEngine::rollout             generation.rs:657-749
+//   streams              HipTtsStream / PollingTextStream  generation.rs:876-963,1086-1451
+// Every frame (15 CodePredictor groups + talker decode step + token
+// selection) is one CUDA graph launch; loop state lives on the device, so a
+// whole generation is enqueued without host round trips and the host reads
+// the codes once at the end (or once per stream chunk).
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <deque>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "json.h"
+#include "kernels.h"
+#include "qtts_b200.h"
+
+namespace qtts {
+namespace {
+
+thread_local std::string g_last_error;
+
+struct QttsError : std::runtime_error {
+  int code;
+  QttsError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+[[noreturn]] void fail(int code, const std::string& m) { throw QttsError(code, m); }
+[[noreturn]] void invalid(const std::string& m) { fail(QTTS_ERR_INVALID_INPUT, m); }
+
+#define QCK(expr)                                                                     \
+  do {                                                                                \
+    cudaError_t e_ = (expr);                                                          \
+    if (e_ != cudaSuccess)                                                            \
+      ::qtts::fail(QTTS_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr uint64_t kSeedXor = 0x9e3779b97f4a7c15ull;  // generation.rs:667
+constexpr int kNewline = 198;                          // text.rs:15
+constexpr int kTalkerPageShift = 5;                    // 32 positions per KV page
+constexpr int kTalkerSplits = 16;                      // decode attention splits
+
+// ---------------------------------------------------------------------------
+// safetensors (8-byte LE header length, JSON header, raw little-endian data)
+// ---------------------------------------------------------------------------
+struct TensorRef {
+  std::string dtype;
+  std::vector<long long> shape;
+  const uint8_t* data = nullptr;
+  size_t nbytes = 0;
+  long long numel() const {
+    long long n = 1;
+    for (long long s : shape) n *= s;
+    return n;
+  }
+};
+
+class SafeTensors {
+ public:
+  explicit SafeTensors(const std::string& path) {
+    fd_ = ::open(path.c_str(), O_RDONLY);
+    if (fd_ < 0) fail(QTTS_ERR_IO, "failed to open " + path);
+    struct stat sb;
+    if (fstat(fd_, &sb) != 0 || sb.st_size < 8) fail(QTTS_ERR_IO, "bad safetensors file " + path);
+    size_ = (size_t)sb.st_size;
+    map_ = mmap(nullptr, size_, PROT_READ, MAP_PRIVATE, fd_, 0);
+    if (map_ == MAP_FAILED) fail(QTTS_ERR_IO, "mmap failed for " + path);
+    const uint8_t* p = static_cast<const uint8_t*>(map_);
+    uint64_t hlen = 0;
+    std::memcpy(&hlen, p, 8);
+    if (8 + hlen > size_) fail(QTTS_ERR_IO, "truncated safetensors header in " + path);
+    try {
+      header_ = Json::parse(reinterpret_cast<const char*>(p + 8), hlen);
+    } catch (const std::exception& e) {
+      fail(QTTS_ERR_IO, std::string("bad safetensors header: ") + e.what());
+    }
+    base_ = p + 8 + hlen;
+    data_size_ = size_ - 8 - hlen;
+  }
+  ~SafeTensors() {
+    if (map_ && map_ != MAP_FAILED) munmap(map_, size_);
+    if (fd_ >= 0) ::close(fd_);
+  }
+  bool has(const std::string& name) const { return header_.has(name); }
+  TensorRef get(const std::string& name) const {
+    if (!header_.has(name)) invalid("failed to load " + name + ": tensor not found");
+    const Json& m = header_.at(name);
+    TensorRef t;
+    t.dtype = m.string("dtype");
+    for (const Json& s : m.at("shape").arr) t.shape.push_back((long long)s.num);
+    const Json& off = m.at("data_offsets");
+    const size_t b = (size_t)off.arr.at(0).num, e = (size_t)off.arr.at(1).num;
+    if (e < b || e > data_size_) fail(QTTS_ERR_IO, "tensor " + name + " outside file");
+    t.data = base_ + b;
+    t.nbytes = e - b;
+    const size_t esz = t.dtype == "BF16" ? 2 : t.dtype == "F32" ? 4 : 0;
+    if (esz == 0) invalid(name + " has dtype " + t.dtype + ", expected F32 or BF16");
+    if ((size_t)t.numel() * esz != t.nbytes) fail(QTTS_ERR_IO, "tensor " + name + " size mismatch");
+    return t;
+  }
+
+ private:
+  int fd_ = -1;
+  void* map_ = nullptr;
+  size_t size_ = 0, data_size_ = 0;
+  const uint8_t* base_ = nullptr;
+  Json header_;
+};
+
+uint16_t f32_to_bf16(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+float bf16_to_f32(uint16_t b) {
+  uint32_t u = (uint32_t)b << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+// ---------------------------------------------------------------------------
+// configuration (src/model/config.rs:47-150)
+// ---------------------------------------------------------------------------
+struct StackCfg {
+  int hidden, intermediate, layers, q_heads, kv_heads, head_dim, vocab, groups;
+  float eps, theta;
+};
+
+struct ModelCfg {
+  StackCfg talker, cp;
+  int codec_bos, codec_eos, codec_pad, codec_think, codec_think_bos, codec_think_eos;
+  std::map<std::string, int> language_ids, speaker_ids;
+  int tts_pad, tts_bos, tts_eos, im_start, assistant;
+};
+
+StackCfg stack_cfg(const Json& j) {
+  StackCfg c;
+  c.hidden = (int)j.integer("hidden_size");
+  c.intermediate = (int)j.integer("intermediate_size");
+  c.layers = (int)j.integer("num_hidden_layers");
+  c.q_heads = (int)j.integer("num_attention_heads");
+  c.kv_heads = (int)j.integer("num_key_value_heads");
+  c.head_dim = (int)j.integer("head_dim");
+  c.vocab = (int)j.integer("vocab_size");
+  c.groups = (int)j.integer("num_code_groups");
+  c.eps = (float)j.number("rms_norm_eps");
+  c.theta = (float)j.number("rope_theta");
+  return c;
+}
+
+ModelCfg load_config(const std::string& dir) {
+  const std::string path = dir + "/config.json";
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) invalid("failed to read " + path);
+  std::string text;
+  char buf[65536];
+  size_t n;
+  while ((n = std::fread(buf, 1, sizeof buf, f)) > 0) text.append(buf, n);
+  std::fclose(f);
+  Json raw;
+  try {
+    raw = Json::parse(text.data(), text.size());
+  } catch (const std::exception& e) {
+    invalid("failed to parse " + path + ": " + e.what());
+  }
+  ModelCfg m;
+  try {
+    const Json& t = raw.at("talker_config");
+    m.talker = stack_cfg(t);
+    m.cp = stack_cfg(t.at("code_predictor_config"));
+    m.codec_bos = (int)t.integer("codec_bos_id");
+    m.codec_eos = (int)t.integer("codec_eos_token_id");
+    m.codec_pad = (int)t.integer("codec_pad_id");
+    m.codec_think = (int)t.integer("codec_think_id");
+    m.codec_think_bos = (int)t.integer("codec_think_bos_id");
+    m.codec_think_eos = (int)t.integer("codec_think_eos_id");
+    for (auto& kv : t.at("codec_language_id").obj) m.language_ids[kv.first] = (int)kv.second.num;
+    for (auto& kv : t.at("spk_id").obj) m.speaker_ids[kv.first] = (int)kv.second.num;
+    m.tts_pad = (int)raw.integer("tts_pad_token_id");
+    m.tts_bos = (int)raw.integer("tts_bos_token_id");
+    m.tts_eos = (int)raw.integer("tts_eos_token_id");
+    m.im_start = (int)raw.integer("im_start_token_id");
+    m.assistant = (int)raw.integer("assistant_token_id");
+  } catch (const QttsError&) {
+    throw;
+  } catch (const std::exception& e) {
+    invalid("failed to parse " + path + ": " + e.what());
+  }
+  return m;
+}
+
+// ---------------------------------------------------------------------------
+// device memory
+// ---------------------------------------------------------------------------
+class Arena {
+ public:
+  ~Arena() {
+    for (void* p : ptrs_) cudaFree(p);
+  }
+  template <typename T>
+  T* alloc(size_t count) {
+    void* p = nullptr;
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    QCK(cudaMalloc(&p, bytes));
+    QCK(cudaMemset(p, 0, bytes));
+    ptrs_.push_back(p);
+    bytes_ += bytes;
+    return static_cast<T*>(p);
+  }
+  size_t bytes() const { return bytes_; }
+
+ private:
+  std::vector<void*> ptrs_;
+  size_t bytes_ = 0;
+};
+
+struct DevStack {
+  StackCfg c;
+  int q_out, kv_out, qkv_w;
+  std::vector<__nv_bfloat16*> wqkv, wo, wgu, wdown;
+  std::vector<float*> in_g, post_g, q_g, k_g;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+};
+
+struct StackBufs {
+  float *x, *qkv, *q, *attn, *h1, *act;
+};
+
+struct SampleKey {
+  SampleCfg t, s;
+  float penalty;
+  int last;
+  bool operator<(const SampleKey& o) const { return std::memcmp(this, &o, sizeof *this) < 0; }
+};
+
+SampleCfg talker_cfg(const qtts_generate_options& o) {
+  return SampleCfg{o.do_sample ? 1 : 0, (int)o.top_k, o.top_p, o.temperature};
+}
+SampleCfg sub_cfg(const qtts_generate_options& o) {
+  return SampleCfg{o.subtalker_dosample ? 1 : 0, (int)o.subtalker_top_k, o.subtalker_top_p,
+                   o.subtalker_temperature};
+}
+
+class Engine {
+ public:
+  Engine(const std::string& dir, int device, size_t max_cache_steps);
+  ~Engine();
+
+  ModelCfg cfg;
+  size_t max_cache_steps;
+  int device;
+  cudaStream_t stream = nullptr;
+  Arena arena;
+
+  // weights
+  DevStack talker, cp;
+  __nv_bfloat16 *head = nullptr, *codec_emb = nullptr, *text_emb = nullptr;
+  __nv_bfloat16 *fc1 = nullptr, *fc2 = nullptr, *cp_heads = nullptr, *cp_embs = nullptr;
+  __nv_bfloat16* proj_w = nullptr;
+  float *norm_g = nullptr, *fc1_b = nullptr, *fc2_b = nullptr, *cp_norm_g = nullptr,
+        *proj_b = nullptr;
+  int text_vocab = 0, text_hidden = 0, text_inter = 0;
+
+  // workspaces
+  StackBufs tb{}, cb{};
+  KvView tkv{}, ckv{};
+  float *partial = nullptr, *logits = nullptr, *dbg_logits = nullptr;
+  unsigned* tickets = nullptr;
+  SeqState* st = nullptr;
+  SeqState* st_host = nullptr;  // pinned
+  int *codes = nullptr, *history = nullptr, *token = nullptr;
+  float *trailing = nullptr, *tts_pad = nullptr, *cp_prefix = nullptr, *cp_next = nullptr,
+        *emb_sum = nullptr, *xvec = nullptr;
+  int *tp_ids = nullptr, *tp_pidx = nullptr, *tp_cids = nullptr;
+  float *tp_a = nullptr, *tp_b = nullptr, *tp_c = nullptr;
+  int tp_rows = 0;
+  std::vector<int> pinned_ids_storage;
+
+  std::map<SampleKey, cudaGraphExec_t> graphs;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
+  float last_prefill_ms = 0.f, last_frames_ms = 0.f;
+  size_t last_frames = 0;
+
+  // current sequence (host view)
+  int seq_P = 0;
+  int seq_frames = 0;
+  int seq_semantic = -1;
+  bool seq_ended = false;
+  size_t seq_max_frames = 0;
+  qtts_generate_options seq_opts{};
+  uint64_t seq_id = 0;
+
+  bool has_proj() const { return cfg.cp.hidden != cfg.talker.hidden; }
+  float* cp_prefix_target() const { return has_proj() ? cp_prefix : cb.x; }
+  float* cp_next_target() const { return has_proj() ? cp_next : cb.x; }
+
+  // ---- launch helpers ----
+  void linear(const __nv_bfloat16* W, const float* x, int ldx, const float* gamma, float eps,
+              float* y, int ldy, const float* resid, int ldr, const float* bias, int M, int N,
+              int K, Epilogue epi, const int* halt) {
+    LinearArgs a{W, x, ldx, gamma, eps, y, ldy, resid, ldr, bias, M, N, K, halt};
+    QCK(launch_linear(a, epi, stream));
+  }
+  void stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int pos0, const int* halt);
+  void stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* pos_ptr, int pos_const,
+                  int nsplit, const int* halt);
+  HeadArgs head_args(int role, const SampleCfg& c, const int* halt);
+  void talker_head(int role, const float* x, const SampleCfg& c, float penalty, const int* halt,
+                   float* cp_prefix_dst);
+  void cp_head(int group, const float* x, const SampleCfg& c, const int* halt);
+  void enqueue_frame(const SampleKey& k);
+  cudaGraphExec_t frame_graph(const SampleKey& k);
+
+  // ---- text prep ----
+  void project_text(const std::vector<int>& ids, float* out);
+  int prepare(const uint32_t* ids, size_t n, size_t lookahead, const char* speaker,
+              const char* language, const float* xvec_host, int* n_trailing);
+  void check_ids(const uint32_t* ids, size_t n);
+
+  // ---- sequence ----
+  void validate(const qtts_generate_options& o) const;
+  void begin(int P, int n_trailing, const qtts_generate_options& o);
+  size_t run_frames(size_t n);
+  void read_codes(size_t from, size_t to, int32_t* out);
+  void sync_state();
+};
+
+// ---------------------------------------------------------------------------
+void upload_bf16(Arena& arena, const TensorRef& t, __nv_bfloat16* dst) {
+  if (t.dtype == "BF16") {
+    QCK(cudaMemcpy(dst, t.data, t.nbytes, cudaMemcpyHostToDevice));
+    return;
+  }
+  std::vector<uint16_t> tmp((size_t)t.numel());
+  const float* f = reinterpret_cast<const float*>(t.data);
+  for (size_t i = 0; i < tmp.size(); ++i) tmp[i] = f32_to_bf16(f[i]);
+  QCK(cudaMemcpy(dst, tmp.data(), tmp.size() * 2, cudaMemcpyHostToDevice));
+  (void)arena;
+}
+
+std::vector<float> to_f32(const TensorRef& t) {
+  std::vector<float> out((size_t)t.numel());
+  if (t.dtype == "F32") {
+    std::memcpy(out.data(), t.data, t.nbytes);
+  } else {
+    const uint16_t* b = reinterpret_cast<const uint16_t*>(t.data);
+    for (size_t i = 0; i < out.size(); ++i) out[i] = bf16_to_f32(b[i]);
+  }
+  return out;
+}
+
+void expect_shape(const std::string& name, const TensorRef& t, std::vector<long long> shape) {
+  if (t.shape != shape) {
+    std::string s = name + " shape [";
+    for (size_t i = 0; i < t.shape.size(); ++i) s += (i ? "," : "") + std::to_string(t.shape[i]);
+    s += "] does not match the config";
+    invalid(s);
+  }
+}
+
+float* upload_f32(Arena& arena, const SafeTensors& st, const std::string& name, long long n) {
+  TensorRef t = st.get(name);
+  expect_shape(name, t, {n});
+  std::vector<float> v = to_f32(t);
+  float* d = arena.alloc<float>((size_t)n);
+  QCK(cudaMemcpy(d, v.data(), n * 4, cudaMemcpyHostToDevice));
+  return d;
+}
+
+__nv_bfloat16* upload_matrix(Arena& arena, const SafeTensors& st, const std::string& name,
+                             long long rows, long long cols) {
+  TensorRef t = st.get(name);
+  expect_shape(name, t, {rows, cols});
+  __nv_bfloat16* d = arena.alloc<__nv_bfloat16>((size_t)(rows * cols));
+  upload_bf16(arena, t, d);
+  return d;
+}
+
+void load_stack(Arena& arena, const SafeTensors& st, const std::string& prefix, const StackCfg& c,
+                int rope_positions, DevStack& S) {
+  if (c.head_dim != kHeadDim) invalid("head_dim must be 128");
+  if (c.layers <= 0) invalid("layer count must be non-zero");
+  if (c.hidden % 256 != 0 || c.intermediate % 256 != 0)
+    invalid("hidden and intermediate sizes must be multiples of 256");
+  if (c.kv_heads <= 0 || c.q_heads % c.kv_heads != 0) invalid("q_heads must be a multiple of kv_heads");
+  const int g = c.q_heads / c.kv_heads;
+  if (g != 1 && g != 2 && g != 4) invalid("q_heads / kv_heads must be 1, 2 or 4");
+  S.c = c;
+  S.q_out = c.q_heads * c.head_dim;
+  S.kv_out = c.kv_heads * c.head_dim;
+  S.qkv_w = S.q_out + 2 * S.kv_out;
+  const long long H = c.hidden, I = c.intermediate;
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = prefix + "." + std::to_string(l);
+    // One allocation per layer: [qkv rows | o | gate rows, up rows | down].
+    const size_t n_qkv = (size_t)S.qkv_w * H, n_o = (size_t)H * S.q_out, n_gu = (size_t)2 * I * H,
+                 n_d = (size_t)H * I;
+    __nv_bfloat16* base = arena.alloc<__nv_bfloat16>(n_qkv + n_o + n_gu + n_d);
+    auto put = [&](const std::string& name, long long rows, long long cols, __nv_bfloat16* dst) {
+      TensorRef t = st.get(name);
+      expect_shape(name, t, {rows, cols});
+      upload_bf16(arena, t, dst);
+    };
+    put(p + ".self_attn.q_proj.weight", S.q_out, H, base);
+    put(p + ".self_attn.k_proj.weight", S.kv_out, H, base + (size_t)S.q_out * H);
+    put(p + ".self_attn.v_proj.weight", S.kv_out, H, base + (size_t)(S.q_out + S.kv_out) * H);
+    put(p + ".self_attn.o_proj.weight", H, S.q_out, base + n_qkv);
+    put(p + ".mlp.gate_proj.weight", I, H, base + n_qkv + n_o);
+    put(p + ".mlp.up_proj.weight", I, H, base + n_qkv + n_o + (size_t)I * H);
+    put(p + ".mlp.down_proj.weight", H, I, base + n_qkv + n_o + n_gu);
+    S.wqkv.push_back(base);
+    S.wo.push_back(base + n_qkv);
+    S.wgu.push_back(base + n_qkv + n_o);
+    S.wdown.push_back(base + n_qkv + n_o + n_gu);
+    S.in_g.push_back(upload_f32(arena, st, p + ".input_layernorm.weight", H));
+    S.post_g.push_back(upload_f32(arena, st, p + ".post_attention_layernorm.weight", H));
+    S.q_g.push_back(upload_f32(arena, st, p + ".self_attn.q_norm.weight", c.head_dim));
+    S.k_g.push_back(upload_f32(arena, st, p + ".self_attn.k_norm.weight", c.head_dim));
+  }
+  // RoPE table: angle = pos / powf(theta, 2i/d) in fp32 (kernels.rs:64-67).
+  std::vector<float> cs((size_t)rope_positions * 64), sn((size_t)rope_positions * 64);
+  for (int p = 0; p < rope_positions; ++p)
+    for (int i = 0; i < 64; ++i) {
+      const float expo = (float)(i * 2) / (float)c.head_dim;
+      const float ang = (float)p / powf(c.theta, expo);
+      cs[(size_t)p * 64 + i] = cosf(ang);
+      sn[(size_t)p * 64 + i] = sinf(ang);
+    }
+  S.rope_cos = arena.alloc<float>(cs.size());
+  S.rope_sin = arena.alloc<float>(sn.size());
+  QCK(cudaMemcpy(S.rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  QCK(cudaMemcpy(S.rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+}
+
+StackBufs alloc_bufs(Arena& arena, const DevStack& S, int rows) {
+  StackBufs b;
+  const size_t H = S.c.hidden, I = S.c.intermediate;
+  b.x = arena.alloc<float>(rows * H);
+  b.qkv = arena.alloc<float>((size_t)rows * S.qkv_w);
+  b.q = arena.alloc<float>((size_t)rows * S.q_out);
+  b.attn = arena.alloc<float>((size_t)rows * S.q_out);
+  b.h1 = arena.alloc<float>(rows * H);
+  b.act = arena.alloc<float>(rows * I);
+  return b;
+}
+
+Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mcs), device(dev) {
+  if (mcs == 0) invalid("max_cache_steps must be non-zero");
+  cfg = load_config(dir);
+  int ndev = 0;
+  QCK(cudaGetDeviceCount(&ndev));
+  if (dev < 0 || dev >= ndev) invalid("device " + std::to_string(dev) + " not present");
+  QCK(cudaSetDevice(dev));
+  QCK(configure_kernels());
+  QCK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  QCK(cudaEventCreate(&ev0));
+  QCK(cudaEventCreate(&ev1));
+  QCK(cudaEventCreate(&ev2));
+  const StackCfg& T = cfg.talker;
+  const StackCfg& C = cfg.cp;
+  if (C.groups < 2) invalid("CodePredictor needs at least one semantic and one acoustic group");
+  if (T.groups != C.groups) invalid("talker and CodePredictor num_code_groups differ");
+  if (T.vocab > max_sample_vocab() || C.vocab > max_sample_vocab())
+    invalid("vocab larger than the sampler supports");
+  if (T.vocab <= 1024) invalid("talker vocab must exceed the 1024 suppressed control ids");
+
+  SafeTensors sf(dir + "/model.safetensors");
+  const SafeTensors& st_ = sf;
+  load_stack(arena, st_, "talker.model.layers", T, (int)mcs, talker);
+  load_stack(arena, st_, "talker.code_predictor.model.layers", C, C.groups, cp);
+  norm_g = upload_f32(arena, st_, "talker.model.norm.weight", T.hidden);
+  head = upload_matrix(arena, st_, "talker.codec_head.weight", T.vocab, T.hidden);
+  codec_emb = upload_matrix(arena, st_, "talker.model.codec_embedding.weight", T.vocab, T.hidden);
+  {
+    TensorRef te = st_.get("talker.model.text_embedding.weight");
+    if (te.shape.size() != 2 || (te.shape[1] != T.hidden && te.shape[1] != 2048))
+      invalid("talker.model.text_embedding.weight shape; expected [vocab, text_hidden]");
+    text_vocab = (int)te.shape[0];
+    text_hidden = (int)te.shape[1];
+    text_emb = arena.alloc<__nv_bfloat16>((size_t)te.numel());
+    upload_bf16(arena, te, text_emb);
+    TensorRef f1 = st_.get("talker.text_projection.linear_fc1.weight");
+    if (f1.shape.size() != 2 || f1.shape[1] != text_hidden)
+      invalid("invalid text projection shapes");
+    text_inter = (int)f1.shape[0];
+    if (text_inter % 256 != 0 || text_hidden % 256 != 0)
+      invalid("text projection widths must be multiples of 256");
+    fc1 = upload_matrix(arena, st_, "talker.text_projection.linear_fc1.weight", text_inter,
+                        text_hidden);
+    fc1_b = upload_f32(arena, st_, "talker.text_projection.linear_fc1.bias", text_inter);
+    fc2 = upload_matrix(arena, st_, "talker.text_projection.linear_fc2.weight", T.hidden,
+                        text_inter);
+    fc2_b = upload_f32(arena, st_, "talker.text_projection.linear_fc2.bias", T.hidden);
+  }
+  cp_norm_g = upload_f32(arena, st_, "talker.code_predictor.model.norm.weight", C.hidden);
+  const int na = C.groups - 1;
+  cp_heads = arena.alloc<__nv_bfloat16>((size_t)na * C.vocab * C.hidden);
+  cp_embs = arena.alloc<__nv_bfloat16>((size_t)na * C.vocab * T.hidden);
+  for (int g = 0; g < na; ++g) {
+    const std::string hn = "talker.code_predictor.lm_head." + std::to_string(g) + ".weight";
+    TensorRef h = st_.get(hn);
+    expect_shape(hn, h, {C.vocab, C.hidden});
+    upload_bf16(arena, h, cp_heads + (size_t)g * C.vocab * C.hidden);
+    const std::string en =
+        "talker.code_predictor.model.codec_embedding." + std::to_string(g) + ".weight";
+    TensorRef e = st_.get(en);
+    expect_shape(en, e, {C.vocab, T.hidden});
+    upload_bf16(arena, e, cp_embs + (size_t)g * C.vocab * T.hidden);
+  }
+  if (has_proj()) {
+    proj_w = upload_matrix(arena, st_, "talker.code_predictor.small_to_mtp_projection.weight",
+                           C.hidden, T.hidden);
+    proj_b = upload_f32(arena, st_, "talker.code_predictor.small_to_mtp_projection.bias", C.hidden);
+  }
+
+  // workspaces
+  const int rows = (int)mcs;
+  tb = alloc_bufs(arena, talker, rows);
+  cb = alloc_bufs(arena, cp, 2);
+  {
+    const int shift = kTalkerPageShift;
+    const int pages = (int)((mcs + (1u << shift) - 1) >> shift);
+    tkv.page_shift = shift;
+    tkv.kv_heads = T.kv_heads;
+    tkv.layer_stride = (long long)2 * T.kv_heads * (1 << shift) * kHeadDim;
+    tkv.page_stride = tkv.layer_stride * T.layers;
+    tkv.pool = arena.alloc<__nv_bfloat16>((size_t)(tkv.page_stride * pages));
+    std::vector<int> pt(pages);
+    for (int i = 0; i < pages; ++i) pt[i] = i;
+    int* d = arena.alloc<int>(pages);
+    QCK(cudaMemcpy(d, pt.data(), pages * 4, cudaMemcpyHostToDevice));
+    tkv.page_table = d;
+  }
+  {
+    int shift = 0;
+    while ((1 << shift) < C.groups) ++shift;
+    ckv.page_shift = shift;
+    ckv.kv_heads = C.kv_heads;
+    ckv.layer_stride = (long long)2 * C.kv_heads * (1 << shift) * kHeadDim;
+    ckv.page_stride = ckv.layer_stride * C.layers;
+    ckv.pool = arena.alloc<__nv_bfloat16>((size_t)ckv.page_stride);
+    ckv.page_table = arena.alloc<int>(1);
+  }
+  partial = arena.alloc<float>((size_t)std::max(T.q_heads, C.q_heads) * kTalkerSplits *
+                               (2 + kHeadDim));
+  logits = arena.alloc<float>(std::max(T.vocab, C.vocab));
+  dbg_logits = arena.alloc<float>((size_t)na * C.vocab);
+  tickets = arena.alloc<unsigned>(64);
+  st = arena.alloc<SeqState>(1);
+  QCK(cudaMallocHost(&st_host, sizeof(SeqState)));
+  codes = arena.alloc<int>(mcs * C.groups);
+  history = arena.alloc<int>(mcs);
+  token = arena.alloc<int>(4);
+  trailing = arena.alloc<float>((mcs + 1) * T.hidden);
+  tts_pad = arena.alloc<float>(T.hidden);
+  cp_prefix = arena.alloc<float>(2 * (size_t)T.hidden);
+  cp_next = arena.alloc<float>(T.hidden);
+  emb_sum = arena.alloc<float>(T.hidden);
+  xvec = arena.alloc<float>(T.hidden);
+  tp_rows = (int)mcs + 16;
+  tp_ids = arena.alloc<int>(tp_rows);
+  tp_pidx = arena.alloc<int>(tp_rows);
+  tp_cids = arena.alloc<int>(tp_rows);
+  tp_a = arena.alloc<float>((size_t)tp_rows * text_hidden);
+  tp_b = arena.alloc<float>((size_t)tp_rows * text_inter);
+  tp_c = arena.alloc<float>((size_t)tp_rows * T.hidden);
+  QCK(cudaDeviceSynchronize());
+}
+
+Engine::~Engine() {
+  cudaSetDevice(device);
+  if (stream) cudaStreamSynchronize(stream);
+  for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+  if (st_host) cudaFreeHost(st_host);
+  if (ev0) cudaEventDestroy(ev0);
+  if (ev1) cudaEventDestroy(ev1);
+  if (ev2) cudaEventDestroy(ev2);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+// Decoder layers over M rows at positions pos0.. (prefill_forward, decode.rs:1077-1298).
+void Engine::stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int pos0,
+                        const int* halt) {
+  const StackCfg& c = S.c;
+  const float scale = 1.0f / std::sqrt((float)c.head_dim);
+  for (int l = 0; l < c.layers; ++l) {
+    linear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr, M,
+           S.qkv_w, c.hidden, EPI_STORE, halt);
+    QkPrepArgs qa{B.qkv, S.q_g[l], S.k_g[l], c.eps, S.rope_cos, S.rope_sin, kv, l, pos0, M,
+                  c.q_heads, B.q, halt};
+    QCK(launch_qk_prep(qa, stream));
+    AttnPrefillArgs pa{B.q, kv, l, pos0, M, c.q_heads, scale, B.attn, halt};
+    QCK(launch_attn_prefill(pa, stream));
+    linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, M,
+           c.hidden, S.q_out, EPI_RESID, halt);
+    linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
+           nullptr, M, c.intermediate, c.hidden, EPI_SWIGLU, halt);
+    linear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.x, c.hidden, B.h1, c.hidden,
+           nullptr, M, c.hidden, c.intermediate, EPI_RESID, halt);
+  }
+}
+
+// One position through all layers (decode_step_layer_on_stream, decode.rs:1694-1894).
+void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* pos_ptr,
+                        int pos_const, int nsplit, const int* halt) {
+  const StackCfg& c = S.c;
+  const float scale = 1.0f / std::sqrt((float)c.head_dim);
+  for (int l = 0; l < c.layers; ++l) {
+    linear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr, 1,
+           S.qkv_w, c.hidden, EPI_STORE, halt);
+    AttnDecodeArgs da{B.qkv,   S.q_g[l],  S.k_g[l], c.eps,   S.rope_cos, S.rope_sin,
+                      kv,      l,         pos_ptr,  pos_const, c.q_heads, scale,
+                      partial, tickets + 8, B.attn, nsplit,  halt};
+    QCK(launch_attn_decode(da, stream));
+    linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, 1,
+           c.hidden, S.q_out, EPI_RESID, halt);
+    linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
+           nullptr, 1, c.intermediate, c.hidden, EPI_SWIGLU, halt);
+    linear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.x, c.hidden, B.h1, c.hidden,
+           nullptr, 1, c.hidden, c.intermediate, EPI_RESID, halt);
+  }
+}
+
+HeadArgs Engine::head_args(int role, const SampleCfg& c, const int* halt) {
+  HeadArgs a{};
+  a.ticket = tickets;
+  a.role = role;
+  a.cfg = c;
+  a.st = st;
+  a.penalty = 1.0f;
+  a.history = history;
+  a.eos_token = cfg.codec_eos;
+  a.talker_codec_emb = codec_emb;
+  a.H = cfg.talker.hidden;
+  a.groups = cfg.cp.groups;
+  a.codes = codes;
+  a.history_out = history;
+  a.lin.halt = halt;
+  return a;
+}
+
+void Engine::talker_head(int role, const float* x, const SampleCfg& c, float penalty,
+                         const int* halt, float* cp_prefix_dst) {
+  HeadArgs a = head_args(role, c, halt);
+  const StackCfg& T = cfg.talker;
+  a.lin = LinearArgs{head,    x,       T.hidden, norm_g,  T.eps,   logits, T.vocab,
+                     nullptr, 0,       nullptr,  1,       T.vocab, T.hidden, halt};
+  a.penalty = penalty;
+  a.suppress = 1;
+  a.cp_prefix = cp_prefix_dst;
+  a.token_out = token;
+  QCK(launch_head(a, stream));
+}
+
+void Engine::cp_head(int group, const float* x, const SampleCfg& c, const int* halt) {
+  HeadArgs a = head_args(ROLE_CP_GROUP, c, halt);
+  const StackCfg& C = cfg.cp;
+  a.lin = LinearArgs{cp_heads + (size_t)group * C.vocab * C.hidden,
+                     x, C.hidden, cp_norm_g, C.eps, logits, C.vocab, nullptr, 0, nullptr, 1,
+                     C.vocab, C.hidden, halt};
+  a.group = group;
+  a.last_group = C.groups - 2;
+  a.cp_emb = cp_embs + (size_t)group * C.vocab * cfg.talker.hidden;
+  a.cp_next = cp_next_target();
+  a.emb_sum = emb_sum;
+  a.step_in = tb.x;
+  a.trailing = trailing;
+  a.tts_pad = tts_pad;
+  QCK(launch_head(a, stream));
+}
+
+// One frame: CodePredictor pass (code_predictor.rs:366-471) then, unless it is
+// the last frame, the talker decode step and its token (generation.rs:718-740).
+void Engine::enqueue_frame(const SampleKey& k) {
+  const int* halt = &st->halt;
+  const StackCfg& C = cfg.cp;
+  const int H = cfg.talker.hidden;
+  if (has_proj())
+    linear(proj_w, cp_prefix, H, nullptr, 0.f, cb.x, C.hidden, nullptr, 0, proj_b, 2, C.hidden,
+           H, EPI_BIAS, halt);
+  stack_rows(cp, cb, ckv, 2, 0, halt);
+  cp_head(0, cb.x + C.hidden, k.s, halt);
+  for (int g = 1; g < C.groups - 1; ++g) {
+    if (has_proj())
+      linear(proj_w, cp_next, H, nullptr, 0.f, cb.x, C.hidden, nullptr, 0, proj_b, 1, C.hidden,
+             H, EPI_BIAS, halt);
+    stack_step(cp, cb, ckv, nullptr, g + 1, 1, halt);
+    cp_head(g, cb.x, k.s, halt);
+  }
+  if (!k.last) {
+    stack_step(talker, tb, tkv, &st->talker_pos, 0, kTalkerSplits, halt);
+    talker_head(ROLE_TALKER_STEP, tb.x, k.t, k.penalty, halt, cp_prefix_target());
+  }
+}
+
+cudaGraphExec_t Engine::frame_graph(const SampleKey& k) {
+  auto it = graphs.find(k);
+  if (it != graphs.end()) return it->second;
+  cudaGraph_t g = nullptr;
+  QCK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    enqueue_frame(k);
+  } catch (...) {
+    cudaStreamEndCapture(stream, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  QCK(cudaStreamEndCapture(stream, &g));
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+  cudaGraphDestroy(g);
+  QCK(e);
+  graphs[k] = exec;
+  return exec;
+}
+
+// ---- text prep on the device (text.rs:571-602) ----------------------------
+void Engine::check_ids(const uint32_t* ids, size_t n) {
+  for (size_t i = 0; i < n; ++i)
+    if ((long long)ids[i] >= text_vocab)
+      invalid("text token " + std::to_string(ids[i]) + " is out of range for vocab " +
+              std::to_string(text_vocab));
+}
+
+void Engine::project_text(const std::vector<int>& ids, float* out) {
+  const int n = (int)ids.size();
+  if (n == 0) return;
+  if (n > tp_rows) invalid("too many text rows");
+  QCK(cudaMemcpyAsync(tp_ids, ids.data(), n * 4, cudaMemcpyHostToDevice, stream));
+  QCK(launch_gather_rows(text_emb, tp_ids, n, text_hidden, tp_a, stream));
+  linear(fc1, tp_a, text_hidden, nullptr, 0.f, tp_b, text_inter, nullptr, 0, fc1_b, n,
+         text_inter, text_hidden, EPI_BIAS_SILU, nullptr);
+  linear(fc2, tp_b, text_inter, nullptr, 0.f, out, cfg.talker.hidden, nullptr, 0, fc2_b, n,
+         cfg.talker.hidden, text_inter, EPI_BIAS, nullptr);
+  QCK(cudaStreamSynchronize(stream));  // ids buffer is pageable host memory
+}
+
+// prepare_custom_voice_with_lookahead / prepare_voice_clone_xvector_with_lookahead
+// (text.rs:348-382,432-514): writes the prefill rows into the talker input, the
+// trailing rows and tts_pad row into their device buffers; returns P.
+int Engine::prepare(const uint32_t* ids, size_t n, size_t lookahead, const char* speaker,
+                    const char* language, const float* xvec_host, int* n_trailing) {
+  check_ids(ids, n);
+  const std::string spk = speaker ? speaker : "ryan";
+  const std::string lang = language ? language : "english";
+  auto li = cfg.language_ids.find(lang);
+  if (li == cfg.language_ids.end()) invalid("missing language token id for " + lang);
+  int spk_id = -2;
+  if (!xvec_host) {
+    auto si = cfg.speaker_ids.find(spk);
+    if (si == cfg.speaker_ids.end()) invalid("missing speaker token id for " + spk);
+    spk_id = si->second;
+  }
+  const size_t la = n == 0 ? 0 : (lookahead == 0 ? n : std::max<size_t>(1, std::min(lookahead, n)));
+  const int P = 9 + (int)la;
+  if ((size_t)P > max_cache_steps) invalid("prefill longer than max_cache_steps");
+  const int ntr = (int)(n - la) + 1;
+  std::vector<int> proj = {cfg.im_start, cfg.assistant, kNewline, cfg.tts_pad, cfg.tts_pad,
+                           cfg.tts_pad, cfg.tts_pad, cfg.tts_pad, cfg.tts_bos};
+  for (size_t i = 0; i < la; ++i) proj.push_back((int)ids[i]);
+  for (size_t i = la; i < n; ++i) proj.push_back((int)ids[i]);
+  proj.push_back(cfg.tts_eos);
+  proj.push_back(cfg.tts_pad);
+  for (int id : proj)
+    if (id < 0 || id >= text_vocab) invalid("special text id out of range for the text vocab");
+  if ((size_t)ntr > max_cache_steps + 1) invalid("too many trailing rows");
+  project_text(proj, tp_c);
+  const int codec_list[7] = {cfg.codec_think, cfg.codec_think_bos, li->second, cfg.codec_think_eos,
+                             spk_id, cfg.codec_pad, cfg.codec_bos};
+  std::vector<int> pidx(P), cids(P);
+  for (int r = 0; r < 3; ++r) { pidx[r] = r; cids[r] = -1; }
+  for (int i = 0; i < 6; ++i) { pidx[3 + i] = 3 + i; cids[3 + i] = codec_list[i]; }
+  for (size_t i = 0; i < la; ++i) {
+    pidx[9 + i] = 9 + (int)i;
+    cids[9 + i] = codec_list[i + 1 == la ? 6 : 5];
+  }
+  if (xvec_host) QCK(cudaMemcpy(xvec, xvec_host, cfg.talker.hidden * 4, cudaMemcpyHostToDevice));
+  QCK(cudaMemcpy(tp_pidx, pidx.data(), P * 4, cudaMemcpyHostToDevice));
+  QCK(cudaMemcpy(tp_cids, cids.data(), P * 4, cudaMemcpyHostToDevice));
+  const int H = cfg.talker.hidden;
+  QCK(launch_assemble_rows(tp_c, tp_pidx, codec_emb, tp_cids, xvec, P, H, tb.x, stream));
+  QCK(cudaMemcpyAsync(trailing, tp_c + (size_t)P * H, (size_t)ntr * H * 4,
+                      cudaMemcpyDeviceToDevice, stream));
+  QCK(cudaMemcpyAsync(tts_pad, tp_c + (size_t)(P + ntr) * H, (size_t)H * 4,
+                      cudaMemcpyDeviceToDevice, stream));
+  *n_trailing = ntr;
+  return P;
+}
+
+// ---- options (generation.rs:569-583, sampling.rs:12-26) --------------------
+void Engine::validate(const qtts_generate_options& o) const {
+  if (o.max_frames == 0) invalid("max_frames must be non-zero");
+  if (!(o.repetition_penalty > 0.f)) invalid("repetition_penalty must be positive");
+  auto check = [](const char* name, float top_p, float temp) {
+    if (!(top_p > 0.f) || top_p > 1.f)
+      invalid(std::string(name) + ".top_p must be in (0, 1], got " + std::to_string(top_p));
+    if (!(temp > 0.f))
+      invalid(std::string(name) + ".temperature must be positive, got " + std::to_string(temp));
+  };
+  check("talker", o.top_p, o.temperature);
+  check("subtalker", o.subtalker_top_p, o.subtalker_temperature);
+  if (o.decode_audio) fail(QTTS_ERR_UNSUPPORTED, "decode_audio: the codec is not part of this library");
+  if (o.rng != RNG_LCG && o.rng != RNG_PHILOX) invalid("rng must be 0 (lcg) or 1 (philox)");
+}
+
+// Starts a sequence whose prefill rows are already in the talker input:
+// state reset, talker prefill and the first semantic token (generation.rs:681-693).
+void Engine::begin(int P, int n_trailing, const qtts_generate_options& o) {
+  if ((size_t)P + o.max_frames > max_cache_steps)
+    fail(QTTS_ERR_CACHE_FULL, "requested " + std::to_string(P + o.max_frames) +
+                                  " cache steps but engine was loaded for " +
+                                  std::to_string(max_cache_steps) +
+                                  "; call load_with_max_frames with a larger max_frames");
+  SeqState s{};
+  s.frames = 0;
+  s.semantic = -1;
+  s.talker_pos = P;
+  s.prefill_len = P;
+  s.n_trailing = n_trailing;
+  s.rng_kind = o.rng;
+  s.rng_state = o.seed ^ kSeedXor;
+  s.rng_seed = o.seed;
+  *st_host = s;
+  QCK(cudaMemcpyAsync(st, st_host, sizeof(SeqState), cudaMemcpyHostToDevice, stream));
+  QCK(cudaEventRecord(ev0, stream));
+  stack_rows(talker, tb, tkv, P, 0, nullptr);
+  talker_head(ROLE_TALKER_PREFILL, tb.x + (size_t)(P - 1) * cfg.talker.hidden, talker_cfg(o),
+              1.0f, nullptr, cp_prefix_target());
+  QCK(cudaEventRecord(ev1, stream));
+  seq_P = P;
+  seq_frames = 0;
+  seq_max_frames = o.max_frames;
+  seq_opts = o;
+  seq_ended = false;
+  ++seq_id;
+  sync_state();
+  seq_semantic = st_host->semantic;
+  QCK(cudaEventElapsedTime(&last_prefill_ms, ev0, ev1));
+  last_frames_ms = 0.f;
+  last_frames = 0;
+}
+
+void Engine::sync_state() {
+  QCK(cudaMemcpyAsync(st_host, st, sizeof(SeqState), cudaMemcpyDeviceToHost, stream));
+  QCK(cudaStreamSynchronize(stream));
+  if (st_host->error)
+    fail(QTTS_ERR_DEVICE_STATE, "cannot sample from logits with no finite values");
+}
+
+// Enqueues up to n frames (fewer if EOS stops the loop on the device) and
+// returns the number of frames produced.
+size_t Engine::run_frames(size_t n) {
+  if (seq_ended || (size_t)seq_frames >= seq_max_frames || n == 0) return 0;
+  n = std::min(n, seq_max_frames - seq_frames);
+  SampleKey full{talker_cfg(seq_opts), sub_cfg(seq_opts), seq_opts.repetition_penalty, 0};
+  SampleKey last = full;
+  last.last = 1;
+  cudaGraphExec_t gf = nullptr, gl = nullptr;
+  const size_t begin = seq_frames;
+  for (size_t i = 0; i < n; ++i)
+    if (begin + i + 1 < seq_max_frames) gf = frame_graph(full); else gl = frame_graph(last);
+  QCK(cudaEventRecord(ev1, stream));
+  for (size_t i = 0; i < n; ++i) {
+    const bool is_last = begin + i + 1 >= seq_max_frames;
+    QCK(cudaGraphLaunch(is_last ? gl : gf, stream));
+  }
+  QCK(cudaEventRecord(ev2, stream));
+  sync_state();
+  float ms = 0.f;
+  QCK(cudaEventElapsedTime(&ms, ev1, ev2));
+  last_frames_ms += ms;
+  const int now = st_host->frames;
+  const size_t produced = (size_t)(now - seq_frames);
+  last_frames += produced;
+  seq_frames = now;
+  seq_semantic = st_host->semantic;
+  if (st_host->halt) seq_ended = true;
+  return produced;
+}
+
+void Engine::read_codes(size_t from, size_t to, int32_t* out) {
+  if (to <= from) return;
+  const size_t g = cfg.cp.groups;
+  QCK(cudaMemcpy(out, codes + from * g, (to - from) * g * 4, cudaMemcpyDeviceToHost));
+}
+
+// ---------------------------------------------------------------------------
+struct Stream {
+  Engine* e;
+  uint64_t id;
+  size_t max_frames;
+  std::vector<int32_t> codes;
+};
+
+// PollingTextStream (generation.rs:1086-1451) on token ids.
+struct TextStream {
+  Engine* e;
+  qtts_generate_options opts;
+  qtts_text_stream_options topts;
+  std::deque<uint32_t> queued;
+  bool text_finished = false, eos_pending = false, eos_consumed = false;
+  bool started = false, finished = false;
+  uint64_t id = 0;
+  std::vector<int32_t> codes;
+};
+
+}  // namespace
+}  // namespace qtts
+
+using qtts::Engine;
+using qtts::QttsError;
+
+struct qtts_engine {
+  std::unique_ptr<Engine> e;
+};
+struct qtts_stream {
+  qtts::Stream s;
+};
+struct qtts_text_stream {
+  qtts::TextStream s;
+};
+
+namespace {
+
+template <typename F>
+int32_t guard(F&& f) {
+  try {
+    f();
+    return QTTS_OK;
+  } catch (const QttsError& e) {
+    qtts::g_last_error = e.what();
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    qtts::g_last_error = "out of host memory";
+    return QTTS_ERR_CUDA;
+  } catch (const std::exception& e) {
+    qtts::g_last_error = e.what();
+    return QTTS_ERR_INVALID_INPUT;
+  }
+}
+
+void need(const void* p, const char* what) {
+  if (!p) qtts::invalid(std::string(what) + " must not be null");
+}
+
+Engine& engine_of(qtts_engine* e) {
+  need(e, "engine");
+  QCK(cudaSetDevice(e->e->device));
+  return *e->e;
+}
+
+void finish_generation(Engine& e, int32_t* codes_out, size_t cap, size_t* frames_out,
+                       int32_t* ended) {
+  e.run_frames(e.seq_max_frames);
+  const size_t g = e.cfg.cp.groups;
+  if (cap < (size_t)e.seq_frames * g) qtts::invalid("codes_out capacity too small");
+  e.read_codes(0, e.seq_frames, codes_out);
+  if (frames_out) *frames_out = e.seq_frames;
+  if (ended) *ended = e.seq_ended ? 1 : 0;
+}
+
+int32_t load_engine(const char* dir, int32_t device, size_t mcs, qtts_engine** out) {
+  return guard([&] {
+    need(dir, "model_dir");
+    need(out, "out");
+    *out = nullptr;
+    auto h = std::make_unique<qtts_engine>();
+    h->e = std::make_unique<Engine>(dir, device, mcs);
+    *out = h.release();
+  });
+}
+
+// Host side of next_trailing_buffer (generation.rs:1360-1388): the text id of
+// the next trailing row, or -1 when no row is ready yet.
+long long next_trailing_id(qtts::TextStream& s) {
+  const Engine& e = *s.e;
+  if (!s.text_finished && s.queued.size() < s.topts.min_resume_tokens) return -1;
+  if (!s.queued.empty()) {
+    const uint32_t t = s.queued.front();
+    s.queued.pop_front();
+    return t;
+  }
+  if (s.eos_pending) {
+    s.eos_pending = false;
+    s.eos_consumed = true;
+    return e.cfg.tts_eos;
+  }
+  if (s.text_finished || s.eos_consumed) return e.cfg.tts_pad;
+  return -1;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* qtts_last_error(void) { return qtts::g_last_error.c_str(); }
+int32_t qtts_abi_version(void) { return 1; }
+
+void qtts_generate_options_default(qtts_generate_options* o) {
+  if (!o) return;
+  *o = qtts_generate_options{};
+  o->speaker = "ryan";
+  o->language = "english";
+  o->max_frames = 240;
+  o->decode_audio = 0;
+  o->do_sample = 1;
+  o->top_k = 50;
+  o->top_p = 1.0f;
+  o->temperature = 0.9f;
+  o->repetition_penalty = 1.05f;
+  o->subtalker_dosample = 1;
+  o->subtalker_top_k = 50;
+  o->subtalker_top_p = 1.0f;
+  o->subtalker_temperature = 0.9f;
+  o->seed = 0;
+  o->rng = 0;
+}
+
+void qtts_stream_options_default(qtts_stream_options* o) {
+  if (!o) return;
+  o->text_lookahead_tokens = 8;
+  o->left_context_frames = 25;
+}
+
+void qtts_text_stream_options_default(qtts_text_stream_options* o) {
+  if (!o) return;
+  o->min_start_tokens = 8;
+  o->min_resume_tokens = 1;
+  o->flush_on_punctuation = 1;
+  o->left_context_frames = 25;
+}
+
+int32_t qtts_engine_load(const char* dir, int32_t device, qtts_engine** out) {
+  return load_engine(dir, device, 512, out);
+}
+
+int32_t qtts_engine_load_with_max_frames(const char* dir, int32_t device, size_t max_frames,
+                                         qtts_engine** out) {
+  if (max_frames == 0) {
+    qtts::g_last_error = "max_frames must be non-zero";
+    return QTTS_ERR_INVALID_INPUT;
+  }
+  return load_engine(dir, device, 256 + max_frames, out);
+}
+
+int32_t qtts_engine_load_with_options(const char* dir, int32_t device, size_t mcs,
+                                      qtts_engine** out) {
+  return load_engine(dir, device, mcs, out);
+}
+
+void qtts_engine_destroy(qtts_engine* e) { delete e; }
+
+int32_t qtts_engine_get_info(const qtts_engine* h, qtts_engine_info* out) {
+  return guard([&] {
+    need(h, "engine");
+    need(out, "out");
+    const Engine& e = *h->e;
+    out->hidden = e.cfg.talker.hidden;
+    out->vocab = e.cfg.talker.vocab;
+    out->cp_hidden = e.cfg.cp.hidden;
+    out->cp_vocab = e.cfg.cp.vocab;
+    out->num_code_groups = e.cfg.cp.groups;
+    out->talker_layers = e.cfg.talker.layers;
+    out->cp_layers = e.cfg.cp.layers;
+    out->codec_eos = e.cfg.codec_eos;
+    out->max_cache_steps = e.max_cache_steps;
+    out->device_bytes = e.arena.bytes();
+  });
+}
+
+int32_t qtts_generate_codes_from_ids(qtts_engine* h, const uint32_t* ids, size_t n,
+                                     const qtts_generate_options* o, int32_t* codes_out,
+                                     size_t cap, size_t* frames_out, int32_t* ended) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(o, "options");
+    need(codes_out, "codes_out");
+    if (n) need(ids, "content_ids");
+    e.validate(*o);
+    int ntr = 0;
+    const int P = e.prepare(ids, n, 0, o->speaker, o->language, nullptr, &ntr);
+    e.begin(P, ntr, *o);
+    finish_generation(e, codes_out, cap, frames_out, ended);
+  });
+}
+
+int32_t qtts_generate_voice_clone_codes_from_ids(qtts_engine* h, const uint32_t* ids, size_t n,
+                                                 const float* spk, const qtts_generate_options* o,
+                                                 int32_t* codes_out, size_t cap,
+                                                 size_t* frames_out, int32_t* ended) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(o, "options");
+    need(spk, "speaker_embedding");
+    need(codes_out, "codes_out");
+    if (n) need(ids, "content_ids");
+    e.validate(*o);
+    int ntr = 0;
+    const int P = e.prepare(ids, n, 0, nullptr, o->language, spk, &ntr);
+    e.begin(P, ntr, *o);
+    finish_generation(e, codes_out, cap, frames_out, ended);
+  });
+}
+
+int32_t qtts_generate_codes_from_rows(qtts_engine* h, const float* prefill, size_t P,
+                                      const float* trailing, size_t T, const float* pad,
+                                      const qtts_generate_options* o, int32_t* codes_out,
+                                      size_t cap, size_t* frames_out, int32_t* ended) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(o, "options");
+    need(prefill, "prefill");
+    need(pad, "tts_pad");
+    need(codes_out, "codes_out");
+    if (T) need(trailing, "trailing");
+    e.validate(*o);
+    if (P == 0) qtts::invalid("prefill steps must be non-zero");
+    if (P > e.max_cache_steps) qtts::invalid("prefill longer than max_cache_steps");
+    const size_t H = e.cfg.talker.hidden;
+    const size_t Tn = std::min(T, e.max_cache_steps + 1);
+    QCK(cudaMemcpy(e.tb.x, prefill, P * H * 4, cudaMemcpyHostToDevice));
+    if (Tn) QCK(cudaMemcpy(e.trailing, trailing, Tn * H * 4, cudaMemcpyHostToDevice));
+    QCK(cudaMemcpy(e.tts_pad, pad, H * 4, cudaMemcpyHostToDevice));
+    e.begin((int)P, (int)Tn, *o);
+    finish_generation(e, codes_out, cap, frames_out, ended);
+  });
+}
+
+int32_t qtts_prepare_inputs_from_ids(qtts_engine* h, const uint32_t* ids, size_t n,
+                                     size_t lookahead, const char* speaker, const char* language,
+                                     float* prefill_out, size_t* prefill_steps,
+                                     float* trailing_out, size_t* trailing_steps,
+                                     float* pad_out) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    if (n) need(ids, "content_ids");
+    int ntr = 0;
+    const int P = e.prepare(ids, n, lookahead, speaker, language, nullptr, &ntr);
+    const size_t H = e.cfg.talker.hidden;
+    QCK(cudaStreamSynchronize(e.stream));
+    if (prefill_out) QCK(cudaMemcpy(prefill_out, e.tb.x, P * H * 4, cudaMemcpyDeviceToHost));
+    if (trailing_out)
+      QCK(cudaMemcpy(trailing_out, e.trailing, ntr * H * 4, cudaMemcpyDeviceToHost));
+    if (pad_out) QCK(cudaMemcpy(pad_out, e.tts_pad, H * 4, cudaMemcpyDeviceToHost));
+    if (prefill_steps) *prefill_steps = P;
+    if (trailing_steps) *trailing_steps = ntr;
+  });
+}
+
+int32_t qtts_stream_start_from_ids(qtts_engine* h, const uint32_t* ids, size_t n,
+                                   const qtts_generate_options* o,
+                                   const qtts_stream_options* so, qtts_stream** out) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(o, "options");
+    need(out, "out");
+    *out = nullptr;
+    if (n) need(ids, "content_ids");
+    e.validate(*o);
+    qtts_stream_options sopt;
+    qtts_stream_options_default(&sopt);
+    if (so) sopt = *so;
+    if (sopt.text_lookahead_tokens == 0) qtts::invalid("text_lookahead_tokens must be non-zero");
+    int ntr = 0;
+    const int P = e.prepare(ids, n, sopt.text_lookahead_tokens, o->speaker, o->language, nullptr,
+                            &ntr);
+    e.begin(P, ntr, *o);
+    auto s = std::make_unique<qtts_stream>();
+    s->s.e = &e;
+    s->s.id = e.seq_id;
+    s->s.max_frames = o->max_frames;
+    *out = s.release();
+  });
+}
+
+int32_t qtts_stream_next_codes_chunk(qtts_stream* h, size_t max_chunk, int32_t* codes_out,
+                                     size_t cap, qtts_codes_chunk* chunk) {
+  return guard([&] {
+    need(h, "stream");
+    need(chunk, "chunk");
+    Engine& e = *h->s.e;
+    QCK(cudaSetDevice(e.device));
+    if (max_chunk == 0) qtts::invalid("max_chunk_frames must be non-zero");
+    if (h->s.id != e.seq_id) qtts::invalid("stream was superseded by a newer generation on this engine");
+    const size_t before = e.seq_frames;
+    const size_t produced = e.run_frames(max_chunk);
+    chunk->frames = produced;
+    chunk->total_frames = e.seq_frames;
+    chunk->ended_by_eos = e.seq_ended ? 1 : 0;
+    chunk->status = produced ? QTTS_CHUNK : QTTS_CHUNK_NONE;
+    if (produced) {
+      const size_t g = e.cfg.cp.groups;
+      need(codes_out, "codes_out");
+      if (cap < produced * g) qtts::invalid("codes_out capacity too small");
+      e.read_codes(before, e.seq_frames, codes_out);
+    }
+  });
+}
+
+void qtts_stream_destroy(qtts_stream* s) { delete s; }
+
+int32_t qtts_text_stream_start(qtts_engine* h, const qtts_generate_options* o,
+                               const qtts_text_stream_options* to, qtts_text_stream** out) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(o, "options");
+    need(out, "out");
+    *out = nullptr;
+    e.validate(*o);
+    qtts_text_stream_options topt;
+    qtts_text_stream_options_default(&topt);
+    if (to) topt = *to;
+    if (topt.min_start_tokens == 0) qtts::invalid("min_start_tokens must be non-zero");
+    if (topt.min_resume_tokens == 0) qtts::invalid("min_resume_tokens must be non-zero");
+    auto s = std::make_unique<qtts_text_stream>();
+    s->s.e = &e;
+    s->s.opts = *o;
+    s->s.topts = topt;
+    *out = s.release();
+  });
+}
+
+int32_t qtts_text_stream_push_ids(qtts_text_stream* h, const uint32_t* ids, size_t n) {
+  return guard([&] {
+    need(h, "stream");
+    if (h->s.text_finished) qtts::invalid("cannot push text after finish_text");
+    if (n) need(ids, "ids");
+    h->s.e->check_ids(ids, n);
+    for (size_t i = 0; i < n; ++i) h->s.queued.push_back(ids[i]);
+  });
+}
+
+int32_t qtts_text_stream_finish(qtts_text_stream* h) {
+  return guard([&] {
+    need(h, "stream");
+    if (h->s.text_finished) return;
+    h->s.text_finished = true;
+    h->s.eos_pending = true;
+  });
+}
+
+int32_t qtts_text_stream_next_codes_chunk(qtts_text_stream* h, size_t max_chunk,
+                                          int32_t* codes_out, size_t cap,
+                                          qtts_codes_chunk* chunk) {
+  return guard([&] {
+    need(h, "stream");
+    need(chunk, "chunk");
+    qtts::TextStream& s = h->s;
+    Engine& e = *s.e;
+    QCK(cudaSetDevice(e.device));
+    if (max_chunk == 0) qtts::invalid("max_chunk_frames must be non-zero");
+    chunk->frames = 0;
+    chunk->total_frames = 0;
+    chunk->ended_by_eos = 0;
+    const size_t G = e.cfg.cp.groups;
+    auto finished = [&] {
+      s.finished = true;
+      chunk->status = QTTS_FINISHED;
+      chunk->total_frames = s.codes.size() / G;
+      chunk->ended_by_eos = (s.started && e.seq_id == s.id && e.seq_ended) ? 1 : 0;
+    };
+    if (s.finished) return finished();
+    // try_start_generation (generation.rs:1280-1358)
+    if (!s.started) {
+      bool can = !(s.queued.size() < s.topts.min_start_tokens && !s.text_finished) &&
+                 !s.queued.empty();
+      if (!can) {
+        if (s.text_finished && s.queued.empty() && s.eos_pending) return finished();
+        chunk->status = QTTS_NEED_MORE_TEXT;
+        return;
+      }
+      const size_t la = std::max<size_t>(1, std::min<size_t>(s.topts.min_start_tokens, s.queued.size()));
+      std::vector<uint32_t> pre;
+      for (size_t i = 0; i < la; ++i) {
+        pre.push_back(s.queued.front());
+        s.queued.pop_front();
+      }
+      int ntr_unused = 0;
+      const int P = e.prepare(pre.data(), pre.size(), pre.size(), s.opts.speaker, s.opts.language,
+                              nullptr, &ntr_unused);
+      e.begin(P, 0, s.opts);
+      s.id = e.seq_id;
+      s.started = true;
+    }
+    if (s.id != e.seq_id) qtts::invalid("text stream was superseded by a newer generation on this engine");
+    // next_codes_chunk (generation.rs:1183-1278): plan the trailing rows of the
+    // frames this chunk can run, then run them as one burst.
+    if (e.seq_ended || (size_t)e.seq_frames >= e.seq_max_frames) {
+      return finished();
+    }
+    std::vector<int> tr_ids;
+    size_t n = 0;
+    while (n < max_chunk && e.seq_frames + n < e.seq_max_frames) {
+      const size_t cur = e.seq_frames + n;
+      if (cur + 1 < e.seq_max_frames) {
+        const long long id = next_trailing_id(s);
+        if (id < 0) break;
+        tr_ids.push_back((int)id);
+      }
+      ++n;
+    }
+    if (n == 0) {
+      chunk->status = QTTS_NEED_MORE_TEXT;
+      return;
+    }
+    const size_t H = e.cfg.talker.hidden;
+    if (!tr_ids.empty()) e.project_text(tr_ids, e.trailing + (size_t)e.seq_frames * H);
+    const int ntr = e.seq_frames + (int)tr_ids.size();
+    QCK(cudaMemcpyAsync(&e.st->n_trailing, &ntr, 4, cudaMemcpyHostToDevice, e.stream));
+    QCK(cudaStreamSynchronize(e.stream));
+    const size_t before = e.seq_frames;
+    const size_t produced = e.run_frames(n);
+    if (produced == 0) {
+      if (e.seq_ended || (size_t)e.seq_frames >= e.seq_max_frames) return finished();
+      chunk->status = QTTS_NEED_MORE_TEXT;
+      return;
+    }
+    const size_t old = s.codes.size();
+    s.codes.resize(old + produced * G);
+    e.read_codes(before, e.seq_frames, s.codes.data() + old);
+    chunk->frames = produced;
+    chunk->total_frames = e.seq_frames;
+    chunk->ended_by_eos = e.seq_ended ? 1 : 0;
+    chunk->status = QTTS_CHUNK;
+    if (codes_out) {
+      if (cap < produced * G) qtts::invalid("codes_out capacity too small");
+      std::memcpy(codes_out, s.codes.data() + old, produced * G * 4);
+    }
+  });
+}
+
+int32_t qtts_text_stream_codes(qtts_text_stream* h, int32_t* codes_out, size_t cap,
+                               size_t* frames_out, int32_t* ended) {
+  return guard([&] {
+    need(h, "stream");
+    const size_t G = h->s.e->cfg.cp.groups;
+    const size_t frames = h->s.codes.size() / G;
+    if (codes_out) {
+      if (cap < h->s.codes.size()) qtts::invalid("codes_out capacity too small");
+      std::memcpy(codes_out, h->s.codes.data(), h->s.codes.size() * 4);
+    }
+    if (frames_out) *frames_out = frames;
+    if (ended)
+      *ended = (h->s.started && h->s.e->seq_id == h->s.id && h->s.e->seq_ended) ? 1 : 0;
+  });
+}
+
+void qtts_text_stream_destroy(qtts_text_stream* s) { delete s; }
+
+int32_t qtts_talker_prefill(qtts_engine* h, const float* rows, size_t steps, float* hidden_out,
+                            float* logits_out, int32_t* token_out) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(rows, "rows");
+    if (steps == 0) qtts::invalid("prefill steps must be non-zero");
+    if (steps > e.max_cache_steps) qtts::invalid("prefill steps outside cache");
+    const size_t H = e.cfg.talker.hidden;
+    QCK(cudaMemcpy(e.tb.x, rows, steps * H * 4, cudaMemcpyHostToDevice));
+    qtts_generate_options o;
+    qtts_generate_options_default(&o);
+    o.do_sample = 0;
+    o.max_frames = 1;
+    e.begin((int)steps, 0, o);
+    if (token_out) *token_out = e.st_host->semantic;
+    if (hidden_out) QCK(cudaMemcpy(hidden_out, e.cp_prefix_target(), H * 4, cudaMemcpyDeviceToHost));
+    if (logits_out)
+      QCK(cudaMemcpy(logits_out, e.logits, e.cfg.talker.vocab * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+int32_t qtts_talker_decode_step(qtts_engine* h, const float* input, size_t offset,
+                                float* hidden_out, float* logits_out, int32_t* token_out) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(input, "input");
+    if (offset >= e.max_cache_steps) qtts::invalid("offset outside cache length");
+    const size_t H = e.cfg.talker.hidden;
+    QCK(cudaMemcpy(e.tb.x, input, H * 4, cudaMemcpyHostToDevice));
+    e.st_host->talker_pos = (int)offset;
+    e.st_host->halt = 0;
+    e.st_host->frames = 0;
+    QCK(cudaMemcpy(e.st, e.st_host, sizeof(qtts::SeqState), cudaMemcpyHostToDevice));
+    qtts::SampleCfg greedy{0, 0, 1.f, 1.f};
+    e.stack_step(e.talker, e.tb, e.tkv, &e.st->talker_pos, 0, qtts::kTalkerSplits, nullptr);
+    e.talker_head(qtts::ROLE_TALKER_STEP, e.tb.x, greedy, 1.0f, nullptr, e.cp_prefix_target());
+    e.sync_state();
+    if (token_out) *token_out = e.st_host->semantic;
+    if (hidden_out) QCK(cudaMemcpy(hidden_out, e.cp_prefix_target(), H * 4, cudaMemcpyDeviceToHost));
+    if (logits_out)
+      QCK(cudaMemcpy(logits_out, e.logits, e.cfg.talker.vocab * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const float* semantic_embed,
+                            const qtts_generate_options* o, int32_t* tokens_out,
+                            float* emb_sum_out, float* logits_out) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(talker_hidden, "talker_hidden");
+    need(semantic_embed, "semantic_embed");
+    need(o, "options");
+    qtts_generate_options opt = *o;
+    opt.decode_audio = 0;
+    opt.max_frames = 1;
+    e.validate(opt);
+    const size_t H = e.cfg.talker.hidden;
+    const auto& C = e.cfg.cp;
+    QCK(cudaMemcpy(e.cp_prefix_target(), talker_hidden, H * 4, cudaMemcpyHostToDevice));
+    QCK(cudaMemcpy(e.cp_prefix_target() + H, semantic_embed, H * 4, cudaMemcpyHostToDevice));
+    qtts::SeqState s{};
+    s.semantic = 0;
+    s.rng_kind = opt.rng;
+    s.rng_state = opt.seed ^ qtts::kSeedXor;
+    s.rng_seed = opt.seed;
+    s.n_trailing = 0;
+    *e.st_host = s;
+    QCK(cudaMemcpy(e.st, e.st_host, sizeof(s), cudaMemcpyHostToDevice));
+    const qtts::SampleCfg sc = qtts::sub_cfg(opt);
+    // Eager CodePredictor pass with per-group logits kept for parity checks.
+    if (e.has_proj())
+      e.linear(e.proj_w, e.cp_prefix, H, nullptr, 0.f, e.cb.x, C.hidden, nullptr, 0, e.proj_b, 2,
+               C.hidden, H, qtts::EPI_BIAS, nullptr);
+    e.stack_rows(e.cp, e.cb, e.ckv, 2, 0, nullptr);
+    e.cp_head(0, e.cb.x + C.hidden, sc, nullptr);
+    QCK(cudaMemcpyAsync(e.dbg_logits, e.logits, C.vocab * 4, cudaMemcpyDeviceToDevice, e.stream));
+    for (int g = 1; g < C.groups - 1; ++g) {
+      if (e.has_proj())
+        e.linear(e.proj_w, e.cp_next, H, nullptr, 0.f, e.cb.x, C.hidden, nullptr, 0, e.proj_b, 1,
+                 C.hidden, H, qtts::EPI_BIAS, nullptr);
+      e.stack_step(e.cp, e.cb, e.ckv, nullptr, g + 1, 1, nullptr);
+      e.cp_head(g, e.cb.x, sc, nullptr);
+      QCK(cudaMemcpyAsync(e.dbg_logits + (size_t)g * C.vocab, e.logits, C.vocab * 4,
+                                cudaMemcpyDeviceToDevice, e.stream));
+    }
+    e.sync_state();
+    const int na = C.groups - 1;
+    std::vector<int32_t> row(C.groups);
+    e.read_codes(0, 1, row.data());
+    if (tokens_out) std::memcpy(tokens_out, row.data() + 1, na * 4);
+    if (emb_sum_out) QCK(cudaMemcpy(emb_sum_out, e.emb_sum, H * 4, cudaMemcpyDeviceToHost));
+    if (logits_out)
+      QCK(cudaMemcpy(logits_out, e.dbg_logits, (size_t)na * C.vocab * 4, cudaMemcpyDeviceToHost));
+    e.seq_ended = true;  // the talker state was not advanced: no stream may continue
+    ++e.seq_id;
+  });
+}
+
+int32_t qtts_last_timings(const qtts_engine* h, float* prefill_ms, float* frames_ms,
+                          size_t* frames) {
+  return guard([&] {
+    need(h, "engine");
+    if (prefill_ms) *prefill_ms = h->e->last_prefill_ms;
+    if (frames_ms) *frames_ms = h->e->last_frames_ms;
+    if (frames) *frames = h->e->last_frames;
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,885 @@
+// sm_100a kernels for the Qwen3-TTS token loop (talker decode step + CodePredictor pass).
+//
+// Reference semantics (piedshag/qwen3-tts-hip):
+//   projections      rocBLAS sgemm row-major          src/gpu/blas.rs:134-151
+//   RMSNorm          rmsnorm_f32                       src/gpu/kernels.rs:2-37
+//   RoPE             rope_bhsd_f32 (rotate-half)       src/gpu/kernels.rs:41-76
+//   SwiGLU/residual  swiglu_f32 / residual_add_f32     src/gpu/kernels.rs:80-117
+//   decode attention scores/softmax/apply (GQA)        src/gpu/kernels.rs:1048-1119,121-173
+//   KV write         write_kv_cache_f32                src/gpu/kernels.rs:1121-1144
+//   suppression      suppress_codec_logits_f32         src/gpu/kernels.rs:248-263
+//   penalty          apply_repetition_penalty_f32      src/gpu/kernels.rs:408-426
+//   argmax / top-k   argmax_rows_f32 / sample_topk_f32 src/gpu/kernels.rs:177-220,265-336
+//   CPU sampler/LCG  select_token / sample / next_f32  src/model/sampling.rs:40-126
+//
+// Design: weights are bf16 [out, in] rows streamed once per step with 16-byte
+// non-allocating loads; activations stay fp32; the KV cache is paged bf16.
+// Norm prologues, QK-norm + RoPE + KV append, residual/SwiGLU/bias epilogues,
+// split-K attention combine, and token selection + embedding gathers are fused
+// into the kernels that produce their inputs, so one decoder layer is four
+// launches and a token head is one.
+#include <float.h>
+
+#include "kernels.h"
+
+namespace qtts {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxVocab = 4096;
+constexpr int kXFloats = 12288;  // 48 KB fp32 activation tile per block
+
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+
+// ---------------------------------------------------------------------------
+// Projection body: for the block's M-tile and RPW output columns per warp,
+//   acc = W[row] . (gamma * x[m])   then  y = epilogue(inv_rms[m] * acc)
+// The RMSNorm scale is a per-row scalar, so it is applied after the dot
+// product; gamma is folded into the staged activations.
+// ---------------------------------------------------------------------------
+template <int MT, int RPW, int EPI>
+__device__ __forceinline__ bool linear_body(const LinearArgs& a, float* sx, float* s_inv) {
+  constexpr int NR = (EPI == EPI_SWIGLU) ? 2 * RPW : RPW;
+  constexpr int KC_MAX = kXFloats / MT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int col0 = (blockIdx.x * kWarps + warp) * RPW;
+  const int m0 = blockIdx.y * MT;
+  const int K = a.K;
+
+  const __nv_bfloat16* wr[NR];
+  bool valid[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int c = col0 + r;
+    valid[r] = c < a.N;
+    const long long cc = valid[r] ? c : 0;
+    if (EPI == EPI_SWIGLU) {
+      wr[2 * r] = a.W + cc * K;
+      wr[2 * r + 1] = a.W + (a.N + cc) * K;
+    } else {
+      wr[r] = a.W + cc * K;
+    }
+  }
+  // Weights do not depend on the previous kernel: pull this warp's first
+  // 16-byte chunks into L2 before waiting on the producer.
+#pragma unroll
+  for (int r = 0; r < NR; ++r)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(wr[r] + lane * 8));
+
+  pdl_wait();
+  if (a.halt && *a.halt) return false;
+  const int mcount = min(MT, a.M - m0);
+
+  if (a.gamma) {
+    for (int m = warp; m < mcount; m += kWarps) {
+      const float4* xr = reinterpret_cast<const float4*>(a.x + (long long)(m0 + m) * a.ldx);
+      float ss = 0.f;
+      for (int k = lane; k < K / 4; k += 32) {
+        float4 v = xr[k];
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) s_inv[m] = rsqrtf(ss / (float)K + a.eps);
+    }
+  }
+
+  float acc[NR][MT];
+#pragma unroll
+  for (int r = 0; r < NR; ++r)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
+
+  for (int k0 = 0; k0 < K; k0 += KC_MAX) {
+    const int kc = min(KC_MAX, K - k0);
+    __syncthreads();
+    const int kq = kc >> 2;
+    for (int i = threadIdx.x; i < MT * kq; i += kThreads) {
+      const int m = i / kq, k4 = i - m * kq;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m < mcount)
+        v = *reinterpret_cast<const float4*>(a.x + (long long)(m0 + m) * a.ldx + k0 + 4 * k4);
+      if (a.gamma) {
+        const float4 g = *reinterpret_cast<const float4*>(a.gamma + k0 + 4 * k4);
+        v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+      }
+      *reinterpret_cast<float4*>(sx + m * kc + 4 * k4) = v;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int kk = lane * 8; kk < kc; kk += 256) {
+      uint4 wv[NR];
+#pragma unroll
+      for (int r = 0; r < NR; ++r) wv[r] = ldg_stream(wr[r] + k0 + kk);
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        float wf[8];
+        unpack8(wv[r], wf);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          const float4 x0 = *reinterpret_cast<const float4*>(sx + m * kc + kk);
+          const float4 x1 = *reinterpret_cast<const float4*>(sx + m * kc + kk + 4);
+          float t = acc[r][m];
+          t = fmaf(wf[0], x0.x, t); t = fmaf(wf[1], x0.y, t);
+          t = fmaf(wf[2], x0.z, t); t = fmaf(wf[3], x0.w, t);
+          t = fmaf(wf[4], x1.x, t); t = fmaf(wf[5], x1.y, t);
+          t = fmaf(wf[6], x1.z, t); t = fmaf(wf[7], x1.w, t);
+          acc[r][m] = t;
+        }
+      }
+    }
+  }
+  pdl_trigger();
+
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    if (!valid[r]) continue;  // warp-uniform
+    const int c = col0 + r;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m >= mcount) break;
+      const float sc = a.gamma ? s_inv[m] : 1.0f;
+      float out;
+      if (EPI == EPI_SWIGLU) {
+        const float g = warp_sum(acc[2 * r][m]) * sc;
+        const float u = warp_sum(acc[2 * r + 1][m]) * sc;
+        out = g / (1.0f + expf(-g)) * u;
+      } else {
+        out = warp_sum(acc[r][m]) * sc;
+        if (EPI == EPI_RESID) out += a.resid[(long long)(m0 + m) * a.ldr + c];
+        if (EPI == EPI_BIAS) out += a.bias[c];
+        if (EPI == EPI_BIAS_SILU) out = silu(out + a.bias[c]);
+      }
+      if (lane == 0) a.y[(long long)(m0 + m) * a.ldy + c] = out;
+    }
+  }
+  return true;
+}
+
+template <int MT, int RPW, int EPI>
+__global__ void __launch_bounds__(kThreads) k_linear(LinearArgs a) {
+  extern __shared__ float4 dyn4[];
+  __shared__ float s_inv[MT];
+  linear_body<MT, RPW, EPI>(a, reinterpret_cast<float*>(dyn4), s_inv);
+}
+
+// ---------------------------------------------------------------------------
+// Block-wide helpers for token selection (kThreads threads).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned order_key(float f) {
+  const unsigned u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Exclusive prefix sum of one int per thread; returns the exclusive value and
+// writes the block total to *total.
+__device__ int block_excl_scan(int v, int* total) {
+  __shared__ int s_w[kWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += n;
+  }
+  __syncthreads();
+  if (lane == 31) s_w[warp] = inc;
+  __syncthreads();
+  int before = 0, all = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const int t = s_w[w];
+    if (w < warp) before += t;
+    all += t;
+  }
+  *total = all;
+  return before + inc - v;
+}
+
+__device__ float philox_u01(unsigned long long seed, unsigned long long ctr) {
+  unsigned c0 = (unsigned)ctr, c1 = (unsigned)(ctr >> 32), c2 = 0u, c3 = 0u;
+  unsigned k0 = (unsigned)seed, k1 = (unsigned)(seed >> 32);
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    const unsigned hi0 = __umulhi(0xD2511F53u, c0), lo0 = 0xD2511F53u * c0;
+    const unsigned hi1 = __umulhi(0xCD9E8D57u, c2), lo1 = 0xCD9E8D57u * c2;
+    const unsigned n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+    c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+    k0 += 0x9E3779B9u; k1 += 0xBB67AE85u;
+  }
+  return (float)(c0 >> 8) / 16777216.0f;
+}
+
+// One uniform in [0,1) with 24 bits; LCG mode reproduces the reference's
+// next_f32 (sampling.rs:120-126) in the reference's draw order.
+__device__ float rng_next(SeqState* st) {
+  if (st->rng_kind == RNG_LCG) {
+    st->rng_state = st->rng_state * 6364136223846793005ull + 1442695040888963407ull;
+    return (float)(unsigned)(st->rng_state >> 40) / 16777216.0f;
+  }
+  const float u = philox_u01(st->rng_seed, st->rng_counter);
+  st->rng_counter += 1ull;
+  return u;
+}
+
+struct SelectSmem {
+  float* val;   // [kMaxVocab] logits after penalty/suppression
+  int* tmp;     // [kMaxVocab] counts / candidate indices
+  float* cval;  // [kMaxVocab] candidate values
+  int* sidx;    // [kMaxVocab] sorted candidate indices
+};
+
+// Selects a token from smem logits `sv.val[0..V)` following the reference:
+// greedy -> argmax (lowest index on ties); top_k in (0,256] with top_p ~ 1 ->
+// device top-k sampler (non-finite as -FLT_MAX, u * sum walk); otherwise the
+// CPU sampler semantics (finite only, top-k, top-p renormalised, u walk).
+__device__ int block_select(const SelectSmem& s, int V, const SampleCfg& cfg, SeqState* st) {
+  __shared__ int s_res;
+  __shared__ unsigned s_hist[256];
+  __shared__ unsigned s_prefix;
+  __shared__ int s_rem;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  if (!cfg.do_sample) {
+    float bv = -FLT_MAX;
+    int bi = 0;
+    for (int v = tid; v < V; v += kThreads) {
+      const float x = s.val[v];
+      if (x > bv) { bv = x; bi = v; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    __shared__ float s_bv[kWarps];
+    __shared__ int s_bi[kWarps];
+    if (lane == 0) { s_bv[warp] = bv; s_bi[warp] = bi; }
+    __syncthreads();
+    if (tid == 0) {
+      float b = s_bv[0];
+      int i0 = s_bi[0];
+      for (int w = 1; w < kWarps; ++w)
+        if (s_bv[w] > b || (s_bv[w] == b && s_bi[w] < i0)) { b = s_bv[w]; i0 = s_bi[w]; }
+      s_res = i0;
+    }
+    __syncthreads();
+    return s_res;
+  }
+
+  const bool device_path = cfg.top_k > 0 && cfg.top_k <= 256 && cfg.top_p >= 0.999999f;
+  // eligibility: device path keeps every entry (non-finite -> -FLT_MAX);
+  // CPU path keeps finite entries only.
+  int nfin = 0;
+  for (int v = tid; v < V; v += kThreads) {
+    float x = s.val[v];
+    const bool fin = isfinite(x);
+    if (device_path && !fin) s.val[v] = -FLT_MAX;
+    nfin += fin ? 1 : 0;
+  }
+  int n_elig_total;
+  block_excl_scan(nfin, &n_elig_total);
+  if (device_path) n_elig_total = V;
+  if (n_elig_total == 0) {
+    if (tid == 0) st->error = 1;
+    __syncthreads();
+    return 0;
+  }
+  const int K = device_path ? min(cfg.top_k, V)
+                            : ((cfg.top_k > 0 && cfg.top_k < n_elig_total) ? cfg.top_k
+                                                                           : n_elig_total);
+
+  // Radix select (8-bit digits, MSB first) of the K-th largest key.
+  if (tid == 0) { s_prefix = 0u; s_rem = K; }
+  unsigned mask = 0u;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    s_hist[tid] = 0u;
+    __syncthreads();
+    const unsigned prefix = s_prefix;
+    for (int v = tid; v < V; v += kThreads) {
+      const float x = s.val[v];
+      if (!device_path && !isfinite(x)) continue;
+      const unsigned key = order_key(x);
+      if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    const int digit = 255 - tid;  // descending digit order
+    const int cnt = (int)s_hist[digit];
+    int tot;
+    const int before = block_excl_scan(cnt, &tot);
+    const int rem = s_rem;
+    __syncthreads();
+    if (before < rem && rem <= before + cnt) {
+      s_prefix = prefix | ((unsigned)digit << shift);
+      s_rem = rem - before;
+    }
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  const unsigned thr = s_prefix;
+  const int take_eq = s_rem;
+
+  // Index-ordered compaction of candidates: keys above thr, then the lowest
+  // `take_eq` indices equal to thr.
+  const int per = (V + kThreads - 1) / kThreads;
+  const int lo = tid * per, hi = min(V, lo + per);
+  int gt = 0, eq = 0;
+  for (int v = lo; v < hi; ++v) {
+    const float x = s.val[v];
+    if (!device_path && !isfinite(x)) continue;
+    const unsigned key = order_key(x);
+    gt += key > thr;
+    eq += key == thr;
+  }
+  int tot;
+  const int eq_before = block_excl_scan(eq, &tot);
+  const int eq_take = max(0, min(eq, take_eq - eq_before));
+  const int out_before = block_excl_scan(gt + eq_take, &tot);
+  {
+    int o = out_before, e = 0;
+    for (int v = lo; v < hi; ++v) {
+      const float x = s.val[v];
+      if (!device_path && !isfinite(x)) continue;
+      const unsigned key = order_key(x);
+      bool take = key > thr;
+      if (key == thr) { take = e < eq_take; ++e; }
+      if (take) { s.cval[o] = x; s.tmp[o] = v; ++o; }
+    }
+  }
+  __syncthreads();
+  // Rank sort: value descending, index ascending.
+  for (int i = tid; i < K; i += kThreads) {
+    const float vi = s.cval[i];
+    const int ii = s.tmp[i];
+    int rank = 0;
+    for (int j = 0; j < K; ++j) {
+      const float vj = s.cval[j];
+      const int ij = s.tmp[j];
+      rank += (vj > vi) || (vj == vi && ij < ii);
+    }
+    s.val[rank] = vi;
+    s.sidx[rank] = ii;
+  }
+  __syncthreads();
+
+  if (tid == 0) {
+    float* prob = s.cval;
+    const float mx = s.val[0];
+    const float temp = cfg.temperature;
+    float sum = 0.f;
+    for (int i = 0; i < K; ++i) {
+      const float p = expf((s.val[i] - mx) / temp);
+      prob[i] = p;
+      sum += p;
+    }
+    int tok;
+    if (device_path) {
+      const float u = rng_next(st);  // drawn before the kernel in the reference
+      if (!isfinite(sum) || sum <= 0.f) {
+        tok = s.sidx[0];
+      } else {
+        float target = u * sum;
+        tok = s.sidx[K - 1];
+        for (int i = 0; i < K; ++i) {
+          if (target <= prob[i]) { tok = s.sidx[i]; break; }
+          target -= prob[i];
+        }
+      }
+    } else if (!isfinite(sum) || sum <= 0.f) {
+      tok = s.sidx[0];  // no draw (sampling.rs:79-81)
+    } else {
+      int keep = K;
+      for (int i = 0; i < K; ++i) prob[i] /= sum;
+      if (cfg.top_p < 1.0f) {
+        float cum = 0.f;
+        keep = 0;
+        for (int i = 0; i < K; ++i) {
+          ++keep;
+          cum += prob[i];
+          if (cum >= cfg.top_p) break;
+        }
+        keep = max(keep, 1);
+        float ks = 0.f;
+        for (int i = 0; i < keep; ++i) ks += prob[i];
+        if (ks > 0.f)
+          for (int i = 0; i < keep; ++i) prob[i] /= ks;
+      }
+      float target = rng_next(st);
+      tok = s.sidx[keep - 1];
+      for (int i = 0; i < keep; ++i) {
+        if (target <= prob[i]) { tok = s.sidx[i]; break; }
+        target -= prob[i];
+      }
+    }
+    s_res = tok;
+  }
+  __syncthreads();
+  return s_res;
+}
+
+// Head: final/group RMSNorm + LM head GEMV over all CTAs; the last CTA to
+// finish applies penalty/suppression, selects the token and performs the
+// gathers the next stage needs (so no logits or tokens visit the host).
+__global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
+  extern __shared__ float4 dyn4[];
+  float* smem = reinterpret_cast<float*>(dyn4);
+  __shared__ float s_inv[1];
+  __shared__ bool s_last;
+  __shared__ int s_frame, s_sem;
+  if (!linear_body<1, 1, EPI_STORE>(a.lin, smem, s_inv)) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  if (threadIdx.x == 0) *a.ticket = 0u;
+  __threadfence();
+  if (a.role == ROLE_LOGITS_ONLY) return;
+
+  const int V = a.lin.N;
+  SelectSmem s{smem, reinterpret_cast<int*>(smem + kMaxVocab), smem + 2 * kMaxVocab,
+               reinterpret_cast<int*>(smem + 3 * kMaxVocab)};
+  const int tid = threadIdx.x;
+  for (int v = tid; v < V; v += kThreads) s.val[v] = __ldcg(a.lin.y + v);
+  if (tid == 0) { s_frame = a.st->frames; s_sem = a.st->semantic; }
+  __syncthreads();
+  if (a.role == ROLE_TALKER_STEP && a.penalty != 1.0f) {
+    for (int v = tid; v < V; v += kThreads) s.tmp[v] = 0;
+    __syncthreads();
+    for (int i = tid; i < s_frame; i += kThreads) {
+      const int t = a.history[i];
+      if (t >= 0 && t < V) atomicAdd(&s.tmp[t], 1);
+    }
+    __syncthreads();
+    for (int v = tid; v < V; v += kThreads) {
+      float x = s.val[v];
+      for (int c = s.tmp[v]; c > 0; --c) x = x < 0.f ? x * a.penalty : x / a.penalty;
+      s.val[v] = x;
+    }
+  }
+  if (a.suppress) {
+    for (int v = max(0, V - 1024) + tid; v < V; v += kThreads)
+      if (v != a.eos_token) s.val[v] = -__int_as_float(0x7f800000);
+  }
+  __syncthreads();
+  const int tok = block_select(s, V, a.cfg, a.st);
+  if (a.token_out && tid == 0) *a.token_out = tok;
+
+  const int H = a.H;
+  if (a.role == ROLE_TALKER_PREFILL || a.role == ROLE_TALKER_STEP) {
+    const float inv = s_inv[0];
+    const float* x = a.lin.x;
+    const float* g = a.lin.gamma;
+    const __nv_bfloat16* e = a.talker_codec_emb + (long long)tok * H;
+    for (int i = tid; i < H; i += kThreads) {
+      a.cp_prefix[i] = x[i] * inv * g[i];
+      a.cp_prefix[H + i] = __bfloat162float(e[i]);
+    }
+    if (tid == 0) {
+      a.st->semantic = tok;
+      if (tok == a.eos_token) a.st->halt = 1;
+    }
+  } else if (a.role == ROLE_CP_GROUP) {
+    const __nv_bfloat16* e = a.cp_emb + (long long)tok * H;
+    const bool last = a.group == a.last_group;
+    const float* tr = nullptr;
+    const __nv_bfloat16* se = nullptr;
+    if (last) {
+      tr = s_frame < a.st->n_trailing ? a.trailing + (long long)s_frame * H : a.tts_pad;
+      se = a.talker_codec_emb + (long long)s_sem * H;
+    }
+    for (int i = tid; i < H; i += kThreads) {
+      const float ev = __bfloat162float(e[i]);
+      a.cp_next[i] = ev;
+      const float sum = a.group == 0 ? ev : a.emb_sum[i] + ev;
+      a.emb_sum[i] = sum;
+      if (last) a.step_in[i] = (__bfloat162float(se[i]) + sum) + tr[i];
+    }
+    if (tid == 0) {
+      a.codes[(long long)s_frame * a.groups + 1 + a.group] = tok;
+      if (last) {
+        a.codes[(long long)s_frame * a.groups] = s_sem;
+        a.history_out[s_frame] = s_sem;
+        a.st->talker_pos = a.st->prefill_len + s_frame;
+        a.st->frames = s_frame + 1;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention: one CTA per (kv head, split). Prologue fuses QK-RMSNorm,
+// RoPE and the bf16 KV append of the current position; the last CTA of each
+// kv head merges the split partials (flash-decode combine).
+// ---------------------------------------------------------------------------
+template <int G>
+__global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
+  __shared__ float sq[G][kHeadDim];
+  __shared__ float sk[kHeadDim], sv[kHeadDim];
+  __shared__ float red[4][G + 1];
+  __shared__ float wm[4][G], wl[4][G];
+  __shared__ float wacc[4][G][kHeadDim];
+  __shared__ bool s_last;
+  pdl_wait();
+  if (a.halt && *a.halt) return;
+  const int h = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int pos = a.pos_ptr ? *a.pos_ptr : a.pos_const;
+  const int T = pos + 1;
+  const int kvh = a.kv.kv_heads;
+  const int q_out = a.q_heads * kHeadDim, kv_out = kvh * kHeadDim;
+
+  float qr[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) qr[g] = a.qkv[(h * G + g) * kHeadDim + tid];
+  const float kr = a.qkv[q_out + h * kHeadDim + tid];
+  const float vr = a.qkv[q_out + kv_out + h * kHeadDim + tid];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float t = warp_sum(qr[g] * qr[g]);
+    if (lane == 0) red[warp][g] = t;
+  }
+  {
+    const float t = warp_sum(kr * kr);
+    if (lane == 0) red[warp][G] = t;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float ss = red[0][g] + red[1][g] + red[2][g] + red[3][g];
+    sq[g][tid] = qr[g] * rsqrtf(ss / (float)kHeadDim + a.eps) * a.q_gamma[tid];
+  }
+  {
+    const float ss = red[0][G] + red[1][G] + red[2][G] + red[3][G];
+    sk[tid] = kr * rsqrtf(ss / (float)kHeadDim + a.eps) * a.k_gamma[tid];
+  }
+  __syncthreads();
+  const int pi = tid & 63;
+  const float c = a.rope_cos[pos * 64 + pi], sn = a.rope_sin[pos * 64 + pi];
+  float rq[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float x0 = sq[g][pi], x1 = sq[g][pi + 64];
+    rq[g] = tid < 64 ? x0 * c - x1 * sn : x1 * c + x0 * sn;
+  }
+  const float k0 = sk[pi], k1 = sk[pi + 64];
+  const float kroped = tid < 64 ? k0 * c - k1 * sn : k1 * c + k0 * sn;
+  __syncthreads();
+  const __nv_bfloat16 kb = __float2bfloat16_rn(kroped);
+  const __nv_bfloat16 vb = __float2bfloat16_rn(vr);
+#pragma unroll
+  for (int g = 0; g < G; ++g) sq[g][tid] = rq[g];
+  sk[tid] = __bfloat162float(kb);
+  sv[tid] = __bfloat162float(vb);
+  if (s == 0) {
+    kv_ptr(a.kv, a.layer, 0, h, pos)[tid] = kb;
+    kv_ptr(a.kv, a.layer, 1, h, pos)[tid] = vb;
+  }
+  __syncthreads();
+
+  const int chunk = (T + a.nsplit - 1) / a.nsplit;
+  const int start = s * chunk, end = min(T, start + chunk);
+  float q[G][4], m[G], l[G], acc[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { q[g][j] = sq[g][4 * lane + j]; acc[g][j] = 0.f; }
+  }
+  for (int p = start + warp; p < end; p += 4) {
+    float kf[4], vf[4];
+    if (p == pos) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { kf[j] = sk[4 * lane + j]; vf[j] = sv[4 * lane + j]; }
+    } else {
+      const uint2 ku = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 0, h, p) + 4 * lane);
+      const uint2 vu = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 1, h, p) + 4 * lane);
+      kf[0] = bf16lo(ku.x); kf[1] = bf16hi(ku.x); kf[2] = bf16lo(ku.y); kf[3] = bf16hi(ku.y);
+      vf[0] = bf16lo(vu.x); vf[1] = bf16hi(vu.x); vf[2] = bf16lo(vu.y); vf[3] = bf16hi(vu.y);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float d = q[g][0] * kf[0] + q[g][1] * kf[1] + q[g][2] * kf[2] + q[g][3] * kf[3];
+      d = warp_sum(d) * a.scale;
+      const float mn = fmaxf(m[g], d);
+      const float corr = expf(m[g] - mn), pe = expf(d - mn);
+      l[g] = l[g] * corr + pe;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[g][j] = acc[g][j] * corr + pe * vf[j];
+      m[g] = mn;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) wacc[warp][g][4 * lane + j] = acc[g][j];
+    if (lane == 0) { wm[warp][g] = m[g]; wl[warp][g] = l[g]; }
+  }
+  __syncthreads();
+  const int stride = 2 + kHeadDim;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][g]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < 4; ++w) {
+        if (wm[w][g] == -INFINITY) continue;
+        const float f = expf(wm[w][g] - M);
+        L += wl[w][g] * f;
+        A += wacc[w][g][tid] * f;
+      }
+    }
+    float* part = a.partial + ((long long)(h * G + g) * a.nsplit + s) * stride;
+    if (tid == 0) { part[0] = M; part[1] = L; }
+    part[2 + tid] = A;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&a.tickets[h], 1u) == (unsigned)a.nsplit - 1u;
+  __syncthreads();
+  if (!s_last) return;
+  if (tid == 0) a.tickets[h] = 0u;
+  __threadfence();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float* base = a.partial + (long long)(h * G + g) * a.nsplit * stride;
+    float M = -INFINITY;
+    for (int t = 0; t < a.nsplit; ++t) M = fmaxf(M, __ldcg(base + t * stride));
+    float L = 0.f, A = 0.f;
+    for (int t = 0; t < a.nsplit; ++t) {
+      const float mt = __ldcg(base + t * stride);
+      if (mt == -INFINITY) continue;
+      const float f = expf(mt - M);
+      L += __ldcg(base + t * stride + 1) * f;
+      A += __ldcg(base + t * stride + 2 + tid) * f;
+    }
+    a.out[(h * G + g) * kHeadDim + tid] = A / L;
+  }
+}
+
+// Prefill: QK-RMSNorm + RoPE for M rows at positions pos0.., K/V appended to
+// the cache as bf16; Q kept fp32 for the prefill attention.
+__global__ void __launch_bounds__(128) k_qk_prep(QkPrepArgs a) {
+  __shared__ float sx[kHeadDim];
+  __shared__ float red[4];
+  pdl_wait();
+  if (a.halt && *a.halt) return;
+  const int m = blockIdx.x, j = blockIdx.y, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int kvh = a.kv.kv_heads;
+  const int q_out = a.q_heads * kHeadDim, kv_out = kvh * kHeadDim;
+  const int ld = q_out + 2 * kv_out;
+  const float* row = a.qkv + (long long)m * ld;
+  const bool is_q = j < a.q_heads;
+  const int hh = is_q ? j : j - a.q_heads;
+  const float raw = is_q ? row[hh * kHeadDim + tid] : row[q_out + hh * kHeadDim + tid];
+  const float t = warp_sum(raw * raw);
+  if (lane == 0) red[warp] = t;
+  __syncthreads();
+  const float ss = red[0] + red[1] + red[2] + red[3];
+  const float* gam = is_q ? a.q_gamma : a.k_gamma;
+  sx[tid] = raw * rsqrtf(ss / (float)kHeadDim + a.eps) * gam[tid];
+  __syncthreads();
+  const int pos = a.pos0 + m;
+  const int pi = tid & 63;
+  const float c = a.rope_cos[pos * 64 + pi], sn = a.rope_sin[pos * 64 + pi];
+  const float x0 = sx[pi], x1 = sx[pi + 64];
+  const float r = tid < 64 ? x0 * c - x1 * sn : x1 * c + x0 * sn;
+  if (is_q) {
+    a.q_out[(long long)m * q_out + hh * kHeadDim + tid] = r;
+  } else {
+    kv_ptr(a.kv, a.layer, 0, hh, pos)[tid] = __float2bfloat16_rn(r);
+    kv_ptr(a.kv, a.layer, 1, hh, pos)[tid] =
+        __float2bfloat16_rn(row[q_out + kv_out + hh * kHeadDim + tid]);
+  }
+}
+
+// Prefill attention: one warp per (query row, q head), causal over the cache.
+__global__ void __launch_bounds__(128) k_attn_prefill(AttnPrefillArgs a) {
+  pdl_wait();
+  if (a.halt && *a.halt) return;
+  const int qh = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.y * 4 + warp;
+  if (m >= a.M) return;
+  const int G = a.q_heads / a.kv.kv_heads;
+  const int kh = qh / G;
+  const int pos = a.pos0 + m;
+  const int q_out = a.q_heads * kHeadDim;
+  float q[4], acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const float4 qv = *reinterpret_cast<const float4*>(a.q + (long long)m * q_out + qh * kHeadDim + 4 * lane);
+  q[0] = qv.x; q[1] = qv.y; q[2] = qv.z; q[3] = qv.w;
+  float mx = -INFINITY, l = 0.f;
+  for (int p = 0; p <= pos; ++p) {
+    const uint2 ku = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 0, kh, p) + 4 * lane);
+    const uint2 vu = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 1, kh, p) + 4 * lane);
+    float d = q[0] * bf16lo(ku.x) + q[1] * bf16hi(ku.x) + q[2] * bf16lo(ku.y) + q[3] * bf16hi(ku.y);
+    d = warp_sum(d) * a.scale;
+    const float mn = fmaxf(mx, d);
+    const float corr = expf(mx - mn), pe = expf(d - mn);
+    l = l * corr + pe;
+    acc[0] = acc[0] * corr + pe * bf16lo(vu.x);
+    acc[1] = acc[1] * corr + pe * bf16hi(vu.x);
+    acc[2] = acc[2] * corr + pe * bf16lo(vu.y);
+    acc[3] = acc[3] * corr + pe * bf16hi(vu.y);
+    mx = mn;
+  }
+  const float il = 1.0f / l;
+  *reinterpret_cast<float4*>(a.out + (long long)m * q_out + qh * kHeadDim + 4 * lane) =
+      make_float4(acc[0] * il, acc[1] * il, acc[2] * il, acc[3] * il);
+}
+
+__global__ void k_gather_rows(const __nv_bfloat16* table, const int* ids, int width, float* out) {
+  pdl_wait();
+  const int r = blockIdx.x;
+  const __nv_bfloat16* src = table + (long long)ids[r] * width;
+  for (int c = threadIdx.x; c < width; c += blockDim.x)
+    out[(long long)r * width + c] = __bfloat162float(src[c]);
+}
+
+__global__ void k_assemble_rows(const float* proj, const int* proj_index,
+                                const __nv_bfloat16* codec, const int* codec_ids,
+                                const float* xvec, int width, float* out) {
+  pdl_wait();
+  const int r = blockIdx.x;
+  const float* p = proj + (long long)proj_index[r] * width;
+  const int cid = codec_ids[r];
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+    float v = p[c];
+    if (cid >= 0) v += __bfloat162float(codec[(long long)cid * width + c]);
+    if (cid == -2) v += xvec[c];
+    out[(long long)r * width + c] = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+constexpr size_t kLinearSmem = sizeof(float) * (size_t)kXFloats;
+constexpr size_t kHeadSmem = sizeof(float) * 4 * (size_t)kMaxVocab;  // >= kLinearSmem
+
+template <int MT, int RPW, int EPI>
+cudaError_t configure_linear_t() {
+  return cudaFuncSetAttribute(k_linear<MT, RPW, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)kLinearSmem);
+}
+
+template <int EPI>
+cudaError_t configure_linear_epi() {
+  cudaError_t e;
+  if ((e = configure_linear_t<1, 1, EPI>()) != cudaSuccess) return e;
+  if ((e = configure_linear_t<1, 2, EPI>()) != cudaSuccess) return e;
+  if ((e = configure_linear_t<2, 1, EPI>()) != cudaSuccess) return e;
+  if ((e = configure_linear_t<2, 2, EPI>()) != cudaSuccess) return e;
+  if ((e = configure_linear_t<8, 1, EPI>()) != cudaSuccess) return e;
+  return configure_linear_t<8, 2, EPI>();
+}
+
+template <int MT, int RPW, int EPI>
+cudaError_t launch_linear_t(const LinearArgs& a, cudaStream_t stream) {
+  const size_t smem = kLinearSmem;
+  const int per_block = kWarps * RPW;
+  dim3 grid((a.N + per_block - 1) / per_block, (a.M + MT - 1) / MT);
+  return launch(k_linear<MT, RPW, EPI>, grid, dim3(kThreads), smem, stream, a);
+}
+
+template <int MT, int EPI>
+cudaError_t launch_linear_mt(const LinearArgs& a, cudaStream_t stream) {
+  // Two columns per warp only when that still leaves >= 2 CTAs per SM of work.
+  const int blocks2 = (a.N + 2 * kWarps - 1) / (2 * kWarps);
+  if (MT == 1 && blocks2 >= 256) return launch_linear_t<MT, 2, EPI>(a, stream);
+  return launch_linear_t<MT, 1, EPI>(a, stream);
+}
+
+template <int EPI>
+cudaError_t launch_linear_epi(const LinearArgs& a, cudaStream_t stream) {
+  if (a.M == 1) return launch_linear_mt<1, EPI>(a, stream);
+  if (a.M == 2) return launch_linear_mt<2, EPI>(a, stream);
+  return launch_linear_mt<8, EPI>(a, stream);
+}
+
+}  // namespace
+
+int max_sample_vocab() { return kMaxVocab; }
+
+cudaError_t launch_linear(const LinearArgs& a, Epilogue epi, cudaStream_t stream) {
+  if (a.K % 8 != 0 || a.ldx % 4 != 0 || a.M <= 0 || a.N <= 0) return cudaErrorInvalidValue;
+  switch (epi) {
+    case EPI_STORE: return launch_linear_epi<EPI_STORE>(a, stream);
+    case EPI_RESID: return launch_linear_epi<EPI_RESID>(a, stream);
+    case EPI_SWIGLU: return launch_linear_epi<EPI_SWIGLU>(a, stream);
+    case EPI_BIAS: return launch_linear_epi<EPI_BIAS>(a, stream);
+    case EPI_BIAS_SILU: return launch_linear_epi<EPI_BIAS_SILU>(a, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_head(const HeadArgs& a, cudaStream_t stream) {
+  if (a.lin.N > kMaxVocab || a.lin.M != 1 || a.lin.K % 8 != 0) return cudaErrorInvalidValue;
+  dim3 grid((a.lin.N + kWarps - 1) / kWarps);
+  return launch(k_head, grid, dim3(kThreads), kHeadSmem, stream, a);
+}
+
+cudaError_t configure_kernels() {
+  cudaError_t e;
+  if ((e = configure_linear_epi<EPI_STORE>()) != cudaSuccess) return e;
+  if ((e = configure_linear_epi<EPI_RESID>()) != cudaSuccess) return e;
+  if ((e = configure_linear_epi<EPI_SWIGLU>()) != cudaSuccess) return e;
+  if ((e = configure_linear_epi<EPI_BIAS>()) != cudaSuccess) return e;
+  if ((e = configure_linear_epi<EPI_BIAS_SILU>()) != cudaSuccess) return e;
+  return cudaFuncSetAttribute(k_head, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem);
+}
+
+cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
+  const int G = a.q_heads / a.kv.kv_heads;
+  dim3 grid(a.kv.kv_heads, a.nsplit);
+  switch (G) {
+    case 1: return launch(k_attn_decode<1>, grid, dim3(128), 0, stream, a);
+    case 2: return launch(k_attn_decode<2>, grid, dim3(128), 0, stream, a);
+    case 4: return launch(k_attn_decode<4>, grid, dim3(128), 0, stream, a);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_qk_prep(const QkPrepArgs& a, cudaStream_t stream) {
+  dim3 grid(a.M, a.q_heads + a.kv.kv_heads);
+  return launch(k_qk_prep, grid, dim3(128), 0, stream, a);
+}
+
+cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t stream) {
+  dim3 grid(a.q_heads, (a.M + 3) / 4);
+  return launch(k_attn_prefill, grid, dim3(128), 0, stream, a);
+}
+
+cudaError_t launch_gather_rows(const __nv_bfloat16* table, const int* ids, int n, int width,
+                               float* out, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  return launch(k_gather_rows, dim3(n), dim3(256), 0, stream, table, ids, width, out);
+}
+
+cudaError_t launch_assemble_rows(const float* proj, const int* proj_index,
+                                 const __nv_bfloat16* codec, const int* codec_ids,
+                                 const float* xvec, int n, int width, float* out,
+                                 cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  return launch(k_assemble_rows, dim3(n), dim3(256), 0, stream, proj, proj_index, codec,
+                codec_ids, xvec, width, out);
+}
+
+}  // namespace qtts

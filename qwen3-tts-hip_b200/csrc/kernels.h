@@ -1,0 +1,168 @@
+// Host-facing argument blocks and launchers for the sm_100a token-loop kernels.
+// All launchers enqueue on `stream` with programmatic dependent launch enabled,
+// so they may be captured into one CUDA graph per frame.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace qtts {
+
+// Output transform applied by the projection kernels.
+enum Epilogue : int {
+  EPI_STORE = 0,      // y = W x
+  EPI_RESID = 1,      // y = W x + r          (O-proj / down-proj residual)
+  EPI_SWIGLU = 2,     // y[c] = silu(W[c] x) * (W[N + c] x)   (gate|up, N = intermediate)
+  EPI_BIAS = 3,       // y = W x + b          (small_to_mtp_projection, text fc2)
+  EPI_BIAS_SILU = 4,  // y = silu(W x + b)    (text fc1)
+};
+
+struct LinearArgs {
+  const __nv_bfloat16* W;  // [rows, K] row-major (PyTorch [out, in])
+  const float* x;          // [M, ldx]
+  int ldx;
+  const float* gamma;      // optional RMSNorm gamma [K]; nullptr = raw input
+  float eps;
+  float* y;                // [M, ldy]
+  int ldy;
+  const float* resid;      // EPI_RESID source [M, ldr] (may alias y)
+  int ldr;
+  const float* bias;       // EPI_BIAS* [N]
+  int M, N, K;
+  const int* halt;         // optional: kernel is a no-op while *halt != 0
+};
+
+// Sampling parameters of one token kind (talker or subtalker).
+struct SampleCfg {
+  int do_sample;
+  int top_k;
+  float top_p;
+  float temperature;
+};
+
+enum RngKind : int { RNG_LCG = 0, RNG_PHILOX = 1 };
+
+// Per-sequence device-resident loop state (one 64-byte block).
+struct SeqState {
+  int frames;       // frames whose 16 codes are complete
+  int semantic;     // semantic token that starts the next frame
+  int talker_pos;   // cache position of the next talker decode step
+  int prefill_len;  // P
+  int n_trailing;   // trailing text rows uploaded
+  int halt;         // set once the semantic token is codec EOS
+  int error;        // nonzero: device-side invalid state (e.g. no finite logits)
+  int rng_kind;
+  unsigned long long rng_state;    // LCG state (reference draw order)
+  unsigned long long rng_seed;     // Philox key
+  unsigned long long rng_counter;  // Philox counter
+  int pad[2];
+};
+
+enum HeadRole : int {
+  ROLE_TALKER_PREFILL = 0,  // token from prefill; no penalty
+  ROLE_TALKER_STEP = 1,     // token from a decode step; penalty over history
+  ROLE_CP_GROUP = 2,        // CodePredictor group token
+  ROLE_LOGITS_ONLY = 3,     // debug: logits only
+};
+
+struct HeadArgs {
+  LinearArgs lin;         // M = 1 projection to logits (lin.y = logits)
+  unsigned* ticket;       // zero-initialised counter (reset by the last CTA)
+  int role;
+  SampleCfg cfg;
+  SeqState* st;
+  // talker
+  float penalty;
+  const int* history;     // semantic history (length st->frames)
+  int eos_token;
+  int suppress;           // suppress [V-1024, V) except eos
+  const __nv_bfloat16* talker_codec_emb;  // [V, H]
+  float* cp_prefix;       // [2, H]: normed hidden, codec_emb[semantic]
+  int H;
+  // CodePredictor
+  int group, last_group;
+  const __nv_bfloat16* cp_emb;  // [Vcp, H] embedding of this group
+  float* cp_next;          // [H] next group input (pre-projection)
+  float* emb_sum;          // [H]
+  float* step_in;          // [H] talker decode input (written by the last group)
+  const float* trailing;   // [n_trailing, H]
+  const float* tts_pad;    // [H]
+  int* codes;              // [max_frames, groups]
+  int* history_out;        // semantic history
+  int groups;
+  int* token_out;          // optional: selected token
+};
+
+struct AttnDecodeArgs {
+  const float* qkv;        // raw projections of the current position [q_out + 2 kv_out]
+  const float* q_gamma;
+  const float* k_gamma;
+  float eps;
+  const float* rope_cos;   // [positions, 64]
+  const float* rope_sin;
+  KvView kv;
+  int layer;
+  const int* pos_ptr;      // position = pos_ptr ? *pos_ptr : pos_const
+  int pos_const;
+  int q_heads;
+  float scale;
+  float* partial;          // [q_heads, nsplit, 2 + 128]
+  unsigned* tickets;       // [kv_heads]
+  float* out;              // [q_heads * 128]
+  int nsplit;
+  const int* halt;
+};
+
+struct QkPrepArgs {
+  const float* qkv;        // [M, q_out + 2 kv_out]
+  const float* q_gamma;
+  const float* k_gamma;
+  float eps;
+  const float* rope_cos;
+  const float* rope_sin;
+  KvView kv;
+  int layer;
+  int pos0;
+  int M;
+  int q_heads;
+  float* q_out;            // [M, q_heads * 128]
+  const int* halt;
+};
+
+struct AttnPrefillArgs {
+  const float* q;          // [M, q_heads * 128] normed + roped
+  KvView kv;
+  int layer;
+  int pos0;
+  int M;
+  int q_heads;
+  float scale;
+  float* out;              // [M, q_heads * 128]
+  const int* halt;
+};
+
+cudaError_t launch_linear(const LinearArgs& a, Epilogue epi, cudaStream_t stream);
+cudaError_t launch_head(const HeadArgs& a, cudaStream_t stream);
+cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t stream);
+cudaError_t launch_qk_prep(const QkPrepArgs& a, cudaStream_t stream);
+cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t stream);
+
+// out[r, :] = float(table[ids[r], :])
+cudaError_t launch_gather_rows(const __nv_bfloat16* table, const int* ids, int n, int width,
+                               float* out, cudaStream_t stream);
+// out[r] = proj[proj_index[r]] + (codec_ids[r] >= 0 ? codec[codec_ids[r]] :
+//                                  codec_ids[r] == -2 ? xvec : 0)
+cudaError_t launch_assemble_rows(const float* proj, const int* proj_index,
+                                 const __nv_bfloat16* codec, const int* codec_ids,
+                                 const float* xvec, int n, int width, float* out,
+                                 cudaStream_t stream);
+
+int max_sample_vocab();
+// Sets the dynamic shared-memory limits of every kernel; call once per device
+// before the first launch (and before any stream capture).
+cudaError_t configure_kernels();
+
+}  // namespace qtts
