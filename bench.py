@@ -1,0 +1,338 @@
+"""Benchmark of the B200 Qwen3-TTS token loop (codec frames/s, RTF).
+
+One step = one request through the public API: content ids -> device text
+prep -> talker prefill -> every 80 ms frame (CodePredictor pass + talker
+decode step + on-device sampling) -> codes back on the host. Default workload
+is BASELINE config 1 (0.6B-shaped, 64 random ids, 240 frames, Qwen-default
+sampling, Philox seed 0, batch 1) on random-init weights (oracle/synth.py).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+Multi-GPU (torchrun, one rank per GPU): independent request replicas, no
+collective on the data path; value = all ranks' frames / max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # BASELINE.json configs[1]
+    "0.6b-sampled": dict(shape="0.6b", n_ids=64, frames=240, do_sample=True, top_k=50,
+                         top_p=1.0, temperature=0.9, penalty=1.05, sub_sample=True, sub_top_k=50,
+                         sub_temperature=0.9, rng="philox"),
+    # north-star target (0.6B greedy 240 frames); prompt as BASELINE configs[0] (32 ids)
+    "0.6b-greedy": dict(shape="0.6b", n_ids=32, frames=240, do_sample=False, top_k=50, top_p=1.0,
+                        temperature=0.9, penalty=1.0, sub_sample=False, sub_top_k=50,
+                        sub_temperature=0.9, rng="lcg"),
+    # BASELINE.json configs[2]
+    "1.7b-greedy": dict(shape="1.7b", n_ids=128, frames=240, do_sample=False, top_k=50, top_p=1.0,
+                        temperature=0.9, penalty=1.0, sub_sample=False, sub_top_k=50,
+                        sub_temperature=0.9, rng="lcg"),
+}
+FRAME_SECONDS = 0.08
+
+
+def options(pkg, c, seed):
+    return pkg.GenerateOptions(decode_audio=False, max_frames=c["frames"], do_sample=c["do_sample"],
+                               top_k=c["top_k"], top_p=c["top_p"], temperature=c["temperature"],
+                               repetition_penalty=c["penalty"], subtalker_dosample=c["sub_sample"],
+                               subtalker_top_k=c["sub_top_k"],
+                               subtalker_temperature=c["sub_temperature"], seed=seed, rng=c["rng"])
+
+
+def model_dir(shape: str) -> Path:
+    base = Path(os.environ.get("QTTS_BENCH_MODELS", "/tmp/qtts_bench_models"))
+    return base / shape
+
+
+def frame_bytes(shape_name: str, P: int, frames: int) -> float:
+    """Algorithmic HBM bytes of one average frame: every weight read once per
+    pass (talker step once, CodePredictor layers + head once per group pass),
+    plus the talker KV cache read (positions 0..pos) and append, all bf16."""
+    from oracle import synth
+
+    s = synth.SHAPES[shape_name]
+    q_out, kv_out = s.q_heads * s.head_dim, s.kv_heads * s.head_dim
+
+    def layer(h, inter):
+        return 2 * ((q_out + 2 * kv_out) * h + h * q_out + 2 * inter * h + h * inter)
+
+    talker = s.layers * layer(s.hidden, s.intermediate) + 2 * s.vocab * s.hidden
+    kv_per_pos = 2 * s.layers * 2 * kv_out  # K and V, bf16
+    avg_pos = P + (frames - 1) / 2.0 + 1
+    talker += kv_per_pos * (avg_pos + 1)
+    cp_pass = s.cp_layers * layer(s.cp_hidden, s.cp_intermediate) + 2 * s.cp_vocab * s.cp_hidden
+    if s.cp_hidden != s.hidden:
+        cp_pass += 2 * s.cp_hidden * s.hidden
+    return talker + (s.num_code_groups - 1) * cp_pass
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        loaded = [x for x in sm if x > 0.5 * (mx or 1)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except (OSError, json.JSONDecodeError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def committed_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "gateup_gemv_0p6b.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_reference_run(c, mdir, ids, n_frames, steps, warmup, seed=0):
+    """The CPU oracle (PyTorch-CPU fp32 restatement of the reference loop) on a
+    bounded sample: prefill + n_frames frames per step. Returns frames/s."""
+    import torch
+
+    from oracle import qtts_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    m = O.OracleModel(mdir, 512)
+    t_cfg = O.SamplingConfig(c["do_sample"], c["top_k"], c["top_p"], c["temperature"])
+    s_cfg = O.SamplingConfig(c["sub_sample"], c["sub_top_k"], 1.0, c["sub_temperature"])
+    pre, tr, pad = m.prepare(list(ids))
+    times, frames = [], 0
+    with torch.inference_mode():
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            codes, _, _ = m.rollout(pre, tr, pad, n_frames, t_cfg, s_cfg, c["penalty"], seed,
+                                    c["rng"])
+            dt = time.perf_counter() - t0
+            if i >= warmup:
+                times.append(dt)
+                frames += len(codes) // 16
+    total = sum(times)
+    return frames / total, frames, total, torch.get_num_threads(), pre.shape[0]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="0.6b-sampled", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-frames", type=int, default=6, help="frames per CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--frames", type=int, default=0, help="override frames per request (profiling)")
+    args = ap.parse_args()
+    c = dict(CONFIGS[args.config])
+    if args.frames:
+        c["frames"] = args.frames
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    metric = "codec_frames_per_s"
+    workload = {"workload": f"{args.config}: {c['shape']}-shaped talker+CodePredictor, "
+                            f"{c['n_ids']} random text ids, {c['frames']} frames, batch 1 per GPU",
+                "shape": c["shape"], "frames_per_request": c["frames"], "text_ids": c["n_ids"],
+                "sampling": "top_k=50 T=0.9 penalty=1.05, subtalker top_k=50 T=0.9"
+                if c["do_sample"] else "greedy", "rng": c["rng"],
+                "l2": "no flush: each frame streams ~3.3 GB of weights (> 126 MB L2)",
+                "parallelism": f"replicas{max(world, args.gpus)}"}
+
+    from oracle import synth
+
+    mdir = model_dir(c["shape"])
+    ids = np.random.default_rng(0).integers(0, synth.SHAPES[c["shape"]].text_vocab - 1000,
+                                            c["n_ids"]).astype(np.uint32)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        synth.write_model(mdir, c["shape"], 0)
+        fps, frames, total, cores, P = cpu_reference_run(c, mdir, ids, args.cpu_frames,
+                                                         args.steps, args.warmup)
+        sample = (f"prefill P={P} + {args.cpu_frames} frames per step (of {c['frames']}), "
+                  f"{args.steps} timed steps")
+        line = {"metric": metric, "value": fps, "unit": "frames/s", "impl": "reference",
+                "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1000 * total / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "rtf": 1.0 / (fps * FRAME_SECONDS), "config": workload,
+                "cpu_baseline": {"value": fps, "unit": "frames/s", "cores": cores, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": fps, "unit": "frames/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "note": "reference's Rust/ROCm path cannot run here (no cargo, no AMD GPU); "
+                        "timed arm is the repo's PyTorch-CPU fp32 restatement (oracle/)"}
+        print(json.dumps(line))
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    pkg = __graft_entry__.load_package()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    if rank == 0:
+        synth.write_model(mdir, c["shape"], 0)
+    if world > 1:
+        dist.barrier()
+
+    eng = pkg.HipTtsEngine.load_with_options(mdir, pkg.EngineOptions(local, 512))
+    opts = options(pkg, c, seed=rank)
+    for _ in range(args.warmup):
+        eng.generate_codes_from_ids(ids, opts)
+
+    dev_ms, wall_s, frames, launches, last = 0.0, 0.0, 0, 0, None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            out = eng.generate_codes_from_ids(ids, opts)
+            wall_s += time.perf_counter() - t0
+            tm = eng.last_timings()
+            dev_ms += tm["prefill_ms"] + tm["frames_ms"]
+            frames += out.frames
+            launches += tm["kernels"]
+            last = (out, tm)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        t = torch.tensor([dev_ms, wall_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        f = torch.tensor([frames, launches], dtype=torch.float64, device="cuda")
+        dist.all_reduce(f, op=dist.ReduceOp.SUM)
+        dev_ms_max, wall_max = t.tolist()
+        frames_all, launches_all = (int(x) for x in f.tolist())
+    else:
+        dev_ms_max, wall_max, frames_all, launches_all = dev_ms, wall_s, frames, launches
+
+    # dominant kernel: talker gate|up GEMV (+ RMSNorm prologue, SwiGLU epilogue)
+    ms_k, bytes_k = eng.profile_projection(0, 280)
+    peaks, peak_kind = measured_peaks()
+    achieved = bytes_k / (ms_k * 1e-3) / 1e9
+    P = 9 + c["n_ids"]
+    out, tm = last
+    fb = frame_bytes(c["shape"], P, c["frames"])
+    frame_ms = tm["frames_ms"] / max(1, tm["frames"])
+    frame_gbs = fb / (frame_ms * 1e-3) / 1e9
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    value = frames_all / (dev_ms_max / 1000.0)
+    e2e = frames_all / wall_max
+    line = {
+        "metric": metric, "value": value, "unit": "frames/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init N(0,0.02) bf16 weights, seed 0; random text ids)",
+        "rtf": (dev_ms_max / 1000.0) / (frames_all / world * FRAME_SECONDS),
+        "frames_per_step": frames_all / world / args.steps,
+        "config": workload,
+        "e2e": {"value": e2e, "unit": "frames/s",
+                "rtf": wall_max / (frames_all / world * FRAME_SECONDS),
+                "h2d_bytes_per_step": int(ids.nbytes),
+                "d2h_bytes_per_step": int(out.frames * 16 * 4 + 64)},
+        "gpu_launches": launches_all,
+        "roofline": {"bound": "hbm", "kernel": "k_linear<M=1,SwiGLU> talker gate|up (1024->2x3072)",
+                     "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind,
+                     "bytes_per_launch": bytes_k, "ms_per_launch": ms_k,
+                     "traffic": committed_traffic()},
+        "frame_roofline": {"bytes_per_frame": fb, "ms_per_frame": frame_ms,
+                           "achieved": frame_gbs, "unit": "GB/s",
+                           "frac": frame_gbs / peaks["hbm_gbs"], "peak_kind": peak_kind,
+                           "frac_of_8tbs": frame_gbs / 8000.0},
+        "clocks": clk.summary(),
+        "prefill_ms": tm["prefill_ms"],
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        fps, cf, total, cores, _ = cpu_reference_run(c, mdir, ids, args.cpu_frames, 1, 0)
+        line["cpu_baseline"] = {"value": fps, "unit": "frames/s", "cores": cores, "kind": "port",
+                                "sample": f"prefill P={P} + {args.cpu_frames} frames, 1 run"}
+    print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

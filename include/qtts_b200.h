@@ -214,6 +214,18 @@ int32_t qtts_code_predictor(qtts_engine* engine, const float* talker_hidden,
 int32_t qtts_last_timings(const qtts_engine* engine, float* prefill_ms, float* frames_ms,
                           size_t* frames);
 
+/* Kernels launched by the last generation (prefill launches + frame-graph
+ * nodes x graph launches). */
+int32_t qtts_last_launch_count(const qtts_engine* engine, size_t* kernels);
+
+/* Measurement hook (no reference counterpart): times `launches` back-to-back
+ * launches of one talker projection kernel, cycling through all layers'
+ * weights, with CUDA events on the engine stream. which: 0 gate|up+SwiGLU,
+ * 1 QKV, 2 down+residual, 3 O+residual. bytes_per_launch = algorithmic bytes
+ * (bf16 weights + fp32 activations in/out). Clobbers the talker workspace. */
+int32_t qtts_profile_projection(qtts_engine* engine, int32_t which, int32_t launches,
+                                float* ms_per_launch, double* bytes_per_launch);
+
 #ifdef __cplusplus
 }
 #endif

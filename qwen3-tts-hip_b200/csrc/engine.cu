@@ -298,6 +298,9 @@ class Engine {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
   float last_prefill_ms = 0.f, last_frames_ms = 0.f;
   size_t last_frames = 0;
+  size_t launches = 0;        // kernels enqueued directly (or captured) by this engine
+  size_t last_launches = 0;   // kernels launched by the last generation (graphs expanded)
+  std::map<SampleKey, size_t> graph_nodes;
 
   // current sequence (host view)
   int seq_P = 0;
@@ -318,6 +321,7 @@ class Engine {
               int K, Epilogue epi, const int* halt) {
     LinearArgs a{W, x, ldx, gamma, eps, y, ldy, resid, ldr, bias, M, N, K, halt};
     QCK(launch_linear(a, epi, stream));
+    ++launches;
   }
   void stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int pos0, const int* halt);
   void stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* pos_ptr, int pos_const,
@@ -609,6 +613,7 @@ void Engine::stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int 
     QCK(launch_qk_prep(qa, stream));
     AttnPrefillArgs pa{B.q, kv, l, pos0, M, c.q_heads, scale, B.attn, halt};
     QCK(launch_attn_prefill(pa, stream));
+    launches += 2;
     linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, M,
            c.hidden, S.q_out, EPI_RESID, halt);
     linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
@@ -630,6 +635,7 @@ void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* 
                       kv,      l,         pos_ptr,  pos_const, c.q_heads, scale,
                       partial, tickets + 8, B.attn, nsplit,  halt};
     QCK(launch_attn_decode(da, stream));
+    ++launches;
     linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, 1,
            c.hidden, S.q_out, EPI_RESID, halt);
     linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
@@ -668,6 +674,7 @@ void Engine::talker_head(int role, const float* x, const SampleCfg& c, float pen
   a.cp_prefix = cp_prefix_dst;
   a.token_out = token;
   QCK(launch_head(a, stream));
+  ++launches;
 }
 
 void Engine::cp_head(int group, const float* x, const SampleCfg& c, const int* halt) {
@@ -685,6 +692,7 @@ void Engine::cp_head(int group, const float* x, const SampleCfg& c, const int* h
   a.trailing = trailing;
   a.tts_pad = tts_pad;
   QCK(launch_head(a, stream));
+  ++launches;
 }
 
 // One frame: CodePredictor pass (code_predictor.rs:366-471) then, unless it is
@@ -715,15 +723,19 @@ cudaGraphExec_t Engine::frame_graph(const SampleKey& k) {
   auto it = graphs.find(k);
   if (it != graphs.end()) return it->second;
   cudaGraph_t g = nullptr;
+  const size_t before = launches;
   QCK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
   try {
     enqueue_frame(k);
   } catch (...) {
     cudaStreamEndCapture(stream, &g);
     if (g) cudaGraphDestroy(g);
+    launches = before;
     throw;
   }
   QCK(cudaStreamEndCapture(stream, &g));
+  graph_nodes[k] = launches - before;
+  launches = before;
   cudaGraphExec_t exec = nullptr;
   cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
   cudaGraphDestroy(g);
@@ -841,6 +853,7 @@ void Engine::begin(int P, int n_trailing, const qtts_generate_options& o) {
   *st_host = s;
   QCK(cudaMemcpyAsync(st, st_host, sizeof(SeqState), cudaMemcpyHostToDevice, stream));
   QCK(cudaEventRecord(ev0, stream));
+  const size_t l0 = launches;
   stack_rows(talker, tb, tkv, P, 0, nullptr);
   talker_head(ROLE_TALKER_PREFILL, tb.x + (size_t)(P - 1) * cfg.talker.hidden, talker_cfg(o),
               1.0f, nullptr, cp_prefix_target());
@@ -856,6 +869,7 @@ void Engine::begin(int P, int n_trailing, const qtts_generate_options& o) {
   QCK(cudaEventElapsedTime(&last_prefill_ms, ev0, ev1));
   last_frames_ms = 0.f;
   last_frames = 0;
+  last_launches = launches - l0;
 }
 
 void Engine::sync_state() {
@@ -881,6 +895,7 @@ size_t Engine::run_frames(size_t n) {
   for (size_t i = 0; i < n; ++i) {
     const bool is_last = begin + i + 1 >= seq_max_frames;
     QCK(cudaGraphLaunch(is_last ? gl : gf, stream));
+    last_launches += graph_nodes[is_last ? last : full];
   }
   QCK(cudaEventRecord(ev2, stream));
   sync_state();
@@ -1460,6 +1475,61 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
       QCK(cudaMemcpy(logits_out, e.dbg_logits, (size_t)na * C.vocab * 4, cudaMemcpyDeviceToHost));
     e.seq_ended = true;  // the talker state was not advanced: no stream may continue
     ++e.seq_id;
+  });
+}
+
+int32_t qtts_last_launch_count(const qtts_engine* h, size_t* kernels) {
+  return guard([&] {
+    need(h, "engine");
+    need(kernels, "kernels");
+    *kernels = h->e->last_launches;
+  });
+}
+
+int32_t qtts_profile_projection(qtts_engine* h, int32_t which, int32_t n_launch,
+                                float* ms_per_launch, double* bytes_per_launch) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(ms_per_launch, "ms_per_launch");
+    if (n_launch <= 0) qtts::invalid("launches must be positive");
+    qtts::DevStack& S = e.talker;
+    const auto& c = S.c;
+    const qtts::StackBufs& B = e.tb;
+    double bytes = 0;
+    auto one = [&](int l) {
+      switch (which) {
+        case 0:  // gate|up + SwiGLU, RMSNorm prologue
+          e.linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
+                   nullptr, 1, c.intermediate, c.hidden, qtts::EPI_SWIGLU, nullptr);
+          bytes = 2.0 * c.intermediate * c.hidden * 2 + 4.0 * (c.hidden * 2 + c.intermediate);
+          break;
+        case 1:  // QKV, RMSNorm prologue
+          e.linear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr,
+                   1, S.qkv_w, c.hidden, qtts::EPI_STORE, nullptr);
+          bytes = 2.0 * S.qkv_w * c.hidden + 4.0 * (c.hidden * 2 + S.qkv_w);
+          break;
+        case 2:  // down + residual
+          e.linear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.q, c.hidden, B.h1, c.hidden,
+                   nullptr, 1, c.hidden, c.intermediate, qtts::EPI_RESID, nullptr);
+          bytes = 2.0 * c.hidden * c.intermediate + 4.0 * (c.intermediate + 2 * c.hidden);
+          break;
+        default:  // O + residual
+          e.linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.q, c.hidden, B.x, c.hidden, nullptr, 1,
+                   c.hidden, S.q_out, qtts::EPI_RESID, nullptr);
+          bytes = 2.0 * c.hidden * S.q_out + 4.0 * (S.q_out + 2 * c.hidden);
+      }
+    };
+    // Cycle through every layer's weights so each launch streams from HBM
+    // (28 distinct matrices exceed the 126 MB L2).
+    for (int i = 0; i < c.layers; ++i) one(i);
+    QCK(cudaEventRecord(e.ev1, e.stream));
+    for (int i = 0; i < n_launch; ++i) one(i % c.layers);
+    QCK(cudaEventRecord(e.ev2, e.stream));
+    QCK(cudaEventSynchronize(e.ev2));
+    float ms = 0.f;
+    QCK(cudaEventElapsedTime(&ms, e.ev1, e.ev2));
+    *ms_per_launch = ms / n_launch;
+    if (bytes_per_launch) *bytes_per_launch = bytes;
   });
 }
 

@@ -118,6 +118,8 @@ SIGNATURES = {
     "qtts_talker_decode_step": (C.c_int32, [_P, _F, C.c_size_t, _F, _F, _I32]),
     "qtts_code_predictor": (C.c_int32, [_P, _F, _F, C.POINTER(_Options), _I32, _F, _F]),
     "qtts_last_timings": (C.c_int32, [_P, _F, _F, _SZ]),
+    "qtts_last_launch_count": (C.c_int32, [_P, _SZ]),
+    "qtts_profile_projection": (C.c_int32, [_P, C.c_int32, C.c_int32, _F, C.POINTER(C.c_double)]),
 }
 
 
@@ -434,7 +436,18 @@ class HipTtsEngine:
     def last_timings(self):
         p, f, n = C.c_float(), C.c_float(), C.c_size_t()
         _check(lib().qtts_last_timings(self._h, C.byref(p), C.byref(f), C.byref(n)))
-        return {"prefill_ms": p.value, "frames_ms": f.value, "frames": n.value}
+        k = C.c_size_t()
+        _check(lib().qtts_last_launch_count(self._h, C.byref(k)))
+        return {"prefill_ms": p.value, "frames_ms": f.value, "frames": n.value,
+                "kernels": k.value}
+
+    def profile_projection(self, which: int = 0, launches: int = 280):
+        """Average device time (ms) and algorithmic bytes of one talker
+        projection launch (0 gate|up, 1 QKV, 2 down, 3 O), weights from HBM."""
+        ms, b = C.c_float(), C.c_double()
+        _check(lib().qtts_profile_projection(self._h, int(which), int(launches), C.byref(ms),
+                                             C.byref(b)))
+        return ms.value, b.value
 
 
 class HipTtsStream:
