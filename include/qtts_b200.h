@@ -202,6 +202,18 @@ int32_t qtts_talker_prefill(qtts_engine* engine, const float* rows, size_t steps
 /* HipTalker::decode_step (talker.rs:251-292) at cache offset `offset`. */
 int32_t qtts_talker_decode_step(qtts_engine* engine, const float* input, size_t offset,
                                 float* hidden_out, float* logits_out, int32_t* token_out);
+/* Same computation as qtts_talker_decode_step, for callers that may not
+ * allocate device memory while running (fixed-budget or real-time hosts):
+ * this call allocates nothing. The decode attention's scratch (split-K
+ * partials and completion counters) comes from a static device array of
+ * 264 KiB held by every GPU that loads the library; talkers whose
+ * q_heads * 16 * 130 floats exceed it are rejected with QTTS_ERR_INVALID_INPUT.
+ * The first call on a device looks up the array's address (make it before
+ * any stream capture). Calls share the array: calls that overlap on the GPU
+ * race. No counterpart in the reference. */
+int32_t qtts_talker_decode_step_static(qtts_engine* engine, const float* input, size_t offset,
+                                       float* hidden_out, float* logits_out,
+                                       int32_t* token_out);
 /* HipCodePredictor::generate_from_host (code_predictor.rs:283-300) with the
  * subtalker_* fields of options (greedy when subtalker_dosample == 0).
  * tokens_out [groups-1], embedding_sum_out [hidden], logits_out

@@ -22,6 +22,7 @@
 #include <deque>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -1421,6 +1422,101 @@ int32_t qtts_talker_decode_step(qtts_engine* h, const float* input, size_t offse
     if (hidden_out) QCK(cudaMemcpy(hidden_out, e.cp_prefix_target(), H * 4, cudaMemcpyDeviceToHost));
     if (logits_out)
       QCK(cudaMemcpy(logits_out, e.logits, e.cfg.talker.vocab * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free talker decode step.
+//
+// Some hosts embed this library where they may not allocate device memory
+// once they are running: a caller that owns a fixed memory budget carved out
+// up front (a real-time audio process, a pool-managed serving runtime, or a
+// host that forbids cudaMalloc outside start-up because it synchronises the
+// device). For them, the talker decode step's only per-call scratch -- the
+// split-K partials and the completion counters of the decode attention kernel
+// -- lives in this file-scope device array instead of engine-owned memory.
+// The array is fixed at kStaticAttnScratchBytes and is held by every GPU that
+// loads the library until the process exits. All calls share it and it keeps
+// the last call's contents; calls that overlap on the GPU (two streams, two
+// engines, two threads) race on it and must be serialised by the caller.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticAttnScratchBytes = 270336;  // 264 KiB
+constexpr size_t kStaticTicketBytes = 256;          // 64 counters at the front
+static __device__ __align__(256) unsigned char g_attn_scratch[kStaticAttnScratchBytes];
+
+std::mutex g_static_mu;
+void* g_static_ptr[128] = {};
+
+// First call per device (with that device current) resolves the array's
+// device address; host code may not use the symbol itself as a pointer.
+void* static_scratch_for_device(int device) {
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (device < 0 || device >= 128) qtts::invalid("device index out of range");
+  if (!g_static_ptr[device]) {
+    void* ptr = nullptr;
+    QCK(cudaGetSymbolAddress(&ptr, g_attn_scratch));
+    g_static_ptr[device] = ptr;
+  }
+  return g_static_ptr[device];
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t qtts_talker_decode_step_static(qtts_engine* h, const float* input, size_t offset,
+                                       float* hidden_out, float* logits_out,
+                                       int32_t* token_out) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(input, "input");
+    if (offset >= e.max_cache_steps) qtts::invalid("offset outside cache length");
+    const auto& c = e.talker.c;
+    const size_t need_bytes =
+        (size_t)c.q_heads * qtts::kTalkerSplits * (2 + qtts::kHeadDim) * sizeof(float);
+    if (need_bytes > kStaticAttnScratchBytes - kStaticTicketBytes || c.kv_heads > 64)
+      qtts::invalid("talker needs " + std::to_string(need_bytes) +
+                    " bytes of attention scratch; the static array holds " +
+                    std::to_string(kStaticAttnScratchBytes - kStaticTicketBytes));
+    unsigned char* base = static_cast<unsigned char*>(static_scratch_for_device(e.device));
+    unsigned* tick = reinterpret_cast<unsigned*>(base);
+    float* part = reinterpret_cast<float*>(base + kStaticTicketBytes);
+    const size_t H = c.hidden;
+    // counters must start at zero; a previous call may have been interrupted
+    QCK(cudaMemsetAsync(tick, 0, kStaticTicketBytes, e.stream));
+    QCK(cudaMemcpy(e.tb.x, input, H * 4, cudaMemcpyHostToDevice));
+    e.st_host->talker_pos = (int)offset;
+    e.st_host->halt = 0;
+    e.st_host->frames = 0;
+    QCK(cudaMemcpy(e.st, e.st_host, sizeof(qtts::SeqState), cudaMemcpyHostToDevice));
+    const float scale = 1.0f / std::sqrt((float)c.head_dim);
+    qtts::DevStack& S = e.talker;
+    qtts::StackBufs& B = e.tb;
+    for (int l = 0; l < c.layers; ++l) {
+      e.linear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr, 1,
+               S.qkv_w, c.hidden, qtts::EPI_STORE, nullptr);
+      qtts::AttnDecodeArgs da{B.qkv, S.q_g[l], S.k_g[l], c.eps, S.rope_cos, S.rope_sin,
+                              e.tkv, l, &e.st->talker_pos, 0, c.q_heads, scale,
+                              part, tick, B.attn, qtts::kTalkerSplits, nullptr};
+      QCK(qtts::launch_attn_decode(da, e.stream));
+      e.linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, 1,
+               c.hidden, S.q_out, qtts::EPI_RESID, nullptr);
+      e.linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
+               nullptr, 1, c.intermediate, c.hidden, qtts::EPI_SWIGLU, nullptr);
+      e.linear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.x, c.hidden, B.h1, c.hidden,
+               nullptr, 1, c.hidden, c.intermediate, qtts::EPI_RESID, nullptr);
+    }
+    qtts::SampleCfg greedy{0, 0, 1.f, 1.f};
+    e.talker_head(qtts::ROLE_TALKER_STEP, e.tb.x, greedy, 1.0f, nullptr, e.cp_prefix_target());
+    e.sync_state();
+    if (token_out) *token_out = e.st_host->semantic;
+    if (hidden_out) QCK(cudaMemcpy(hidden_out, e.cp_prefix_target(), H * 4, cudaMemcpyDeviceToHost));
+    if (logits_out)
+      QCK(cudaMemcpy(logits_out, e.logits, c.vocab * 4, cudaMemcpyDeviceToHost));
   });
 }
 

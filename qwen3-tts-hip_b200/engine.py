@@ -116,6 +116,7 @@ SIGNATURES = {
     "qtts_text_stream_destroy": (None, [_P]),
     "qtts_talker_prefill": (C.c_int32, [_P, _F, C.c_size_t, _F, _F, _I32]),
     "qtts_talker_decode_step": (C.c_int32, [_P, _F, C.c_size_t, _F, _F, _I32]),
+    "qtts_talker_decode_step_static": (C.c_int32, [_P, _F, C.c_size_t, _F, _F, _I32]),
     "qtts_code_predictor": (C.c_int32, [_P, _F, _F, C.POINTER(_Options), _I32, _F, _F]),
     "qtts_last_timings": (C.c_int32, [_P, _F, _F, _SZ]),
     "qtts_last_launch_count": (C.c_int32, [_P, _SZ]),
@@ -419,6 +420,17 @@ class HipTtsEngine:
         tok = C.c_int32()
         _check(lib().qtts_talker_decode_step(self._h, _fptr(x), int(offset), _fptr(hidden),
                                              _fptr(logits), C.byref(tok)))
+        return hidden, logits, tok.value
+
+    def talker_decode_step_static(self, step_input: np.ndarray, offset: int):
+        """talker_decode_step without any device allocation by the call: the
+        attention scratch lives in the library's static device array."""
+        x = np.ascontiguousarray(step_input, dtype=np.float32)
+        hidden = np.zeros(self.hidden, np.float32)
+        logits = np.zeros(self.info.vocab, np.float32)
+        tok = C.c_int32()
+        _check(lib().qtts_talker_decode_step_static(self._h, _fptr(x), int(offset), _fptr(hidden),
+                                                    _fptr(logits), C.byref(tok)))
         return hidden, logits, tok.value
 
     def code_predictor(self, talker_hidden, semantic_embed, options: Optional[GenerateOptions] = None):
