@@ -17,6 +17,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <deque>
@@ -27,6 +28,7 @@
 #include <string>
 #include <vector>
 
+#include "frame_kernel.h"
 #include "json.h"
 #include "kernels.h"
 #include "qtts_b200.h"
@@ -54,6 +56,7 @@ constexpr uint64_t kSeedXor = 0x9e3779b97f4a7c15ull;  // generation.rs:667
 constexpr int kNewline = 198;                          // text.rs:15
 constexpr int kTalkerPageShift = 5;                    // 32 positions per KV page
 constexpr int kTalkerSplits = 16;                      // decode attention splits
+constexpr int kFrameTalkerSplits = 4;                  // frame kernel talker attention splits
 
 // ---------------------------------------------------------------------------
 // safetensors (8-byte LE header length, JSON header, raw little-endian data)
@@ -296,6 +299,19 @@ class Engine {
   std::vector<int> pinned_ids_storage;
 
   std::map<SampleKey, cudaGraphExec_t> graphs;
+  // persistent frame kernel
+  std::map<SampleKey, std::pair<FrameOp*, int>> frame_ops;  // device op lists
+  int frame_grid = 0;
+  bool use_frame_kernel = true;
+  unsigned* frame_seq = nullptr;
+  int* frame_error = nullptr;
+  unsigned* frame_counters = nullptr;
+  long long* frame_trace = nullptr;  // QTTS_FRAME_TRACE=<file>: per-op clock64 trace
+  std::string frame_trace_path;
+  struct TagBufs {
+    TV *x, *qkv, *attn, *h1, *act;
+  } ct{}, tt{};
+  TV *logits_t = nullptr, *cp_cache_t = nullptr, *cp_dummy_t = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
   float last_prefill_ms = 0.f, last_frames_ms = 0.f;
   size_t last_frames = 0;
@@ -332,6 +348,11 @@ class Engine {
                    float* cp_prefix_dst);
   void cp_head(int group, const float* x, const SampleCfg& c, const int* halt);
   void enqueue_frame(const SampleKey& k);
+  void enqueue_frame_kernel(const SampleKey& k);
+  std::vector<FrameOp> build_frame_ops(const SampleKey& k);
+  bool frame_ops_fit(const std::vector<FrameOp>& ops) const;
+  void check_frame_error();
+  void dump_frame_trace(const SampleKey& k);
   cudaGraphExec_t frame_graph(const SampleKey& k);
 
   // ---- text prep ----
@@ -475,6 +496,7 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   if (dev < 0 || dev >= ndev) invalid("device " + std::to_string(dev) + " not present");
   QCK(cudaSetDevice(dev));
   QCK(configure_kernels());
+  QCK(configure_frame_kernel());
   QCK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   QCK(cudaEventCreate(&ev0));
   QCK(cudaEventCreate(&ev1));
@@ -587,6 +609,44 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   tp_a = arena.alloc<float>((size_t)tp_rows * text_hidden);
   tp_b = arena.alloc<float>((size_t)tp_rows * text_inter);
   tp_c = arena.alloc<float>((size_t)tp_rows * T.hidden);
+  {
+    // The persistent frame kernel is opt-in (QTTS_FRAME_KERNEL=1) until it
+    // beats the per-op graph; both paths are parity-tested.
+    const char* env = std::getenv("QTTS_FRAME_KERNEL");
+    use_frame_kernel = env && env[0] == '1';
+    frame_grid = frame_grid_size(dev);
+    if (const char* g = std::getenv("QTTS_FRAME_GRID"))  // profiling aid: fewer CTAs
+      frame_grid = std::min(frame_grid, std::atoi(g));
+    if (use_frame_kernel && frame_grid > 0) {
+      auto bufs = [&](const DevStack& S, int rows, int nsplit) {
+        TagBufs b;
+        const size_t Hh = S.c.hidden, I = S.c.intermediate;
+        b.x = arena.alloc<TV>(rows * Hh);
+        b.qkv = arena.alloc<TV>((size_t)rows * S.qkv_w);
+        b.attn = arena.alloc<TV>(nsplit > 1 ? (size_t)S.c.q_heads * nsplit * (2 + kHeadDim)
+                                            : (size_t)rows * S.q_out);
+        b.h1 = arena.alloc<TV>(rows * Hh);
+        b.act = arena.alloc<TV>(rows * I);
+        return b;
+      };
+      ct = bufs(cp, 2, 1);
+      tt = bufs(talker, 1, kFrameTalkerSplits);
+      logits_t = arena.alloc<TV>(std::max(T.vocab, C.vocab));
+      cp_cache_t = arena.alloc<TV>((size_t)C.layers * 2 * C.kv_heads * kFrameCpPositions * kHeadDim);
+      cp_dummy_t = arena.alloc<TV>(T.hidden);
+      frame_seq = arena.alloc<unsigned>(4);
+      const unsigned one = 1;
+      QCK(cudaMemcpy(frame_seq, &one, 4, cudaMemcpyHostToDevice));
+      frame_error = arena.alloc<int>(4);
+      frame_counters = arena.alloc<unsigned>(8 * 8192);
+      if (const char* tp = std::getenv("QTTS_FRAME_TRACE")) {
+        frame_trace_path = tp;
+        frame_trace = arena.alloc<long long>(8 * 8192);
+      }
+    } else {
+      use_frame_kernel = false;
+    }
+  }
   QCK(cudaDeviceSynchronize());
 }
 
@@ -720,14 +780,228 @@ void Engine::enqueue_frame(const SampleKey& k) {
   }
 }
 
+// Static op list of one frame for the persistent frame kernel (same order and
+// semantics as enqueue_frame). Each reader records which op last wrote its
+// input so it can wait for that op's tag.
+std::vector<FrameOp> Engine::build_frame_ops(const SampleKey& k) {
+  std::vector<FrameOp> ops;
+  const StackCfg& C = cfg.cp;
+  const StackCfg& T = cfg.talker;
+  const int H = T.hidden;
+  struct Src {
+    int src;
+    const float* ext;
+    const TV* tag;
+    int op;
+  };
+  auto gemv = [&](const __nv_bfloat16* W, Src x, int ldx, const float* gamma, float eps, TV* y,
+                  int ldy, Src r, int ldr, const float* bias, int M, int N, int K, int epi) {
+    FrameOp o{};
+    o.kind = FOP_GEMV;
+    o.epi = epi;
+    o.M = M; o.N = N; o.K = K;
+    o.x_src = x.src; o.x_ext = x.ext; o.x_tag = x.tag; o.x_op = x.op; o.ldx = ldx;
+    o.r_src = r.src; o.r_ext = r.ext; o.r_tag = r.tag; o.r_op = r.op; o.ldr = ldr;
+    o.W = W; o.gamma = gamma; o.eps = eps; o.bias = bias; o.y = y; o.ldy = ldy;
+    ops.push_back(o);
+    return (int)ops.size() - 1;
+  };
+  auto attn = [&](DevStack& S, const TagBufs& B, int qkv_op, int l, int kind, int pos, int nsplit) {
+    FrameOp o{};
+    o.kind = kind;
+    o.x_src = FSRC_TAG; o.x_tag = B.qkv; o.x_op = qkv_op;
+    o.y = B.attn;
+    o.q_gamma = S.q_g[l]; o.k_gamma = S.k_g[l]; o.eps = S.c.eps;
+    o.rope_cos = S.rope_cos; o.rope_sin = S.rope_sin;
+    o.kv = tkv; o.cp_cache = cp_cache_t; o.layer = l;
+    o.q_heads = S.c.q_heads; o.kv_heads = S.c.kv_heads;
+    o.pos_const = pos; o.nsplit = nsplit;
+    o.scale = 1.0f / std::sqrt((float)S.c.head_dim);
+    ops.push_back(o);
+    return (int)ops.size() - 1;
+  };
+  const Src none{FSRC_NONE, nullptr, nullptr, 0};
+  // one decoder layer; returns the index of the op that wrote B.x
+  auto layer = [&](DevStack& S, const TagBufs& B, int l, int M, Src x_in, Src r_in, int akind,
+                   int pos, int nsplit) {
+    const StackCfg& c = S.c;
+    const int q = gemv(S.wqkv[l], x_in, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, none, 0,
+                       nullptr, M, S.qkv_w, c.hidden, EPI_STORE);
+    const int a = attn(S, B, q, l, akind, pos, nsplit);
+    Src ain{nsplit > 1 ? FSRC_PARTIALS : FSRC_TAG, nullptr, B.attn, a};
+    const int o = gemv(S.wo[l], ain, S.q_out, nullptr, 0.f, B.h1, c.hidden, r_in, c.hidden,
+                       nullptr, M, c.hidden, S.q_out, EPI_RESID);
+    if (nsplit > 1) { ops[o].q_heads = c.q_heads; ops[o].nsplit = nsplit; }
+    const int g = gemv(S.wgu[l], Src{FSRC_TAG, nullptr, B.h1, o}, c.hidden, S.post_g[l], c.eps,
+                       B.act, c.intermediate, none, 0, nullptr, M, c.intermediate, c.hidden,
+                       EPI_SWIGLU);
+    return gemv(S.wdown[l], Src{FSRC_TAG, nullptr, B.act, g}, c.intermediate, nullptr, 0.f, B.x,
+                c.hidden, Src{FSRC_TAG, nullptr, B.h1, o}, c.hidden, nullptr, M, c.hidden,
+                c.intermediate, EPI_RESID);
+  };
+  auto add_head = [&](const __nv_bfloat16* W, Src x, const float* gamma, float eps, int V, int K,
+                      int role, const SampleCfg& sc, float penalty, int suppress, int group,
+                      const __nv_bfloat16* emb, TV* next_x) {
+    const int i = gemv(W, x, K, gamma, eps, logits_t, V, none, 0, nullptr, 1, V, K, EPI_STORE);
+    FrameOp& o = ops[i];
+    o.kind = FOP_HEAD;
+    o.role = role; o.cfg = sc; o.penalty = penalty; o.suppress = suppress;
+    o.group = group; o.last_group = C.groups - 2; o.emb = emb; o.next_x = next_x;
+    return i;
+  };
+  const bool proj = has_proj();
+  const int Hc = C.hidden;
+  // CodePredictor 2-row prefill (positions 0, 1)
+  Src first{FSRC_EXT, cb.x, nullptr, 0}, first_r = first;
+  int wx = -1;
+  if (proj) {
+    wx = gemv(proj_w, Src{FSRC_EXT, cp_prefix, nullptr, 0}, H, nullptr, 0.f, ct.x, Hc, none, 0,
+              proj_b, 2, Hc, H, EPI_BIAS);
+    first = first_r = Src{FSRC_TAG, nullptr, ct.x, wx};
+  }
+  for (int l = 0; l < C.layers; ++l) {
+    const Src xin = l == 0 ? first : Src{FSRC_TAG, nullptr, ct.x, wx};
+    const Src rin = l == 0 ? first_r : Src{FSRC_TAG, nullptr, ct.x, wx};
+    wx = layer(cp, ct, l, 2, xin, rin, FOP_ATTN_PAIR, 0, 1);
+  }
+  TV* cp_next = proj ? cp_dummy_t : ct.x;
+  int wh = add_head(cp_heads, Src{FSRC_TAG, nullptr, ct.x + Hc, wx}, cp_norm_g, C.eps, C.vocab,
+                    Hc, ROLE_CP_GROUP, k.s, 1.0f, 0, 0, cp_embs,
+                    C.groups - 2 == 0 ? tt.x : cp_next);
+  for (int g = 1; g < C.groups - 1; ++g) {
+    if (proj) {
+      wx = gemv(proj_w, Src{FSRC_LOCAL, nullptr, nullptr, 0}, H, nullptr, 0.f, ct.x, Hc, none, 0,
+                proj_b, 1, Hc, H, EPI_BIAS);
+      first = first_r = Src{FSRC_TAG, nullptr, ct.x, wx};
+    } else {
+      first = Src{FSRC_LOCAL, nullptr, nullptr, 0};
+      first_r = Src{FSRC_TAG, nullptr, ct.x, wh};
+    }
+    for (int l = 0; l < C.layers; ++l) {
+      const Src xin = l == 0 ? first : Src{FSRC_TAG, nullptr, ct.x, wx};
+      const Src rin = l == 0 ? first_r : Src{FSRC_TAG, nullptr, ct.x, wx};
+      wx = layer(cp, ct, l, 1, xin, rin, FOP_ATTN_DECODE, g + 1, 1);
+    }
+    wh = add_head(cp_heads + (size_t)g * C.vocab * Hc, Src{FSRC_TAG, nullptr, ct.x, wx},
+                  cp_norm_g, C.eps, C.vocab, Hc, ROLE_CP_GROUP, k.s, 1.0f, 0, g,
+                  cp_embs + (size_t)g * C.vocab * H, g == C.groups - 2 ? tt.x : cp_next);
+  }
+  if (!k.last) {
+    int wt = wh;  // the last CodePredictor head wrote the talker input slices
+    for (int l = 0; l < T.layers; ++l) {
+      const Src xin = l == 0 ? Src{FSRC_LOCAL, nullptr, nullptr, 0} : Src{FSRC_TAG, nullptr, tt.x, wt};
+      wt = layer(talker, tt, l, 1, xin, Src{FSRC_TAG, nullptr, tt.x, wt}, FOP_ATTN_DECODE, -1,
+                 kFrameTalkerSplits);
+    }
+    add_head(head, Src{FSRC_TAG, nullptr, tt.x, wt}, norm_g, T.eps, T.vocab, T.hidden,
+             ROLE_TALKER_STEP, k.t, k.penalty, 1, 0, codec_emb, nullptr);
+  }
+  for (FrameOp& o : ops)
+    o.writers = (o.kind == FOP_GEMV || o.kind == FOP_HEAD) ? frame_grid : o.q_heads * o.nsplit;
+  return ops;
+}
+
+// Per-CTA limits of the frame kernel (rows per CTA, shared-memory scratch).
+bool Engine::frame_ops_fit(const std::vector<FrameOp>& ops) const {
+  const int G = frame_grid;
+  if (G <= 0) return false;
+  for (const FrameOp& o : ops) {
+    if (o.kind == FOP_GEMV || o.kind == FOP_HEAD) {
+      const int rows = (o.N + G - 1) / G;
+      if (o.N < G || rows * o.M > 256 || o.K > 6144 || o.K % 256 != 0 || o.M > 2) return false;
+      const size_t floats = (size_t)o.M * o.K + (size_t)rows * (o.epi == EPI_SWIGLU ? 2 : 1) * 16;
+      if (floats * 4 > (size_t)kFrameScratchBytes) return false;
+      if (o.kind == FOP_HEAD && o.N > max_sample_vocab()) return false;
+      if (o.x_src == FSRC_PARTIALS && (o.nsplit > 4 || o.q_heads * o.nsplit > 128)) return false;
+    } else if (o.q_heads * o.nsplit > G) {
+      return false;
+    }
+  }
+  if (ops.size() > 8192) return false;
+  return cfg.talker.hidden <= kFrameMaxH && cfg.cp.groups <= kFrameCpPositions;
+}
+
+void Engine::enqueue_frame_kernel(const SampleKey& k) {
+  const auto& ol = frame_ops.at(k);
+  FrameParams p{};
+  p.ops = ol.first;
+  p.n_ops = ol.second;
+  p.st = st;
+  p.seq = frame_seq;
+  p.error = frame_error;
+  p.counters = frame_counters;
+  {
+    const char* env = std::getenv("QTTS_FRAME_COUNTERS");
+    p.use_counters = env ? std::atoi(env) : 1;
+  }
+  p.talker_codec_emb = codec_emb;
+  p.H = cfg.talker.hidden;
+  p.groups = cfg.cp.groups;
+  p.eos_token = cfg.codec_eos;
+  p.codes = codes;
+  p.history = history;
+  p.trailing = trailing;
+  p.tts_pad = tts_pad;
+  p.cp_prefix = cp_prefix_target();
+  p.trace = frame_trace;
+  p.trace_cta = 0;
+  p.trace_frame = 5;
+  QCK(launch_frame(p, frame_grid, stream));
+  launches += 1;
+}
+
+void Engine::check_frame_error() {
+  if (!use_frame_kernel) return;
+  int err[2] = {0, 0};
+  QCK(cudaMemcpy(err, frame_error, sizeof err, cudaMemcpyDeviceToHost));
+  if (err[0])
+    fail(QTTS_ERR_DEVICE_STATE, "frame kernel wait timed out (code " + std::to_string(err[0]) +
+                                    ", op " + std::to_string(err[1]) + ")");
+}
+
+void Engine::dump_frame_trace(const SampleKey& k) {
+  if (!frame_trace || !frame_ops.count(k)) return;
+  const auto& ol = frame_ops.at(k);
+  std::vector<long long> tr(8 * (size_t)ol.second + 128);
+  std::vector<FrameOp> ops(ol.second);
+  QCK(cudaMemcpy(tr.data(), frame_trace, tr.size() * 8, cudaMemcpyDeviceToHost));
+  QCK(cudaMemcpy(ops.data(), ol.first, ops.size() * sizeof(FrameOp), cudaMemcpyDeviceToHost));
+  if (FILE* f = std::fopen(frame_trace_path.c_str(), "w")) {
+    for (size_t i = 0; i < ops.size(); ++i)
+      std::fprintf(f, "%d %d %d %d %d %lld %lld %lld %lld %lld\n", ops[i].kind, ops[i].epi,
+                   ops[i].M, ops[i].N, ops[i].K, tr[8 * i], tr[8 * i + 1], tr[8 * i + 2],
+                   tr[8 * i + 3], tr[8 * i + 4] + 0 * tr[8 * i + 5]);
+    for (size_t i = 0; i < ops.size(); ++i)
+      std::fprintf(f, "#w %zu %lld %lld %lld\n", i, tr[8 * i + 5], tr[8 * i + 6], tr[8 * i + 7]);
+    for (int h = 0; h < 32; ++h) {
+      const long long* t = tr.data() + 8 * ops.size() + 4 * h;
+      if (t[0] && t[3] > t[0])
+        std::fprintf(f, "# head %d gemv->logits %lld select %lld actions %lld\n", h, t[1] - t[0],
+                     t[2] - t[1], t[3] - t[2]);
+    }
+    std::fclose(f);
+  }
+}
+
 cudaGraphExec_t Engine::frame_graph(const SampleKey& k) {
   auto it = graphs.find(k);
   if (it != graphs.end()) return it->second;
   cudaGraph_t g = nullptr;
   const size_t before = launches;
+  bool fk = use_frame_kernel;
+  if (fk && !frame_ops.count(k)) {
+    std::vector<FrameOp> ops = build_frame_ops(k);
+    if (frame_ops_fit(ops)) {
+      FrameOp* d = arena.alloc<FrameOp>(ops.size());
+      QCK(cudaMemcpy(d, ops.data(), ops.size() * sizeof(FrameOp), cudaMemcpyHostToDevice));
+      frame_ops[k] = {d, (int)ops.size()};
+    } else {
+      fk = use_frame_kernel = false;
+    }
+  }
   QCK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
   try {
-    enqueue_frame(k);
+    if (fk) enqueue_frame_kernel(k); else enqueue_frame(k);
   } catch (...) {
     cudaStreamEndCapture(stream, &g);
     if (g) cudaGraphDestroy(g);
@@ -900,6 +1174,8 @@ size_t Engine::run_frames(size_t n) {
   }
   QCK(cudaEventRecord(ev2, stream));
   sync_state();
+  check_frame_error();
+  if (gf) dump_frame_trace(full);
   float ms = 0.f;
   QCK(cudaEventElapsedTime(&ms, ev1, ev2));
   last_frames_ms += ms;

@@ -21,13 +21,14 @@
 #include <float.h>
 
 #include "kernels.h"
+#include "select.cuh"
 
 namespace qtts {
 namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxVocab = 4096;
+constexpr int kMaxVocab = kSelMaxVocab;
 constexpr int kXFloats = 12288;  // 48 KB fp32 activation tile per block
 
 __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
@@ -163,261 +164,6 @@ __global__ void __launch_bounds__(kThreads) k_linear(LinearArgs a) {
   linear_body<MT, RPW, EPI>(a, reinterpret_cast<float*>(dyn4), s_inv);
 }
 
-// ---------------------------------------------------------------------------
-// Block-wide helpers for token selection (kThreads threads).
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ unsigned order_key(float f) {
-  const unsigned u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// Exclusive prefix sum of one int per thread; returns the exclusive value and
-// writes the block total to *total.
-__device__ int block_excl_scan(int v, int* total) {
-  __shared__ int s_w[kWarps];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int inc = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int n = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += n;
-  }
-  __syncthreads();
-  if (lane == 31) s_w[warp] = inc;
-  __syncthreads();
-  int before = 0, all = 0;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    const int t = s_w[w];
-    if (w < warp) before += t;
-    all += t;
-  }
-  *total = all;
-  return before + inc - v;
-}
-
-__device__ float philox_u01(unsigned long long seed, unsigned long long ctr) {
-  unsigned c0 = (unsigned)ctr, c1 = (unsigned)(ctr >> 32), c2 = 0u, c3 = 0u;
-  unsigned k0 = (unsigned)seed, k1 = (unsigned)(seed >> 32);
-#pragma unroll
-  for (int i = 0; i < 10; ++i) {
-    const unsigned hi0 = __umulhi(0xD2511F53u, c0), lo0 = 0xD2511F53u * c0;
-    const unsigned hi1 = __umulhi(0xCD9E8D57u, c2), lo1 = 0xCD9E8D57u * c2;
-    const unsigned n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
-    c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
-    k0 += 0x9E3779B9u; k1 += 0xBB67AE85u;
-  }
-  return (float)(c0 >> 8) / 16777216.0f;
-}
-
-// One uniform in [0,1) with 24 bits; LCG mode reproduces the reference's
-// next_f32 (sampling.rs:120-126) in the reference's draw order.
-__device__ float rng_next(SeqState* st) {
-  if (st->rng_kind == RNG_LCG) {
-    st->rng_state = st->rng_state * 6364136223846793005ull + 1442695040888963407ull;
-    return (float)(unsigned)(st->rng_state >> 40) / 16777216.0f;
-  }
-  const float u = philox_u01(st->rng_seed, st->rng_counter);
-  st->rng_counter += 1ull;
-  return u;
-}
-
-struct SelectSmem {
-  float* val;   // [kMaxVocab] logits after penalty/suppression
-  int* tmp;     // [kMaxVocab] counts / candidate indices
-  float* cval;  // [kMaxVocab] candidate values
-  int* sidx;    // [kMaxVocab] sorted candidate indices
-};
-
-// Selects a token from smem logits `sv.val[0..V)` following the reference:
-// greedy -> argmax (lowest index on ties); top_k in (0,256] with top_p ~ 1 ->
-// device top-k sampler (non-finite as -FLT_MAX, u * sum walk); otherwise the
-// CPU sampler semantics (finite only, top-k, top-p renormalised, u walk).
-__device__ int block_select(const SelectSmem& s, int V, const SampleCfg& cfg, SeqState* st) {
-  __shared__ int s_res;
-  __shared__ unsigned s_hist[256];
-  __shared__ unsigned s_prefix;
-  __shared__ int s_rem;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-
-  if (!cfg.do_sample) {
-    float bv = -FLT_MAX;
-    int bi = 0;
-    for (int v = tid; v < V; v += kThreads) {
-      const float x = s.val[v];
-      if (x > bv) { bv = x; bi = v; }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    __shared__ float s_bv[kWarps];
-    __shared__ int s_bi[kWarps];
-    if (lane == 0) { s_bv[warp] = bv; s_bi[warp] = bi; }
-    __syncthreads();
-    if (tid == 0) {
-      float b = s_bv[0];
-      int i0 = s_bi[0];
-      for (int w = 1; w < kWarps; ++w)
-        if (s_bv[w] > b || (s_bv[w] == b && s_bi[w] < i0)) { b = s_bv[w]; i0 = s_bi[w]; }
-      s_res = i0;
-    }
-    __syncthreads();
-    return s_res;
-  }
-
-  const bool device_path = cfg.top_k > 0 && cfg.top_k <= 256 && cfg.top_p >= 0.999999f;
-  // eligibility: device path keeps every entry (non-finite -> -FLT_MAX);
-  // CPU path keeps finite entries only.
-  int nfin = 0;
-  for (int v = tid; v < V; v += kThreads) {
-    float x = s.val[v];
-    const bool fin = isfinite(x);
-    if (device_path && !fin) s.val[v] = -FLT_MAX;
-    nfin += fin ? 1 : 0;
-  }
-  int n_elig_total;
-  block_excl_scan(nfin, &n_elig_total);
-  if (device_path) n_elig_total = V;
-  if (n_elig_total == 0) {
-    if (tid == 0) st->error = 1;
-    __syncthreads();
-    return 0;
-  }
-  const int K = device_path ? min(cfg.top_k, V)
-                            : ((cfg.top_k > 0 && cfg.top_k < n_elig_total) ? cfg.top_k
-                                                                           : n_elig_total);
-
-  // Radix select (8-bit digits, MSB first) of the K-th largest key.
-  if (tid == 0) { s_prefix = 0u; s_rem = K; }
-  unsigned mask = 0u;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    s_hist[tid] = 0u;
-    __syncthreads();
-    const unsigned prefix = s_prefix;
-    for (int v = tid; v < V; v += kThreads) {
-      const float x = s.val[v];
-      if (!device_path && !isfinite(x)) continue;
-      const unsigned key = order_key(x);
-      if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
-    }
-    __syncthreads();
-    const int digit = 255 - tid;  // descending digit order
-    const int cnt = (int)s_hist[digit];
-    int tot;
-    const int before = block_excl_scan(cnt, &tot);
-    const int rem = s_rem;
-    __syncthreads();
-    if (before < rem && rem <= before + cnt) {
-      s_prefix = prefix | ((unsigned)digit << shift);
-      s_rem = rem - before;
-    }
-    mask |= 255u << shift;
-    __syncthreads();
-  }
-  const unsigned thr = s_prefix;
-  const int take_eq = s_rem;
-
-  // Index-ordered compaction of candidates: keys above thr, then the lowest
-  // `take_eq` indices equal to thr.
-  const int per = (V + kThreads - 1) / kThreads;
-  const int lo = tid * per, hi = min(V, lo + per);
-  int gt = 0, eq = 0;
-  for (int v = lo; v < hi; ++v) {
-    const float x = s.val[v];
-    if (!device_path && !isfinite(x)) continue;
-    const unsigned key = order_key(x);
-    gt += key > thr;
-    eq += key == thr;
-  }
-  int tot;
-  const int eq_before = block_excl_scan(eq, &tot);
-  const int eq_take = max(0, min(eq, take_eq - eq_before));
-  const int out_before = block_excl_scan(gt + eq_take, &tot);
-  {
-    int o = out_before, e = 0;
-    for (int v = lo; v < hi; ++v) {
-      const float x = s.val[v];
-      if (!device_path && !isfinite(x)) continue;
-      const unsigned key = order_key(x);
-      bool take = key > thr;
-      if (key == thr) { take = e < eq_take; ++e; }
-      if (take) { s.cval[o] = x; s.tmp[o] = v; ++o; }
-    }
-  }
-  __syncthreads();
-  // Rank sort: value descending, index ascending.
-  for (int i = tid; i < K; i += kThreads) {
-    const float vi = s.cval[i];
-    const int ii = s.tmp[i];
-    int rank = 0;
-    for (int j = 0; j < K; ++j) {
-      const float vj = s.cval[j];
-      const int ij = s.tmp[j];
-      rank += (vj > vi) || (vj == vi && ij < ii);
-    }
-    s.val[rank] = vi;
-    s.sidx[rank] = ii;
-  }
-  __syncthreads();
-
-  if (tid == 0) {
-    float* prob = s.cval;
-    const float mx = s.val[0];
-    const float temp = cfg.temperature;
-    float sum = 0.f;
-    for (int i = 0; i < K; ++i) {
-      const float p = expf((s.val[i] - mx) / temp);
-      prob[i] = p;
-      sum += p;
-    }
-    int tok;
-    if (device_path) {
-      const float u = rng_next(st);  // drawn before the kernel in the reference
-      if (!isfinite(sum) || sum <= 0.f) {
-        tok = s.sidx[0];
-      } else {
-        float target = u * sum;
-        tok = s.sidx[K - 1];
-        for (int i = 0; i < K; ++i) {
-          if (target <= prob[i]) { tok = s.sidx[i]; break; }
-          target -= prob[i];
-        }
-      }
-    } else if (!isfinite(sum) || sum <= 0.f) {
-      tok = s.sidx[0];  // no draw (sampling.rs:79-81)
-    } else {
-      int keep = K;
-      for (int i = 0; i < K; ++i) prob[i] /= sum;
-      if (cfg.top_p < 1.0f) {
-        float cum = 0.f;
-        keep = 0;
-        for (int i = 0; i < K; ++i) {
-          ++keep;
-          cum += prob[i];
-          if (cum >= cfg.top_p) break;
-        }
-        keep = max(keep, 1);
-        float ks = 0.f;
-        for (int i = 0; i < keep; ++i) ks += prob[i];
-        if (ks > 0.f)
-          for (int i = 0; i < keep; ++i) prob[i] /= ks;
-      }
-      float target = rng_next(st);
-      tok = s.sidx[keep - 1];
-      for (int i = 0; i < keep; ++i) {
-        if (target <= prob[i]) { tok = s.sidx[i]; break; }
-        target -= prob[i];
-      }
-    }
-    s_res = tok;
-  }
-  __syncthreads();
-  return s_res;
-}
-
 // Head: final/group RMSNorm + LM head GEMV over all CTAs; the last CTA to
 // finish applies penalty/suppression, selects the token and performs the
 // gathers the next stage needs (so no logits or tokens visit the host).
@@ -438,32 +184,21 @@ __global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
   if (a.role == ROLE_LOGITS_ONLY) return;
 
   const int V = a.lin.N;
-  SelectSmem s{smem, reinterpret_cast<int*>(smem + kMaxVocab), smem + 2 * kMaxVocab,
-               reinterpret_cast<int*>(smem + 3 * kMaxVocab)};
+  Selector<SyncBlock> sel{smem, reinterpret_cast<int*>(smem + kSelMaxVocab)};
   const int tid = threadIdx.x;
-  for (int v = tid; v < V; v += kThreads) s.val[v] = __ldcg(a.lin.y + v);
+  for (int v = tid; v < V; v += kThreads) sel.val[v] = __ldcg(a.lin.y + v);
   if (tid == 0) { s_frame = a.st->frames; s_sem = a.st->semantic; }
   __syncthreads();
-  if (a.role == ROLE_TALKER_STEP && a.penalty != 1.0f) {
-    for (int v = tid; v < V; v += kThreads) s.tmp[v] = 0;
-    __syncthreads();
-    for (int i = tid; i < s_frame; i += kThreads) {
-      const int t = a.history[i];
-      if (t >= 0 && t < V) atomicAdd(&s.tmp[t], 1);
-    }
-    __syncthreads();
-    for (int v = tid; v < V; v += kThreads) {
-      float x = s.val[v];
-      for (int c = s.tmp[v]; c > 0; --c) x = x < 0.f ? x * a.penalty : x / a.penalty;
-      s.val[v] = x;
-    }
+  if (a.role == ROLE_TALKER_STEP)
+    sel.penalise(V, a.history, s_frame, -1, a.penalty, a.suppress, a.eos_token);
+  else
+    sel.penalise(V, a.history, 0, -1, 1.0f, a.suppress, a.eos_token);
+  Rng rng{a.st->rng_kind, a.st->rng_state, a.st->rng_seed, a.st->rng_counter};
+  const int tok = sel.select(V, a.cfg, rng, &a.st->error);
+  if (tid == 0) {
+    a.st->rng_state = rng.state;
+    a.st->rng_counter = rng.counter;
   }
-  if (a.suppress) {
-    for (int v = max(0, V - 1024) + tid; v < V; v += kThreads)
-      if (v != a.eos_token) s.val[v] = -__int_as_float(0x7f800000);
-  }
-  __syncthreads();
-  const int tok = block_select(s, V, a.cfg, a.st);
   if (a.token_out && tid == 0) *a.token_out = tok;
 
   const int H = a.H;
@@ -772,7 +507,7 @@ cudaError_t launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
 }
 
 constexpr size_t kLinearSmem = sizeof(float) * (size_t)kXFloats;
-constexpr size_t kHeadSmem = sizeof(float) * 4 * (size_t)kMaxVocab;  // >= kLinearSmem
+constexpr size_t kHeadSmem = sizeof(float) * (size_t)kXFloats;  // >= 2 * kMaxVocab words
 
 template <int MT, int RPW, int EPI>
 cudaError_t configure_linear_t() {

@@ -337,3 +337,45 @@ def test_full_size_0p6b(pkg, tmp_path_factory):
     codes, _, recs = m.rollout(pre, tr, pad, 4, GREEDY, GREEDY, forced_codes=out.codes)
     assert_tokens_match(out.codes, codes, gaps_per_code(recs))
     e.close()
+
+
+def test_frame_kernel_path_parity(model_dirs, tmp_path):
+    """The opt-in persistent frame kernel (QTTS_FRAME_KERNEL=1) against the
+    oracle, run in a child process so the engine picks up the setting."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    code = f"""
+import sys, numpy as np
+sys.path.insert(0, {str(root)!r})
+import __graft_entry__ as G
+from oracle import qtts_oracle as O
+pkg = G.load_package()
+for shape, d in [('tiny', {str(model_dirs['tiny'])!r}), ('tiny_proj', {str(model_dirs['tiny_proj'])!r})]:
+    e = pkg.HipTtsEngine.load_with_options(d, pkg.EngineOptions(0, 128))
+    m = O.OracleModel(d, 128)
+    ids = np.random.default_rng(3).integers(0, 4000, 10)
+    g = O.SamplingConfig(False, 0, 1.0, 1.0)
+    opts = pkg.GenerateOptions(decode_audio=False, do_sample=False, subtalker_dosample=False,
+                               repetition_penalty=1.0, max_frames=12)
+    out = e.generate_codes_from_ids(ids, opts)
+    pre, tr, pad = m.prepare(list(ids))
+    codes, _, recs = m.rollout(pre, tr, pad, 12, g, g, forced_codes=out.codes)
+    gaps = [x for r in recs for x in [r.talker_gap] + r.cp_gaps]
+    bad = [i for i, (a, b) in enumerate(zip(out.codes, codes)) if a != b and gaps[i] > 1e-2]
+    assert out.frames == 12 and not bad, (shape, bad)
+    s = pkg.GenerateOptions(decode_audio=False, max_frames=12, seed=4)
+    out2 = e.generate_codes_from_ids(ids, s)
+    sc = O.SamplingConfig(True, 50, 1.0, 0.9)
+    codes2, _, _ = m.rollout(pre, tr, pad, 12, sc, sc, penalty=1.05, seed=4, forced_codes=out2.codes)
+    agree = np.mean(np.asarray(out2.codes) == np.asarray(codes2[: len(out2.codes)]))
+    assert agree >= 0.98, (shape, agree)
+print("frame kernel ok")
+"""
+    env = dict(os.environ, QTTS_FRAME_KERNEL="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0 and "frame kernel ok" in r.stdout, r.stdout + r.stderr
