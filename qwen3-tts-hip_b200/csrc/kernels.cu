@@ -164,16 +164,125 @@ __global__ void __launch_bounds__(kThreads) k_linear(LinearArgs a) {
   linear_body<MT, RPW, EPI>(a, reinterpret_cast<float*>(dyn4), s_inv);
 }
 
+
+// ---------------------------------------------------------------------------
+// Decode GEMV (one activation row). Every lane owns KCH 16-byte chunks of
+// each of its NR weight rows and loads all of them into registers before the
+// programmatic-dependent-launch wait: weights never depend on the previous
+// kernel, so their HBM latency overlaps the producer's tail. After the wait
+// the CTA stages gamma * x once in shared memory (the RMSNorm sum of squares
+// comes from the same pass) and every warp reads it from there.
+// SWIGLU: the warp's two rows are gate row c and up row N + c.
+// `xs` holds KCH * 256 floats + 32 words of reduction scratch.
+// ---------------------------------------------------------------------------
+template <int KCH, int NR>
+__device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* xs,
+                                           float* inv_out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool swiglu = epi == EPI_SWIGLU;
+  const int outs = swiglu ? 1 : NR;
+  const int c0 = (blockIdx.x * kWarps + warp) * outs;
+  constexpr int K = KCH * 256;
+  uint4 w[NR][KCH];
+  bool valid[NR];
+#pragma unroll
+  for (int r = 0; r < NR; ++r) {
+    const int c = swiglu ? c0 : c0 + r;
+    valid[r] = c < a.N;
+    const long long row = swiglu ? (r == 0 ? c0 : a.N + c0) : c;
+    const __nv_bfloat16* src = a.W + (valid[r] ? row : 0) * (long long)K + lane * 8;
+#pragma unroll
+    for (int j = 0; j < KCH; ++j) w[r][j] = ldg_stream(src + j * 256);
+  }
+  pdl_trigger();
+  pdl_wait();
+  if (a.halt && *a.halt) return false;
+  float* red = xs + K;
+  float ss = 0.f;
+  for (int k = threadIdx.x * 4; k < K; k += kThreads * 4) {
+    float4 v = __ldcg(reinterpret_cast<const float4*>(a.x + k));
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    if (a.gamma) {
+      const float4 g = __ldg(reinterpret_cast<const float4*>(a.gamma + k));
+      v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+    }
+    *reinterpret_cast<float4*>(xs + k) = v;
+  }
+  if (a.gamma) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+  }
+  __syncthreads();
+  float sc = 1.0f;
+  if (a.gamma) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) t += red[i];
+    sc = rsqrtf(t / (float)K + a.eps);
+  }
+  if (inv_out && threadIdx.x == 0) *inv_out = sc;
+  float acc[NR];
+#pragma unroll
+  for (int r = 0; r < NR; ++r) acc[r] = 0.f;
+#pragma unroll
+  for (int j = 0; j < KCH; ++j) {
+    const int k = j * 256 + lane * 8;
+    const float4 x0 = *reinterpret_cast<const float4*>(xs + k);
+    const float4 x1 = *reinterpret_cast<const float4*>(xs + k + 4);
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      float f[8];
+      unpack8(w[r][j], f);
+      float t = acc[r];
+      t = fmaf(f[0], x0.x, t); t = fmaf(f[1], x0.y, t);
+      t = fmaf(f[2], x0.z, t); t = fmaf(f[3], x0.w, t);
+      t = fmaf(f[4], x1.x, t); t = fmaf(f[5], x1.y, t);
+      t = fmaf(f[6], x1.z, t); t = fmaf(f[7], x1.w, t);
+      acc[r] = t;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < NR; ++r) acc[r] = warp_sum(acc[r]);
+  if (lane == 0) {
+    if (swiglu) {
+      if (valid[0]) {
+        const float g = acc[0] * sc, u = acc[NR - 1] * sc;
+        a.y[c0] = g / (1.0f + expf(-g)) * u;
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        if (!valid[r]) continue;
+        const int c = c0 + r;
+        float out = acc[r] * sc;
+        if (epi == EPI_RESID) out += __ldcg(a.resid + c);
+        if (epi == EPI_BIAS) out += a.bias[c];
+        if (epi == EPI_BIAS_SILU) out = silu(out + a.bias[c]);
+        a.y[c] = out;
+      }
+    }
+  }
+  return true;
+}
+
+template <int KCH, int NR>
+__global__ void __launch_bounds__(kThreads) k_gemv1(LinearArgs a, int epi) {
+  __shared__ __align__(16) float xs[KCH * 256 + 32];
+  gemv1_body<KCH, NR>(a, epi, xs, nullptr);
+}
+
 // Head: final/group RMSNorm + LM head GEMV over all CTAs; the last CTA to
 // finish applies penalty/suppression, selects the token and performs the
 // gathers the next stage needs (so no logits or tokens visit the host).
+template <int KCH>
 __global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
   extern __shared__ float4 dyn4[];
   float* smem = reinterpret_cast<float*>(dyn4);
   __shared__ float s_inv[1];
   __shared__ bool s_last;
   __shared__ int s_frame, s_sem;
-  if (!linear_body<1, 1, EPI_STORE>(a.lin, smem, s_inv)) return;
+  if (!gemv1_body<KCH, 1>(a.lin, EPI_STORE, smem, s_inv)) return;
+  __syncthreads();  // the selector reuses the staged activation buffer
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
@@ -507,7 +616,7 @@ cudaError_t launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
 }
 
 constexpr size_t kLinearSmem = sizeof(float) * (size_t)kXFloats;
-constexpr size_t kHeadSmem = sizeof(float) * (size_t)kXFloats;  // >= 2 * kMaxVocab words
+constexpr size_t kHeadSmem = sizeof(float) * 2 * (size_t)kMaxVocab;  // selector scratch
 
 template <int MT, int RPW, int EPI>
 cudaError_t configure_linear_t() {
@@ -542,9 +651,43 @@ cudaError_t launch_linear_mt(const LinearArgs& a, cudaStream_t stream) {
   return launch_linear_t<MT, 1, EPI>(a, stream);
 }
 
+template <int KCH, int NR>
+cudaError_t launch_gemv1_t(const LinearArgs& a, int epi, cudaStream_t stream) {
+  const int per_block = kWarps * (epi == EPI_SWIGLU ? 1 : NR);
+  dim3 grid((a.N + per_block - 1) / per_block);
+  return launch(k_gemv1<KCH, NR>, grid, dim3(kThreads), 0, stream, a, epi);
+}
+
+template <int KCH>
+cudaError_t launch_gemv1_k(const LinearArgs& a, int epi, cudaStream_t stream) {
+  if (epi == EPI_SWIGLU) return launch_gemv1_t<KCH, 2>(a, epi, stream);
+  // two output rows per warp while that still gives >= 256 CTAs (and K is short)
+  if (KCH <= 4 && (a.N + 2 * kWarps - 1) / (2 * kWarps) >= 256)
+    return launch_gemv1_t<KCH, 2>(a, epi, stream);
+  return launch_gemv1_t<KCH, 1>(a, epi, stream);
+}
+
+// Decode GEMV dispatch on K (chunks of 256 per lane); false when K is unsupported.
+bool launch_gemv1(const LinearArgs& a, int epi, cudaStream_t stream, cudaError_t* err) {
+  if (a.M != 1 || a.K % 256 != 0) return false;
+  switch (a.K / 256) {
+    case 1: *err = launch_gemv1_k<1>(a, epi, stream); return true;
+    case 2: *err = launch_gemv1_k<2>(a, epi, stream); return true;
+    case 4: *err = launch_gemv1_k<4>(a, epi, stream); return true;
+    case 8: *err = launch_gemv1_k<8>(a, epi, stream); return true;
+    case 12: *err = launch_gemv1_k<12>(a, epi, stream); return true;
+    case 24: *err = launch_gemv1_k<24>(a, epi, stream); return true;
+  }
+  return false;
+}
+
 template <int EPI>
 cudaError_t launch_linear_epi(const LinearArgs& a, cudaStream_t stream) {
-  if (a.M == 1) return launch_linear_mt<1, EPI>(a, stream);
+  if (a.M == 1) {
+    cudaError_t e;
+    if (launch_gemv1(a, EPI, stream, &e)) return e;
+    return launch_linear_mt<1, EPI>(a, stream);
+  }
   if (a.M == 2) return launch_linear_mt<2, EPI>(a, stream);
   return launch_linear_mt<8, EPI>(a, stream);
 }
@@ -566,9 +709,15 @@ cudaError_t launch_linear(const LinearArgs& a, Epilogue epi, cudaStream_t stream
 }
 
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t stream) {
-  if (a.lin.N > kMaxVocab || a.lin.M != 1 || a.lin.K % 8 != 0) return cudaErrorInvalidValue;
+  if (a.lin.N > kMaxVocab || a.lin.M != 1 || a.lin.K % 256 != 0) return cudaErrorInvalidValue;
   dim3 grid((a.lin.N + kWarps - 1) / kWarps);
-  return launch(k_head, grid, dim3(kThreads), kHeadSmem, stream, a);
+  switch (a.lin.K / 256) {
+    case 1: return launch(k_head<1>, grid, dim3(kThreads), kHeadSmem, stream, a);
+    case 2: return launch(k_head<2>, grid, dim3(kThreads), kHeadSmem, stream, a);
+    case 4: return launch(k_head<4>, grid, dim3(kThreads), kHeadSmem, stream, a);
+    case 8: return launch(k_head<8>, grid, dim3(kThreads), kHeadSmem, stream, a);
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t configure_kernels() {
@@ -578,7 +727,10 @@ cudaError_t configure_kernels() {
   if ((e = configure_linear_epi<EPI_SWIGLU>()) != cudaSuccess) return e;
   if ((e = configure_linear_epi<EPI_BIAS>()) != cudaSuccess) return e;
   if ((e = configure_linear_epi<EPI_BIAS_SILU>()) != cudaSuccess) return e;
-  return cudaFuncSetAttribute(k_head, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem);
+  if ((e = cudaFuncSetAttribute(k_head<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(k_head<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(k_head<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem)) != cudaSuccess) return e;
+  return cudaFuncSetAttribute(k_head<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem);
 }
 
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
