@@ -353,107 +353,158 @@ __global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Decode attention: one CTA per (kv head, split). Prologue fuses QK-RMSNorm,
-// RoPE and the bf16 KV append of the current position; the last CTA of each
-// kv head merges the split partials (flash-decode combine).
+// Decode attention: one CTA per kv head, NW warps. The prologue (threads
+// < 128) fuses QK-RMSNorm, RoPE and the bf16 KV append of the current
+// position. Warp w then owns positions w*8.., (w+NW)*8.., in batches of 8:
+// the next batch's K/V rows are loaded while the current batch is scored, the
+// 8*G dot products are reduced together, and the online softmax is updated
+// once per batch. Warps merge their (max, sum, acc) in shared memory.
 // ---------------------------------------------------------------------------
-template <int G>
-__global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
+constexpr int kAttnBatch = 8;
+
+template <int G, int NW>
+__global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
   __shared__ float sq[G][kHeadDim];
   __shared__ float sk[kHeadDim], sv[kHeadDim];
   __shared__ float red[4][G + 1];
-  __shared__ float wm[4][G], wl[4][G];
-  __shared__ float wacc[4][G][kHeadDim];
-  __shared__ bool s_last;
+  __shared__ float wm[NW][G], wl[NW][G];
+  __shared__ float wacc[NW][G][kHeadDim];
   pdl_wait();
   if (a.halt && *a.halt) return;
-  const int h = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
+  const int h = blockIdx.x, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int pos = a.pos_ptr ? *a.pos_ptr : a.pos_const;
   const int T = pos + 1;
   const int kvh = a.kv.kv_heads;
   const int q_out = a.q_heads * kHeadDim, kv_out = kvh * kHeadDim;
 
-  float qr[G];
+  float qr[G], kr = 0.f, vr = 0.f;
+  if (tid < kHeadDim) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) qr[g] = a.qkv[(h * G + g) * kHeadDim + tid];
-  const float kr = a.qkv[q_out + h * kHeadDim + tid];
-  const float vr = a.qkv[q_out + kv_out + h * kHeadDim + tid];
+    for (int g = 0; g < G; ++g) qr[g] = a.qkv[(h * G + g) * kHeadDim + tid];
+    kr = a.qkv[q_out + h * kHeadDim + tid];
+    vr = a.qkv[q_out + kv_out + h * kHeadDim + tid];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const float t = warp_sum(qr[g] * qr[g]);
-    if (lane == 0) red[warp][g] = t;
-  }
-  {
+    for (int g = 0; g < G; ++g) {
+      const float t = warp_sum(qr[g] * qr[g]);
+      if (lane == 0) red[warp][g] = t;
+    }
     const float t = warp_sum(kr * kr);
     if (lane == 0) red[warp][G] = t;
   }
   __syncthreads();
+  if (tid < kHeadDim) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const float ss = red[0][g] + red[1][g] + red[2][g] + red[3][g];
-    sq[g][tid] = qr[g] * rsqrtf(ss / (float)kHeadDim + a.eps) * a.q_gamma[tid];
-  }
-  {
+    for (int g = 0; g < G; ++g) {
+      const float ss = red[0][g] + red[1][g] + red[2][g] + red[3][g];
+      sq[g][tid] = qr[g] * rsqrtf(ss / (float)kHeadDim + a.eps) * a.q_gamma[tid];
+    }
     const float ss = red[0][G] + red[1][G] + red[2][G] + red[3][G];
     sk[tid] = kr * rsqrtf(ss / (float)kHeadDim + a.eps) * a.k_gamma[tid];
   }
   __syncthreads();
-  const int pi = tid & 63;
-  const float c = a.rope_cos[pos * 64 + pi], sn = a.rope_sin[pos * 64 + pi];
-  float rq[G];
+  float rq[G], kroped = 0.f;
+  if (tid < kHeadDim) {
+    const int pi = tid & 63;
+    const float c = a.rope_cos[pos * 64 + pi], sn = a.rope_sin[pos * 64 + pi];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const float x0 = sq[g][pi], x1 = sq[g][pi + 64];
-    rq[g] = tid < 64 ? x0 * c - x1 * sn : x1 * c + x0 * sn;
+    for (int g = 0; g < G; ++g) {
+      const float x0 = sq[g][pi], x1 = sq[g][pi + 64];
+      rq[g] = tid < 64 ? x0 * c - x1 * sn : x1 * c + x0 * sn;
+    }
+    const float k0 = sk[pi], k1 = sk[pi + 64];
+    kroped = tid < 64 ? k0 * c - k1 * sn : k1 * c + k0 * sn;
   }
-  const float k0 = sk[pi], k1 = sk[pi + 64];
-  const float kroped = tid < 64 ? k0 * c - k1 * sn : k1 * c + k0 * sn;
   __syncthreads();
-  const __nv_bfloat16 kb = __float2bfloat16_rn(kroped);
-  const __nv_bfloat16 vb = __float2bfloat16_rn(vr);
+  if (tid < kHeadDim) {
+    const __nv_bfloat16 kb = __float2bfloat16_rn(kroped);
+    const __nv_bfloat16 vb = __float2bfloat16_rn(vr);
 #pragma unroll
-  for (int g = 0; g < G; ++g) sq[g][tid] = rq[g];
-  sk[tid] = __bfloat162float(kb);
-  sv[tid] = __bfloat162float(vb);
-  if (s == 0) {
+    for (int g = 0; g < G; ++g) sq[g][tid] = rq[g];
+    sk[tid] = __bfloat162float(kb);
+    sv[tid] = __bfloat162float(vb);
     kv_ptr(a.kv, a.layer, 0, h, pos)[tid] = kb;
     kv_ptr(a.kv, a.layer, 1, h, pos)[tid] = vb;
   }
   __syncthreads();
 
-  const int chunk = (T + a.nsplit - 1) / a.nsplit;
-  const int start = s * chunk, end = min(T, start + chunk);
   float q[G][4], m[G], l[G], acc[G][4];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) { q[g][j] = sq[g][4 * lane + j]; acc[g][j] = 0.f; }
+    for (int j = 0; j < 4; ++j) { q[g][j] = sq[g][4 * lane + j] * a.scale; acc[g][j] = 0.f; }
   }
-  for (int p = start + warp; p < end; p += 4) {
-    float kf[4], vf[4];
-    if (p == pos) {
+  // Rows before `pos` come from the cache; the current row from shared memory.
+  auto load = [&](int p0, uint2 (&ku)[kAttnBatch], uint2 (&vu)[kAttnBatch]) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) { kf[j] = sk[4 * lane + j]; vf[j] = sv[4 * lane + j]; }
-    } else {
-      const uint2 ku = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 0, h, p) + 4 * lane);
-      const uint2 vu = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 1, h, p) + 4 * lane);
-      kf[0] = bf16lo(ku.x); kf[1] = bf16hi(ku.x); kf[2] = bf16lo(ku.y); kf[3] = bf16hi(ku.y);
-      vf[0] = bf16lo(vu.x); vf[1] = bf16hi(vu.x); vf[2] = bf16lo(vu.y); vf[3] = bf16hi(vu.y);
+    for (int i = 0; i < kAttnBatch; ++i) {
+      const int p = p0 + i;
+      if (p < pos) {
+        ku[i] = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 0, h, p) + 4 * lane);
+        vu[i] = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 1, h, p) + 4 * lane);
+      } else {
+        ku[i] = make_uint2(0u, 0u);
+        vu[i] = make_uint2(0u, 0u);
+      }
     }
+  };
+  uint2 ku[kAttnBatch], vu[kAttnBatch], nk[kAttnBatch], nv[kAttnBatch];
+  int p0 = warp * kAttnBatch;
+  if (p0 < T) load(p0, ku, vu);
+  for (; p0 < T; p0 += NW * kAttnBatch) {
+    const int pn = p0 + NW * kAttnBatch;
+    if (pn < T) load(pn, nk, nv);
+    float kf[kAttnBatch][4], vf[kAttnBatch][4];
+#pragma unroll
+    for (int i = 0; i < kAttnBatch; ++i) {
+      if (p0 + i == pos) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { kf[i][j] = sk[4 * lane + j]; vf[i][j] = sv[4 * lane + j]; }
+      } else {
+        kf[i][0] = bf16lo(ku[i].x); kf[i][1] = bf16hi(ku[i].x);
+        kf[i][2] = bf16lo(ku[i].y); kf[i][3] = bf16hi(ku[i].y);
+        vf[i][0] = bf16lo(vu[i].x); vf[i][1] = bf16hi(vu[i].x);
+        vf[i][2] = bf16lo(vu[i].y); vf[i][3] = bf16hi(vu[i].y);
+      }
+    }
+    float d[G][kAttnBatch];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int i = 0; i < kAttnBatch; ++i)
+        d[g][i] = q[g][0] * kf[i][0] + q[g][1] * kf[i][1] + q[g][2] * kf[i][2] + q[g][3] * kf[i][3];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < kAttnBatch; ++i) d[g][i] += __shfl_xor_sync(0xffffffffu, d[g][i], o);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float d = q[g][0] * kf[0] + q[g][1] * kf[1] + q[g][2] * kf[2] + q[g][3] * kf[3];
-      d = warp_sum(d) * a.scale;
-      const float mn = fmaxf(m[g], d);
-      const float corr = expf(m[g] - mn), pe = expf(d - mn);
-      l[g] = l[g] * corr + pe;
+      float mb = m[g];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[g][j] = acc[g][j] * corr + pe * vf[j];
-      m[g] = mn;
+      for (int i = 0; i < kAttnBatch; ++i) {
+        if (p0 + i >= T) d[g][i] = -INFINITY;
+        mb = fmaxf(mb, d[g][i]);
+      }
+      const float corr = expf(m[g] - mb);  // m = -inf on the first batch: corr = 0
+      float ls = 0.f, av[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < kAttnBatch; ++i) {
+        const float pe = expf(d[g][i] - mb);
+        ls += pe;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) av[j] = fmaf(pe, vf[i][j], av[j]);
+      }
+      l[g] = l[g] * corr + ls;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[g][j] = acc[g][j] * corr + av[j];
+      m[g] = mb;
     }
+#pragma unroll
+    for (int i = 0; i < kAttnBatch; ++i) { ku[i] = nk[i]; vu[i] = nv[i]; }
   }
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -462,45 +513,20 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
     if (lane == 0) { wm[warp][g] = m[g]; wl[warp][g] = l[g]; }
   }
   __syncthreads();
-  const int stride = 2 + kHeadDim;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int t = tid; t < G * kHeadDim; t += NW * 32) {
+    const int g = t / kHeadDim, dd = t % kHeadDim;
     float M = -INFINITY;
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][g]);
-    float L = 0.f, A = 0.f;
-    if (M != -INFINITY) {
-      for (int w = 0; w < 4; ++w) {
-        if (wm[w][g] == -INFINITY) continue;
-        const float f = expf(wm[w][g] - M);
-        L += wl[w][g] * f;
-        A += wacc[w][g][tid] * f;
-      }
-    }
-    float* part = a.partial + ((long long)(h * G + g) * a.nsplit + s) * stride;
-    if (tid == 0) { part[0] = M; part[1] = L; }
-    part[2 + tid] = A;
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&a.tickets[h], 1u) == (unsigned)a.nsplit - 1u;
-  __syncthreads();
-  if (!s_last) return;
-  if (tid == 0) a.tickets[h] = 0u;
-  __threadfence();
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const float* base = a.partial + (long long)(h * G + g) * a.nsplit * stride;
-    float M = -INFINITY;
-    for (int t = 0; t < a.nsplit; ++t) M = fmaxf(M, __ldcg(base + t * stride));
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
     float L = 0.f, A = 0.f;
-    for (int t = 0; t < a.nsplit; ++t) {
-      const float mt = __ldcg(base + t * stride);
-      if (mt == -INFINITY) continue;
-      const float f = expf(mt - M);
-      L += __ldcg(base + t * stride + 1) * f;
-      A += __ldcg(base + t * stride + 2 + tid) * f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      if (wm[w][g] == -INFINITY) continue;
+      const float f = expf(wm[w][g] - M);
+      L += wl[w][g] * f;
+      A += wacc[w][g][dd] * f;
     }
-    a.out[(h * G + g) * kHeadDim + tid] = A / L;
+    a.out[(h * G + g) * kHeadDim + dd] = A / L;
   }
 }
 
@@ -735,12 +761,20 @@ cudaError_t configure_kernels() {
 
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   const int G = a.q_heads / a.kv.kv_heads;
-  dim3 grid(a.kv.kv_heads, a.nsplit);
+  // Fixed positions (CodePredictor, <= 17 rows): 4 warps; a position read on
+  // the device (talker): 16 warps (8 with four q heads per kv head).
+  const bool small = !a.pos_ptr && a.pos_const < 4 * 4 * kAttnBatch;
+  dim3 grid(a.kv.kv_heads);
+#define QTTS_ATTN(GG)                                                                    \
+  return small ? launch(k_attn_decode<GG, 4>, grid, dim3(128), 0, stream, a)             \
+               : launch(k_attn_decode<GG, (GG > 2 ? 8 : 16)>, grid,              \
+                        dim3(32 * (GG > 2 ? 8 : 16)), 0, stream, a)
   switch (G) {
-    case 1: return launch(k_attn_decode<1>, grid, dim3(128), 0, stream, a);
-    case 2: return launch(k_attn_decode<2>, grid, dim3(128), 0, stream, a);
-    case 4: return launch(k_attn_decode<4>, grid, dim3(128), 0, stream, a);
+    case 1: QTTS_ATTN(1);
+    case 2: QTTS_ATTN(2);
+    case 4: QTTS_ATTN(4);
   }
+#undef QTTS_ATTN
   return cudaErrorInvalidValue;
 }
 
