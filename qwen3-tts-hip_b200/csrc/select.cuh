@@ -129,11 +129,14 @@ struct Selector {
   // Only thread 0 draws from `rng`.
   __device__ __forceinline__ int select(int V, const SampleCfg& cfg, Rng& rng, int* error) {
     __shared__ int s_res;
-    __shared__ unsigned s_hist[256];
     __shared__ unsigned s_prefix;
     __shared__ int s_rem;
-    __shared__ float cval[kSelSmallK], sval[kSelSmallK], prob[kSelSmallK];
-    __shared__ int cidx[kSelSmallK], sidx[kSelSmallK];
+    __shared__ unsigned s_above, s_lower;
+    __shared__ int s_done, s_cnt, s_ties, s_wcnt[kSelThreads / 32];
+    __shared__ __align__(16) unsigned long long cand[kSelSmallK];
+    __shared__ float sval[kSelSmallK];
+    __shared__ __align__(16) float prob[kSelSmallK];
+    __shared__ int sidx[kSelSmallK];
     __shared__ float s_bv[8];
     __shared__ int s_bi[8];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -166,16 +169,30 @@ struct Selector {
 
     const bool device_path = cfg.top_k > 0 && cfg.top_k <= 256 && cfg.top_p >= 0.999999f;
     stamp(0);
+    // Keys of this thread's entries (v = j * 256 + tid) stay in registers;
+    // 0 marks an ineligible entry (no finite float maps to 0). The device
+    // path maps non-finite logits to -FLT_MAX, in `val` too.
+    constexpr int kPer = kSelMaxVocab / kSelThreads;
+    unsigned key[kPer];
     int nfin = 0;
-    for (int v = tid; v < V; v += kSelThreads) {
-      const float x = val[v];
-      const bool fin = isfinite(x);
-      if (device_path && !fin) val[v] = -FLT_MAX;
-      nfin += fin ? 1 : 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int v = j * kSelThreads + tid;
+      unsigned k = 0u;
+      if (v < V) {
+        const float x = val[v];
+        if (isfinite(x)) {
+          k = order_key(x);
+          ++nfin;
+        } else if (device_path) {
+          val[v] = -FLT_MAX;
+          k = order_key(-FLT_MAX);
+        }
+      }
+      key[j] = k;
     }
-    int n_elig;
-    scan_excl(nfin, &n_elig);
-    if (device_path) n_elig = V;
+    int n_elig = V;
+    if (!device_path) scan_excl(nfin, &n_elig);
     if (n_elig == 0) {
       if (tid == 0) *error = 1;
       Sync::sync();
@@ -186,84 +203,135 @@ struct Selector {
     const float* sv;
     const int* si;
     if (K <= kSelSmallK) {
-      // Radix select (8-bit digits, MSB first) of the K-th largest key, with
-      // warp-aggregated histogram updates (many keys share the top digits).
+      // Radix select over 8-bit digits, MSB first, that stops as soon as the
+      // keys at or above the current bucket fit the candidate buffer; those
+      // candidates are compacted and ranked exactly (value desc, index asc).
       stamp(1);
-      if (tid == 0) { s_prefix = 0u; s_rem = K; }
+      if (tid == 0) { s_prefix = 0u; s_rem = K; s_lower = 0u; s_done = 0; s_above = 0u; s_ties = 0; }
+      // Stop once at most `stop` keys are at or above the bucket: ranking is
+      // quadratic in the candidate count.
+      const int stop = min(kSelSmallK, max(2 * K, 64));
+      unsigned* whist = reinterpret_cast<unsigned*>(aux) + warp * 256;  // per-warp bins
       unsigned mask = 0u;
       for (int shift = 24; shift >= 0; shift -= 8) {
-        s_hist[tid] = 0u;
-        Sync::sync();
+        for (int i = lane; i < 256; i += 32) whist[i] = 0u;
+        __syncwarp();
         const unsigned prefix = s_prefix;
-        for (int v0 = 0; v0 < V; v0 += kSelThreads) {
-          const int v = v0 + tid;
-          int bin = -1;
-          if (v < V) {
-            const float x = val[v];
-            if (device_path || isfinite(x)) {
-              const unsigned key = order_key(x);
-              if ((key & mask) == prefix) bin = (int)((key >> shift) & 255u);
-            }
-          }
-          const unsigned peers = __match_any_sync(0xffffffffu, bin);
-          if (bin >= 0 && (__ffs(peers) - 1) == lane) atomicAdd(&s_hist[bin], __popc(peers));
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+          if (j * kSelThreads >= V) break;
+          const unsigned k = key[j];
+          const int bin = (k != 0u && (k & mask) == prefix) ? (int)((k >> shift) & 255u) : -1;
+          if (bin >= 0) atomicAdd(&whist[bin], 1u);  // (__match_any_sync costs ~200 cycles here)
         }
         Sync::sync();
         const int digit = 255 - tid;
-        const int cnt = (int)s_hist[digit];
+        int cnt = 0;
+#pragma unroll
+        for (int w = 0; w < kSelThreads / 32; ++w) cnt += (int)aux[w * 256 + digit];
         int tot;
         const int before = scan_excl(cnt, &tot);
         const int rem = s_rem;
+        const int above = (int)s_above;
         Sync::sync();
         if (before < rem && rem <= before + cnt) {
-          s_prefix = prefix | ((unsigned)digit << shift);
+          const unsigned p = prefix | ((unsigned)digit << shift);
+          s_prefix = p;
           s_rem = rem - before;
+          // keys >= p (bits below `shift` zero) = everything above this bucket plus it
+          if (above + before + cnt <= stop || shift == 0) {
+            s_lower = p;
+            s_done = 1;
+            s_ties = above + before + cnt > kSelSmallK;  // many equal keys at the threshold
+          }
+          s_above = above + before;
         }
         mask |= 255u << shift;
         Sync::sync();
+        if (s_done) break;
       }
       stamp(2);
-      const unsigned thr = s_prefix;
-      const int take_eq = s_rem;
-      const int per = (V + kSelThreads - 1) / kSelThreads;
-      const int lo = tid * per, hi = min(V, lo + per);
-      int gt = 0, eq = 0;
-      for (int v = lo; v < hi; ++v) {
-        const float x = val[v];
-        if (!device_path && !isfinite(x)) continue;
-        const unsigned key = order_key(x);
-        gt += key > thr;
-        eq += key == thr;
+      const unsigned lower = s_lower;
+      const bool ties = s_ties;
+      // Compaction from the register keys: per-warp ballots give each warp's
+      // count, a prefix over warps gives its first slot (no atomics).
+      auto take = [&](unsigned k) { return k != 0u && (ties ? k > lower : k >= lower); };
+      int wc = 0;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        if (j * kSelThreads >= V) break;
+        wc += __popc(__ballot_sync(0xffffffffu, take(key[j])));
       }
-      int tot;
-      const int eq_before = scan_excl(eq, &tot);
-      const int eq_take = max(0, min(eq, take_eq - eq_before));
-      int o = scan_excl(gt + eq_take, &tot);
-      for (int v = lo, e = 0; v < hi; ++v) {
-        const float x = val[v];
-        if (!device_path && !isfinite(x)) continue;
-        const unsigned key = order_key(x);
-        bool take = key > thr;
-        if (key == thr) { take = e < eq_take; ++e; }
-        if (take) { cval[o] = x; cidx[o] = v; ++o; }
-      }
+      stamp(8);
+      if (lane == 0) s_wcnt[warp] = wc;
       Sync::sync();
-      stamp(3);
-      if (tid < K) {
-        const float vi = cval[tid];
-        const int ii = cidx[tid];
-        int rank = 0;
-        for (int j = 0; j < K; ++j) {
-          const float vj = cval[j];
-          rank += (vj > vi) || (vj == vi && cidx[j] < ii);
+      stamp(9);
+      constexpr int nw = kSelThreads / 32;
+      int base = 0, total = 0;
+#pragma unroll
+      for (int w = 0; w < nw; ++w) {
+        const int c = s_wcnt[w];
+        base += w < warp ? c : 0;
+        total += c;
+      }
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        if (j * kSelThreads >= V) break;
+        const bool t = take(key[j]);
+        const unsigned bal = __ballot_sync(0xffffffffu, t);
+        if (t)
+          cand[base + __popc(bal & ((1u << lane) - 1u))] =
+              ((unsigned long long)key[j] << 32) |
+              (unsigned)(0xffffffffu - (unsigned)(j * kSelThreads + tid));
+        base += __popc(bal);
+      }
+      stamp(10);
+      if (tid == 0) s_cnt = total;
+      Sync::sync();
+      if (ties) {
+        // Keys equal to the threshold, lowest indices first, until K are held.
+        const int greater = s_cnt;
+        const int per = (V + kSelThreads - 1) / kSelThreads;
+        const int lo = tid * per, hi = min(V, lo + per);
+        int eq = 0;
+        for (int v = lo; v < hi; ++v) {
+          const float x = val[v];
+          if ((device_path || isfinite(x)) && order_key(x) == lower) ++eq;
         }
-        sval[rank] = vi;
-        sidx[rank] = ii;
+        int tot;
+        int o = scan_excl(eq, &tot);
+        for (int v = lo; v < hi && greater + o < K; ++v) {
+          const float x = val[v];
+          if ((device_path || isfinite(x)) && order_key(x) == lower)
+            cand[greater + o++] = ((unsigned long long)lower << 32) | (0xffffffffu - (unsigned)v);
+        }
+        Sync::sync();
+        if (tid == 0) s_cnt = min(greater + tot, K);
+        Sync::sync();
+      }
+      stamp(3);
+      const int C = s_cnt;
+      if (tid < C) {
+        const unsigned long long me = cand[tid];
+        int rank = 0;
+        int j = 0;
+        for (; j + 4 <= C; j += 4) {
+          const ulonglong2 p0 = *reinterpret_cast<const ulonglong2*>(cand + j);
+          const ulonglong2 p1 = *reinterpret_cast<const ulonglong2*>(cand + j + 2);
+          rank += (p0.x > me) + (p0.y > me) + (p1.x > me) + (p1.y > me);
+        }
+        for (; j < C; ++j) rank += cand[j] > me;
+        if (rank < K) {
+          const int idx = (int)(0xffffffffu - (unsigned)me);
+          sval[rank] = val[idx];
+          sidx[rank] = idx;
+        }
       }
       Sync::sync();
       // exponentials in parallel; the sum stays sequential (thread 0)
       stamp(4);
       if (tid < K) prob[tid] = expf((sval[tid] - sval[0]) / cfg.temperature);
+      else if (tid < ((K + 3) & ~3)) prob[tid] = 0.f;  // pads the float4 reads below
       Sync::sync();
       stamp(5);
       sv = sval;
@@ -302,7 +370,39 @@ struct Selector {
       si = aux;
     }
 
-    if (tid == 0) {
+    if (device_path && tid == 0) {
+      // Sequential sum and inverse-CDF walk in rank order, 4 entries per load
+      // (adding the zero padding leaves the sum unchanged).
+      const float4* p4 = reinterpret_cast<const float4*>(prob);
+      const int K4 = (K + 3) >> 2;
+      const float u = rng.next();  // drawn before the kernel in the reference
+      float sum = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < K4; ++c) {
+        const float4 q = p4[c];
+        sum += q.x; sum += q.y; sum += q.z; sum += q.w;
+      }
+      int pick = 0;
+      if (isfinite(sum) && sum > 0.f) {
+        float target = u * sum;
+        pick = K - 1;
+        for (int c = 0; c < K4; ++c) {
+          const float4 q = p4[c];
+          const float pv[4] = {q.x, q.y, q.z, q.w};
+          bool found = false;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int i = 4 * c + j;
+            if (!found && i < K) {
+              if (target <= pv[j]) { pick = i; found = true; }
+              else target -= pv[j];
+            }
+          }
+          if (found) break;
+        }
+      }
+      s_res = si[pick];
+    } else if (tid == 0) {
       const float mx = sv[0];
       const float temp = cfg.temperature;
       auto p_at = [&](int i) { return K <= kSelSmallK ? prob[i] : expf((sv[i] - mx) / temp); };
