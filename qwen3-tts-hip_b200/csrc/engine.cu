@@ -303,6 +303,8 @@ class Engine {
   std::map<SampleKey, std::pair<FrameOp*, int>> frame_ops;  // device op lists
   int frame_grid = 0;
   bool use_frame_kernel = true;
+  // CodePredictor attention inside the O projection (QTTS_FUSE_ATTN_O=0: separate kernels)
+  bool fuse_attn_o = true;
   unsigned* frame_seq = nullptr;
   int* frame_error = nullptr;
   unsigned* frame_counters = nullptr;
@@ -337,8 +339,68 @@ class Engine {
               float* y, int ldy, const float* resid, int ldr, const float* bias, int M, int N,
               int K, Epilogue epi, const int* halt) {
     LinearArgs a{W, x, ldx, gamma, eps, y, ldy, resid, ldr, bias, M, N, K, halt};
+    static const char* kEpi[] = {"gemv", "gemv+resid", "gemv+swiglu", "gemv+bias", "gemv+bias+silu"};
+    a.trace_id = trace_tag(kEpi[epi], N, K);
+    a.trigger = trigger_mode;
+    plan_prefetch(a, (size_t)(epi == EPI_SWIGLU ? 2 : 1) * N * K * sizeof(__nv_bfloat16));
     QCK(launch_linear(a, epi, stream));
     ++launches;
+  }
+
+  // ---- L2 prefetch plan ----
+  // A frame graph is captured twice: the first capture records every weight
+  // matrix in launch order (a cyclic byte stream, since frames repeat); the
+  // second gives each op the stream range pf_ahead bytes past its own
+  // weights, of the same length, to prefetch into L2 before its dependency
+  // wait. HBM then streams weights ahead of the chain of dependent launches.
+  // ---- step trace (QTTS_STEP_TRACE=<file>) ----
+  // Frame `trace_frame` of each run records, per launch, the first CTA entry,
+  // the first CTA past its dependency wait and the last CTA exit.
+  std::string step_trace_path;
+  unsigned long long* step_trace = nullptr;
+  static constexpr int kTraceCap = 4096;
+  bool trace_capture = false;
+  std::vector<std::string> trace_names;
+  size_t trace_frame = 6;
+  int trace_tag(const char* kind, int N, int K) {
+    if (!trace_capture || pf_mode == 1 || (int)trace_names.size() + 1 >= kTraceCap) return 0;
+    trace_names.push_back(std::string(kind) + " N=" + std::to_string(N) + " K=" + std::to_string(K));
+    return (int)trace_names.size();
+  }
+  void dump_step_trace();
+
+  // Decode GEMVs launch their dependents after the dependency wait (1):
+  // measured faster than at entry (0), which floods the memory queues with
+  // weight loads of several launches at once. QTTS_TRIGGER overrides.
+  int trigger_mode = 1;
+  size_t pf_ahead = 0;                          // QTTS_L2_PREFETCH=<MB> enables
+  int pf_mode = 0;                              // 0 off, 1 record, 2 apply
+  std::vector<std::pair<const char*, size_t>> pf_ops;
+  size_t pf_next = 0;
+  void plan_prefetch(LinearArgs& a, size_t bytes) {
+    if (pf_mode == 1) {
+      pf_ops.push_back({reinterpret_cast<const char*>(a.W), bytes});
+    } else if (pf_mode == 2 && pf_next < pf_ops.size()) {
+      size_t total = 0, own = 0;
+      for (size_t i = 0; i < pf_ops.size(); ++i) {
+        if (i == pf_next) own = total;
+        total += pf_ops[i].second;
+      }
+      size_t want = pf_ops[pf_next].second;
+      size_t at = (own + std::min(pf_ahead, total - want)) % total;
+      int piece = 0;
+      while (want > 0 && piece < 3) {
+        size_t base = 0, i = 0;
+        while (base + pf_ops[i].second <= at) base += pf_ops[i++].second;
+        const size_t take = std::min(want, base + pf_ops[i].second - at);
+        a.pf_ptr[piece] = pf_ops[i].first + (at - base);
+        a.pf_bytes[piece] = (unsigned)take;
+        ++piece;
+        want -= take;
+        at = (at + take) % total;
+      }
+      ++pf_next;
+    }
   }
   void stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int pos0, const int* halt);
   void stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* pos_ptr, int pos_const,
@@ -614,6 +676,15 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
     // beats the per-op graph; both paths are parity-tested.
     const char* env = std::getenv("QTTS_FRAME_KERNEL");
     use_frame_kernel = env && env[0] == '1';
+    if (const char* tp = std::getenv("QTTS_STEP_TRACE")) {
+      step_trace_path = tp;
+      step_trace = arena.alloc<unsigned long long>(6 * (size_t)kTraceCap);
+    }
+    if (const char* tg = std::getenv("QTTS_TRIGGER")) trigger_mode = std::atoi(tg);
+    if (const char* pa = std::getenv("QTTS_L2_PREFETCH"))
+      pf_ahead = (size_t)std::max(0, std::atoi(pa)) << 20;
+    const char* fz = std::getenv("QTTS_FUSE_ATTN_O");
+    fuse_attn_o = !(fz && fz[0] == '0');
     frame_grid = frame_grid_size(dev);
     if (const char* g = std::getenv("QTTS_FRAME_GRID"))  // profiling aid: fewer CTAs
       frame_grid = std::min(frame_grid, std::atoi(g));
@@ -695,10 +766,21 @@ void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* 
     AttnDecodeArgs da{B.qkv,   S.q_g[l],  S.k_g[l], c.eps,   S.rope_cos, S.rope_sin,
                       kv,      l,         pos_ptr,  pos_const, c.q_heads, scale,
                       partial, tickets + 8, B.attn, nsplit,  halt};
-    QCK(launch_attn_decode(da, stream));
-    ++launches;
-    linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, 1,
-           c.hidden, S.q_out, EPI_RESID, halt);
+    LinearArgs o{S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden,
+                 nullptr, 1, c.hidden, S.q_out, halt};
+    if (fuse_attn_o && attn_o_fusable(da, o)) {
+      o.trace_id = trace_tag("attn+o+resid", c.hidden, S.q_out);
+      o.trigger = trigger_mode;
+      plan_prefetch(o, (size_t)c.hidden * S.q_out * sizeof(__nv_bfloat16));
+      QCK(launch_attn_o(da, o, stream));  // attention inside the O projection's staging
+      ++launches;
+    } else {
+      da.trace_id = trace_tag("attn", c.q_heads, nsplit);
+      QCK(launch_attn_decode(da, stream));
+      ++launches;
+      linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, 1,
+             c.hidden, S.q_out, EPI_RESID, halt);
+    }
     linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
            nullptr, 1, c.intermediate, c.hidden, EPI_SWIGLU, halt);
     linear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.x, c.hidden, B.h1, c.hidden,
@@ -734,6 +816,9 @@ void Engine::talker_head(int role, const float* x, const SampleCfg& c, float pen
   a.suppress = 1;
   a.cp_prefix = cp_prefix_dst;
   a.token_out = token;
+  a.lin.trace_id = trace_tag("talker head+select", T.vocab, T.hidden);
+  a.lin.trigger = trigger_mode;
+  plan_prefetch(a.lin, (size_t)T.vocab * T.hidden * sizeof(__nv_bfloat16));
   QCK(launch_head(a, stream));
   ++launches;
 }
@@ -752,6 +837,9 @@ void Engine::cp_head(int group, const float* x, const SampleCfg& c, const int* h
   a.step_in = tb.x;
   a.trailing = trailing;
   a.tts_pad = tts_pad;
+  a.lin.trace_id = trace_tag("cp head+select", C.vocab, C.hidden);
+  a.lin.trigger = trigger_mode;
+  plan_prefetch(a.lin, (size_t)C.vocab * C.hidden * sizeof(__nv_bfloat16));
   QCK(launch_head(a, stream));
   ++launches;
 }
@@ -999,16 +1087,32 @@ cudaGraphExec_t Engine::frame_graph(const SampleKey& k) {
       fk = use_frame_kernel = false;
     }
   }
-  QCK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
-  try {
-    if (fk) enqueue_frame_kernel(k); else enqueue_frame(k);
-  } catch (...) {
-    cudaStreamEndCapture(stream, &g);
-    if (g) cudaGraphDestroy(g);
+  const bool pf = !fk && pf_ahead > 0;
+  trace_capture = step_trace != nullptr && !fk && !k.last;
+  if (trace_capture) trace_names.clear();
+  for (int pass = pf ? 1 : 2; pass <= 2; ++pass) {
+    pf_mode = pf ? pass : 0;
+    if (pass == 1) pf_ops.clear();
+    pf_next = 0;
     launches = before;
-    throw;
+    QCK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      if (fk) enqueue_frame_kernel(k); else enqueue_frame(k);
+    } catch (...) {
+      cudaStreamEndCapture(stream, &g);
+      if (g) cudaGraphDestroy(g);
+      launches = before;
+      pf_mode = 0;
+      throw;
+    }
+    QCK(cudaStreamEndCapture(stream, &g));
+    if (pass == 1) {
+      cudaGraphDestroy(g);
+      g = nullptr;
+    }
   }
-  QCK(cudaStreamEndCapture(stream, &g));
+  pf_mode = 0;
+  trace_capture = false;
   graph_nodes[k] = launches - before;
   launches = before;
   cudaGraphExec_t exec = nullptr;
@@ -1167,15 +1271,28 @@ size_t Engine::run_frames(size_t n) {
   for (size_t i = 0; i < n; ++i)
     if (begin + i + 1 < seq_max_frames) gf = frame_graph(full); else gl = frame_graph(last);
   QCK(cudaEventRecord(ev1, stream));
+  bool traced = false;
   for (size_t i = 0; i < n; ++i) {
     const bool is_last = begin + i + 1 >= seq_max_frames;
+    const bool trace_now = step_trace && !is_last && begin + i == trace_frame;
+    if (trace_now) {
+      QCK(cudaMemsetAsync(step_trace, 0xff, 2 * kTraceCap * sizeof(unsigned long long), stream));
+      QCK(cudaMemsetAsync(step_trace + 2 * kTraceCap, 0,
+                          4 * kTraceCap * sizeof(unsigned long long), stream));
+      QCK(set_step_trace(step_trace, kTraceCap, stream));
+    }
     QCK(cudaGraphLaunch(is_last ? gl : gf, stream));
+    if (trace_now) {
+      QCK(set_step_trace(nullptr, 0, stream));
+      traced = true;
+    }
     last_launches += graph_nodes[is_last ? last : full];
   }
   QCK(cudaEventRecord(ev2, stream));
   sync_state();
   check_frame_error();
   if (gf) dump_frame_trace(full);
+  if (traced) dump_step_trace();
   float ms = 0.f;
   QCK(cudaEventElapsedTime(&ms, ev1, ev2));
   last_frames_ms += ms;
@@ -1186,6 +1303,24 @@ size_t Engine::run_frames(size_t n) {
   seq_semantic = st_host->semantic;
   if (st_host->halt) seq_ended = true;
   return produced;
+}
+
+void Engine::dump_step_trace() {
+  std::vector<unsigned long long> t(6 * (size_t)kTraceCap);
+  QCK(cudaMemcpy(t.data(), step_trace, t.size() * sizeof(unsigned long long),
+                 cudaMemcpyDeviceToHost));
+  FILE* f = std::fopen(step_trace_path.c_str(), "w");
+  if (!f) return;
+  std::fprintf(f, "# id entry wait exit last_wait sel_start sel_end name (ns after the first entry)\n");
+  unsigned long long t0 = ~0ull;
+  for (size_t i = 1; i <= trace_names.size(); ++i) t0 = std::min(t0, t[i]);
+  for (size_t i = 1; i <= trace_names.size(); ++i) {
+    auto rel = [&](unsigned long long v) { return v == ~0ull || v == 0 ? -1LL : (long long)(v - t0); };
+    std::fprintf(f, "%zu %lld %lld %lld %lld %lld %lld %s\n", i, rel(t[i]), rel(t[kTraceCap + i]),
+                 rel(t[2 * kTraceCap + i]), rel(t[3 * kTraceCap + i]), rel(t[4 * kTraceCap + i]),
+                 rel(t[5 * kTraceCap + i]), trace_names[i - 1].c_str());
+  }
+  std::fclose(f);
 }
 
 void Engine::read_codes(size_t from, size_t to, int32_t* out) {

@@ -34,6 +34,53 @@ constexpr int kXFloats = 12288;  // 48 KB fp32 activation tile per block
 __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 
 // ---------------------------------------------------------------------------
+// Step trace (profiling aid): per launch, the first CTA entry, the first CTA
+// past the dependency wait and the last CTA exit, in globaltimer ns; slot 3
+// is the last CTA past the wait, slots 4/5 the head's selection start/end.
+// ---------------------------------------------------------------------------
+struct StepTrace {
+  unsigned long long* buf;
+  int cap;
+};
+__device__ StepTrace g_trace;
+
+__device__ __forceinline__ void trace_mark(int id, int slot) {
+  if (id <= 0 || threadIdx.x != 0) return;
+  const StepTrace t = g_trace;
+  if (!t.buf || id >= t.cap) return;
+  unsigned long long now;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+  if (slot == 1) atomicMax(t.buf + 3 * t.cap + id, now);  // last CTA past the wait
+  if (slot >= 2) atomicMax(t.buf + slot * t.cap + id, now);
+  else atomicMin(t.buf + slot * t.cap + id, now);
+}
+
+// This CTA's share of the op's L2 prefetch ranges (warp 0, 4 KB per bulk
+// prefetch; fire-and-forget, so it never delays the kernel).
+__device__ __forceinline__ void l2_prefetch_share(const LinearArgs& a, int cta, int ncta) {
+  const unsigned tot = a.pf_bytes[0] + a.pf_bytes[1] + a.pf_bytes[2];
+  if (tot == 0u || threadIdx.x >= 32) return;
+  const unsigned chunk = ((tot + ncta - 1) / ncta + 15u) & ~15u;
+  const unsigned b = (unsigned)cta * chunk;
+  const unsigned e = min(tot, b + chunk);
+  for (unsigned o = b + threadIdx.x * 4096u; o < e; o += 32u * 4096u) {
+    unsigned n = min(4096u, e - o), at = o, base = 0;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const unsigned len = a.pf_bytes[i];
+      if (n && at < base + len) {
+        const unsigned take = min(n, base + len - at);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+                     :: "l"(a.pf_ptr[i] + (at - base)), "r"(take) : "memory");
+        at += take;
+        n -= take;
+      }
+      base += len;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Projection body: for the block's M-tile and RPW output columns per warp,
 //   acc = W[row] . (gamma * x[m])   then  y = epilogue(inv_rms[m] * acc)
 // The RMSNorm scale is a per-row scalar, so it is applied after the dot
@@ -47,6 +94,8 @@ __device__ __forceinline__ bool linear_body(const LinearArgs& a, float* sx, floa
   const int col0 = (blockIdx.x * kWarps + warp) * RPW;
   const int m0 = blockIdx.y * MT;
   const int K = a.K;
+  trace_mark(a.trace_id, 0);
+  if (blockIdx.y == 0) l2_prefetch_share(a, blockIdx.x, gridDim.x);
 
   const __nv_bfloat16* wr[NR];
   bool valid[RPW];
@@ -69,6 +118,7 @@ __device__ __forceinline__ bool linear_body(const LinearArgs& a, float* sx, floa
     asm volatile("prefetch.global.L2 [%0];" ::"l"(wr[r] + lane * 8));
 
   pdl_wait();
+  trace_mark(a.trace_id, 1);
   if (a.halt && *a.halt) return false;
   const int mcount = min(MT, a.M - m0);
 
@@ -154,6 +204,7 @@ __device__ __forceinline__ bool linear_body(const LinearArgs& a, float* sx, floa
       if (lane == 0) a.y[(long long)(m0 + m) * a.ldy + c] = out;
     }
   }
+  trace_mark(a.trace_id, 2);
   return true;
 }
 
@@ -175,16 +226,20 @@ __global__ void __launch_bounds__(kThreads) k_linear(LinearArgs a) {
 // SWIGLU: the warp's two rows are gate row c and up row N + c.
 // `xs` holds KCH * 256 floats + 32 words of reduction scratch.
 // ---------------------------------------------------------------------------
-template <int KCH, int NR>
+__device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, float* xs, int halted);
+
+template <int KCH, int NR, bool ATTN = false>
 __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* xs,
-                                           float* inv_out) {
+                                           float* inv_out, const AttnDecodeArgs* at = nullptr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool swiglu = epi == EPI_SWIGLU;
   const int outs = swiglu ? 1 : NR;
   const int c0 = (blockIdx.x * kWarps + warp) * outs;
   constexpr int K = KCH * 256;
+  trace_mark(a.trace_id, 0);
   uint4 w[NR][KCH];
   bool valid[NR];
+  const unsigned long long pol = l2_evict_first_policy();
 #pragma unroll
   for (int r = 0; r < NR; ++r) {
     const int c = swiglu ? c0 : c0 + r;
@@ -192,13 +247,20 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
     const long long row = swiglu ? (r == 0 ? c0 : a.N + c0) : c;
     const __nv_bfloat16* src = a.W + (valid[r] ? row : 0) * (long long)K + lane * 8;
 #pragma unroll
-    for (int j = 0; j < KCH; ++j) w[r][j] = ldg_stream(src + j * 256);
+    for (int j = 0; j < KCH; ++j) w[r][j] = ldg_stream(src + j * 256, pol);
   }
-  pdl_trigger();
+  l2_prefetch_share(a, blockIdx.x, gridDim.x);
+  if (a.trigger == 0) pdl_trigger();
   pdl_wait();
-  if (a.halt && *a.halt) return false;
+  trace_mark(a.trace_id, 1);
+  if (a.trigger == 1) pdl_trigger();
+  // The halt flag is loaded alongside the input (not before it) and only
+  // checked before the first write.
+  const int halted = a.halt ? __ldcg(a.halt) : 0;
   float* red = xs + K;
   float ss = 0.f;
+  if (ATTN) stage_cp_attention(*at, xs, halted);
+  else
   for (int k = threadIdx.x * 4; k < K; k += kThreads * 4) {
     float4 v = __ldcg(reinterpret_cast<const float4*>(a.x + k));
     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
@@ -208,19 +270,22 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
     }
     *reinterpret_cast<float4*>(xs + k) = v;
   }
-  if (a.gamma) {
+  if (!ATTN && a.gamma) {
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
   }
   __syncthreads();
   float sc = 1.0f;
-  if (a.gamma) {
+  if (!ATTN && a.gamma) {
     float t = 0.f;
 #pragma unroll
     for (int i = 0; i < kWarps; ++i) t += red[i];
     sc = rsqrtf(t / (float)K + a.eps);
   }
+  if (halted) return false;
   if (inv_out && threadIdx.x == 0) *inv_out = sc;
+  if (a.trigger == 2) pdl_trigger();
+  trace_mark(a.trace_id, 4);
   float acc[NR];
 #pragma unroll
   for (int r = 0; r < NR; ++r) acc[r] = 0.f;
@@ -243,6 +308,7 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
   }
 #pragma unroll
   for (int r = 0; r < NR; ++r) acc[r] = warp_sum(acc[r]);
+  trace_mark(a.trace_id, 5);
   if (lane == 0) {
     if (swiglu) {
       if (valid[0]) {
@@ -262,7 +328,113 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
       }
     }
   }
+  trace_mark(a.trace_id, 2);
   return true;
+}
+
+// CodePredictor attention (at most kCpFusedPositions positions) computed by
+// every CTA of the O projection while it stages its input: warp w handles kv
+// head w (and w + 8, ...) with its two q heads; lane l holds dims 4l..4l+3.
+// QK-RMSNorm, RoPE, the bf16 round of the new K/V row and the softmax follow
+// the standalone decode-attention kernel; CTA 0 appends the row to the cache.
+constexpr int kCpFusedPositions = 16;
+
+__device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, float* xs, int halted) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = at.pos_const, T = pos + 1;
+  const int kvh = at.kv.kv_heads;
+  const int q_out = at.q_heads * kHeadDim, kv_out = kvh * kHeadDim;
+  const int d0 = 4 * lane;
+  for (int g = warp; g < kvh; g += kWarps) {
+    uint2 kc[kCpFusedPositions], vc[kCpFusedPositions];
+#pragma unroll
+    for (int p = 0; p < kCpFusedPositions; ++p) {
+      if (p < pos) {
+        kc[p] = *reinterpret_cast<const uint2*>(kv_ptr(at.kv, at.layer, 0, g, p) + d0);
+        vc[p] = *reinterpret_cast<const uint2*>(kv_ptr(at.kv, at.layer, 1, g, p) + d0);
+      }
+    }
+    float4 q[2];
+    q[0] = __ldcg(reinterpret_cast<const float4*>(at.qkv + (2 * g) * kHeadDim + d0));
+    q[1] = __ldcg(reinterpret_cast<const float4*>(at.qkv + (2 * g + 1) * kHeadDim + d0));
+    float4 kk = __ldcg(reinterpret_cast<const float4*>(at.qkv + q_out + g * kHeadDim + d0));
+    const float4 vv = __ldcg(reinterpret_cast<const float4*>(at.qkv + q_out + kv_out + g * kHeadDim + d0));
+    const float4 qg = __ldg(reinterpret_cast<const float4*>(at.q_gamma + d0));
+    const float4 kg = __ldg(reinterpret_cast<const float4*>(at.k_gamma + d0));
+    const float4 rc = __ldg(reinterpret_cast<const float4*>(at.rope_cos + pos * 64 + (d0 & 63)));
+    const float4 rs = __ldg(reinterpret_cast<const float4*>(at.rope_sin + pos * 64 + (d0 & 63)));
+    auto norm_rope = [&](float4 x, float4 gm) {
+      const float ss = warp_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
+      const float inv = rsqrtf(ss / (float)kHeadDim + at.eps);
+      x.x = x.x * inv * gm.x; x.y = x.y * inv * gm.y; x.z = x.z * inv * gm.z; x.w = x.w * inv * gm.w;
+      float4 o;
+      o.x = __shfl_xor_sync(0xffffffffu, x.x, 16); o.y = __shfl_xor_sync(0xffffffffu, x.y, 16);
+      o.z = __shfl_xor_sync(0xffffffffu, x.z, 16); o.w = __shfl_xor_sync(0xffffffffu, x.w, 16);
+      if (lane < 16) {
+        x.x = x.x * rc.x - o.x * rs.x; x.y = x.y * rc.y - o.y * rs.y;
+        x.z = x.z * rc.z - o.z * rs.z; x.w = x.w * rc.w - o.w * rs.w;
+      } else {
+        x.x = x.x * rc.x + o.x * rs.x; x.y = x.y * rc.y + o.y * rs.y;
+        x.z = x.z * rc.z + o.z * rs.z; x.w = x.w * rc.w + o.w * rs.w;
+      }
+      return x;
+    };
+    q[0] = norm_rope(q[0], qg);
+    q[1] = norm_rope(q[1], qg);
+    kk = norm_rope(kk, kg);
+    const __nv_bfloat162 kb0 = __floats2bfloat162_rn(kk.x, kk.y), kb1 = __floats2bfloat162_rn(kk.z, kk.w);
+    const __nv_bfloat162 vb0 = __floats2bfloat162_rn(vv.x, vv.y), vb1 = __floats2bfloat162_rn(vv.z, vv.w);
+    uint2 kcur, vcur;
+    kcur.x = *reinterpret_cast<const unsigned*>(&kb0); kcur.y = *reinterpret_cast<const unsigned*>(&kb1);
+    vcur.x = *reinterpret_cast<const unsigned*>(&vb0); vcur.y = *reinterpret_cast<const unsigned*>(&vb1);
+    if (blockIdx.x == 0 && !halted) {
+      *reinterpret_cast<uint2*>(kv_ptr(at.kv, at.layer, 0, g, pos) + d0) = kcur;
+      *reinterpret_cast<uint2*>(kv_ptr(at.kv, at.layer, 1, g, pos) + d0) = vcur;
+    }
+    float d[2][kCpFusedPositions];
+#pragma unroll
+    for (int p = 0; p < kCpFusedPositions; ++p) {
+      const uint2 ku = p < pos ? kc[p] : kcur;
+      const float k0 = bf16lo(ku.x), k1 = bf16hi(ku.x), k2 = bf16lo(ku.y), k3 = bf16hi(ku.y);
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        d[j][p] = (q[j].x * at.scale) * k0 + (q[j].y * at.scale) * k1 +
+                  (q[j].z * at.scale) * k2 + (q[j].w * at.scale) * k3;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int p = 0; p < kCpFusedPositions; ++p)
+          d[j][p] += __shfl_xor_sync(0xffffffffu, d[j][p], o);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int p = 0; p < kCpFusedPositions; ++p)
+        if (p < T) m = fmaxf(m, d[j][p]);
+      float l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < kCpFusedPositions; ++p) {
+        if (p >= T) continue;
+        const float e = expf(d[j][p] - m);
+        const uint2 vu = p < pos ? vc[p] : vcur;
+        l += e;
+        acc[0] = fmaf(e, bf16lo(vu.x), acc[0]); acc[1] = fmaf(e, bf16hi(vu.x), acc[1]);
+        acc[2] = fmaf(e, bf16lo(vu.y), acc[2]); acc[3] = fmaf(e, bf16hi(vu.y), acc[3]);
+      }
+      const float il = 1.0f / l;
+      *reinterpret_cast<float4*>(xs + (2 * g + j) * kHeadDim + d0) =
+          make_float4(acc[0] * il, acc[1] * il, acc[2] * il, acc[3] * il);
+    }
+  }
+}
+
+template <int KCH>
+__global__ void __launch_bounds__(kThreads) k_gemv1_attn(LinearArgs a, AttnDecodeArgs at) {
+  __shared__ __align__(16) float xs[KCH * 256 + 32];
+  gemv1_body<KCH, 1, true>(a, EPI_RESID, xs, nullptr, &at);
 }
 
 template <int KCH, int NR>
@@ -292,6 +464,7 @@ __global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
   __threadfence();
   if (a.role == ROLE_LOGITS_ONLY) return;
 
+  trace_mark(a.lin.trace_id, 4);
   const int V = a.lin.N;
   Selector<SyncBlock> sel{smem, reinterpret_cast<int*>(smem + kSelMaxVocab)};
   const int tid = threadIdx.x;
@@ -309,6 +482,7 @@ __global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
     a.st->rng_counter = rng.counter;
   }
   if (a.token_out && tid == 0) *a.token_out = tok;
+  trace_mark(a.lin.trace_id, 5);
 
   const int H = a.H;
   if (a.role == ROLE_TALKER_PREFILL || a.role == ROLE_TALKER_STEP) {
@@ -350,6 +524,7 @@ __global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
       }
     }
   }
+  trace_mark(a.lin.trace_id, 2);
 }
 
 // ---------------------------------------------------------------------------
@@ -369,11 +544,14 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
   __shared__ float red[4][G + 1];
   __shared__ float wm[NW][G], wl[NW][G];
   __shared__ float wacc[NW][G][kHeadDim];
+  trace_mark(a.trace_id, 0);
   pdl_wait();
-  if (a.halt && *a.halt) return;
+  trace_mark(a.trace_id, 1);
+  // halt, position and the projections are independent loads: issue together
+  const int halted = a.halt ? __ldcg(a.halt) : 0;
   const int h = blockIdx.x, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int pos = a.pos_ptr ? *a.pos_ptr : a.pos_const;
+  const int pos = a.pos_ptr ? __ldcg(a.pos_ptr) : a.pos_const;
   const int T = pos + 1;
   const int kvh = a.kv.kv_heads;
   const int q_out = a.q_heads * kHeadDim, kv_out = kvh * kHeadDim;
@@ -381,9 +559,36 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
   float qr[G], kr = 0.f, vr = 0.f;
   if (tid < kHeadDim) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) qr[g] = a.qkv[(h * G + g) * kHeadDim + tid];
-    kr = a.qkv[q_out + h * kHeadDim + tid];
-    vr = a.qkv[q_out + kv_out + h * kHeadDim + tid];
+    for (int g = 0; g < G; ++g) qr[g] = __ldcg(a.qkv + (h * G + g) * kHeadDim + tid);
+    kr = __ldcg(a.qkv + q_out + h * kHeadDim + tid);
+    vr = __ldcg(a.qkv + q_out + kv_out + h * kHeadDim + tid);
+  }
+  // Rows before `pos` come from the cache; the current row from shared memory.
+  auto load = [&](int p0, uint2 (&ku)[kAttnBatch], uint2 (&vu)[kAttnBatch]) {
+#pragma unroll
+    for (int i = 0; i < kAttnBatch; ++i) {
+      const int p = p0 + i;
+      if (p < pos) {
+        ku[i] = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 0, h, p) + 4 * lane);
+        vu[i] = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 1, h, p) + 4 * lane);
+      } else {
+        ku[i] = make_uint2(0u, 0u);
+        vu[i] = make_uint2(0u, 0u);
+      }
+    }
+  };
+  uint2 ku[kAttnBatch], vu[kAttnBatch], nk[kAttnBatch], nv[kAttnBatch];
+  int p0 = warp * kAttnBatch;
+  if (p0 < T) load(p0, ku, vu);  // cached rows: independent of this step's projections
+  float rc = 0.f, rsn = 0.f, qgam = 0.f, kgam = 0.f;
+  if (tid < kHeadDim) {
+    rc = a.rope_cos[pos * 64 + (tid & 63)];
+    rsn = a.rope_sin[pos * 64 + (tid & 63)];
+    qgam = a.q_gamma[tid];
+    kgam = a.k_gamma[tid];
+  }
+  if (halted) return;
+  if (tid < kHeadDim) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const float t = warp_sum(qr[g] * qr[g]);
@@ -397,16 +602,16 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const float ss = red[0][g] + red[1][g] + red[2][g] + red[3][g];
-      sq[g][tid] = qr[g] * rsqrtf(ss / (float)kHeadDim + a.eps) * a.q_gamma[tid];
+      sq[g][tid] = qr[g] * rsqrtf(ss / (float)kHeadDim + a.eps) * qgam;
     }
     const float ss = red[0][G] + red[1][G] + red[2][G] + red[3][G];
-    sk[tid] = kr * rsqrtf(ss / (float)kHeadDim + a.eps) * a.k_gamma[tid];
+    sk[tid] = kr * rsqrtf(ss / (float)kHeadDim + a.eps) * kgam;
   }
   __syncthreads();
   float rq[G], kroped = 0.f;
   if (tid < kHeadDim) {
     const int pi = tid & 63;
-    const float c = a.rope_cos[pos * 64 + pi], sn = a.rope_sin[pos * 64 + pi];
+    const float c = rc, sn = rsn;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const float x0 = sq[g][pi], x1 = sq[g][pi + 64];
@@ -436,23 +641,6 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) { q[g][j] = sq[g][4 * lane + j] * a.scale; acc[g][j] = 0.f; }
   }
-  // Rows before `pos` come from the cache; the current row from shared memory.
-  auto load = [&](int p0, uint2 (&ku)[kAttnBatch], uint2 (&vu)[kAttnBatch]) {
-#pragma unroll
-    for (int i = 0; i < kAttnBatch; ++i) {
-      const int p = p0 + i;
-      if (p < pos) {
-        ku[i] = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 0, h, p) + 4 * lane);
-        vu[i] = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 1, h, p) + 4 * lane);
-      } else {
-        ku[i] = make_uint2(0u, 0u);
-        vu[i] = make_uint2(0u, 0u);
-      }
-    }
-  };
-  uint2 ku[kAttnBatch], vu[kAttnBatch], nk[kAttnBatch], nv[kAttnBatch];
-  int p0 = warp * kAttnBatch;
-  if (p0 < T) load(p0, ku, vu);
   for (; p0 < T; p0 += NW * kAttnBatch) {
     const int pn = p0 + NW * kAttnBatch;
     if (pn < T) load(pn, nk, nv);
@@ -528,6 +716,7 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
     }
     a.out[(h * G + g) * kHeadDim + dd] = A / L;
   }
+  trace_mark(a.trace_id, 2);
 }
 
 // Prefill: QK-RMSNorm + RoPE for M rows at positions pos0.., K/V appended to
@@ -757,6 +946,25 @@ cudaError_t configure_kernels() {
   if ((e = cudaFuncSetAttribute(k_head<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(k_head<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem)) != cudaSuccess) return e;
   return cudaFuncSetAttribute(k_head<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem);
+}
+
+bool attn_o_fusable(const AttnDecodeArgs& at, const LinearArgs& o) {
+  return !at.pos_ptr && at.pos_const < kCpFusedPositions && at.q_heads == 2 * at.kv.kv_heads &&
+         o.M == 1 && o.K == at.q_heads * kHeadDim && !o.gamma &&
+         (o.K == 512 || o.K == 1024 || o.K == 2048);
+}
+
+cudaError_t launch_attn_o(const AttnDecodeArgs& at, const LinearArgs& o, cudaStream_t stream) {
+  if (!attn_o_fusable(at, o)) return cudaErrorInvalidValue;
+  dim3 grid((o.N + kWarps - 1) / kWarps);
+  if (o.K == 512) return launch(k_gemv1_attn<2>, grid, dim3(kThreads), 0, stream, o, at);
+  if (o.K == 1024) return launch(k_gemv1_attn<4>, grid, dim3(kThreads), 0, stream, o, at);
+  return launch(k_gemv1_attn<8>, grid, dim3(kThreads), 0, stream, o, at);
+}
+
+cudaError_t set_step_trace(unsigned long long* buf, int capacity, cudaStream_t stream) {
+  const StepTrace t{buf, buf ? capacity : 0};
+  return cudaMemcpyToSymbolAsync(g_trace, &t, sizeof(t), 0, cudaMemcpyHostToDevice, stream);
 }
 
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t stream) {

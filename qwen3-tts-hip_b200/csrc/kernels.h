@@ -33,6 +33,15 @@ struct LinearArgs {
   const float* bias;       // EPI_BIAS* [N]
   int M, N, K;
   const int* halt;         // optional: kernel is a no-op while *halt != 0
+  // Optional L2 prefetch of up to three byte ranges (16-byte aligned, sizes
+  // multiples of 16), shared out over the grid before the dependency wait:
+  // the weights of ops further down the frame, so HBM streams ahead of the
+  // dependency chain.
+  const char* pf_ptr[3];
+  unsigned pf_bytes[3];
+  int trace_id;            // > 0: record entry / dependency-wait / exit times (step trace)
+  int trigger;             // decode GEMV: 0 = launch dependents at entry, 1 = after the
+                           // wait, 2 = after staging the input, 3 = at exit
 };
 
 // Sampling parameters of one token kind (talker or subtalker).
@@ -114,6 +123,7 @@ struct AttnDecodeArgs {
   float* out;              // [q_heads * 128]
   int nsplit;
   const int* halt;
+  int trace_id;
 };
 
 struct QkPrepArgs {
@@ -146,7 +156,16 @@ struct AttnPrefillArgs {
 
 cudaError_t launch_linear(const LinearArgs& a, Epilogue epi, cudaStream_t stream);
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t stream);
+// CodePredictor decode attention fused into the O projection (o.x unused,
+// o.resid = residual); only for a fixed position below 16 and two q heads per
+// kv head (attn_o_fusable).
+bool attn_o_fusable(const AttnDecodeArgs& at, const LinearArgs& o);
+cudaError_t launch_attn_o(const AttnDecodeArgs& at, const LinearArgs& o, cudaStream_t stream);
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t stream);
+// Step trace buffer: [6][capacity] u64 globaltimer values (first entry, first
+// post-wait, last exit, last post-wait, head selection start/end) indexed by
+// trace_id; nullptr disables. Stream-ordered.
+cudaError_t set_step_trace(unsigned long long* buf, int capacity, cudaStream_t stream);
 cudaError_t launch_qk_prep(const QkPrepArgs& a, cudaStream_t stream);
 cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t stream);
 

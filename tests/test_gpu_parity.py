@@ -339,9 +339,12 @@ def test_full_size_0p6b(pkg, tmp_path_factory):
     e.close()
 
 
-def test_frame_kernel_path_parity(model_dirs, tmp_path):
-    """The opt-in persistent frame kernel (QTTS_FRAME_KERNEL=1) against the
-    oracle, run in a child process so the engine picks up the setting."""
+@pytest.mark.parametrize("env_var,value", [("QTTS_FRAME_KERNEL", "1"), ("QTTS_FUSE_ATTN_O", "0")])
+def test_alternate_path_parity(model_dirs, tmp_path, env_var, value):
+    """The alternate frame paths against the oracle: the opt-in persistent
+    frame kernel (QTTS_FRAME_KERNEL=1) and the unfused CodePredictor attention
+    (QTTS_FUSE_ATTN_O=0). Run in a child process so the engine reads the
+    setting at load."""
     import os
     import subprocess
     import sys
@@ -375,7 +378,7 @@ for shape, d in [('tiny', {str(model_dirs['tiny'])!r}), ('tiny_proj', {str(model
     assert agree >= 0.98, (shape, agree)
 print("frame kernel ok")
 """
-    env = dict(os.environ, QTTS_FRAME_KERNEL="1")
+    env = dict(os.environ, **{env_var: value})
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
                        timeout=600)
     assert r.returncode == 0 and "frame kernel ok" in r.stdout, r.stdout + r.stderr
