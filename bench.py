@@ -184,6 +184,22 @@ def cpu_reference_run(c, mdir, ids, n_frames, steps, warmup, seed=0):
     return frames / total, frames, total, torch.get_num_threads(), pre.shape[0]
 
 
+def reduce_over_ranks(maxed, summed, world, device):
+    """Whole-job figures from per-rank ones: times as the max over ranks (the
+    slowest replica bounds the job), counts as the sum. World 1 returns them
+    unchanged; otherwise every rank of the initialised process group calls it."""
+    if world <= 1:
+        return list(maxed), list(summed)
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(maxed, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    f = torch.tensor(summed, dtype=torch.float64, device=device)
+    dist.all_reduce(f, op=dist.ReduceOp.SUM)
+    return t.tolist(), f.tolist()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -275,14 +291,9 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-        t = torch.tensor([dev_ms, wall_s], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        f = torch.tensor([frames, launches], dtype=torch.float64, device="cuda")
-        dist.all_reduce(f, op=dist.ReduceOp.SUM)
-        dev_ms_max, wall_max = t.tolist()
-        frames_all, launches_all = (int(x) for x in f.tolist())
-    else:
-        dev_ms_max, wall_max, frames_all, launches_all = dev_ms, wall_s, frames, launches
+    (dev_ms_max, wall_max), (frames_all, launches_all) = reduce_over_ranks(
+        [dev_ms, wall_s], [frames, launches], world, "cuda")
+    frames_all, launches_all = int(frames_all), int(launches_all)
 
     # dominant kernel: talker gate|up GEMV (+ RMSNorm prologue, SwiGLU epilogue)
     ms_k, bytes_k = eng.profile_projection(0, 280)
@@ -313,7 +324,7 @@ def main():
                 "h2d_bytes_per_step": int(ids.nbytes),
                 "d2h_bytes_per_step": int(out.frames * 16 * 4 + 64)},
         "gpu_launches": launches_all,
-        "roofline": {"bound": "hbm", "kernel": "k_linear<M=1,SwiGLU> talker gate|up (1024->2x3072)",
+        "roofline": {"bound": "hbm", "kernel": "k_gemv1<4,2> talker gate|up + SwiGLU (1024->2x3072), RMSNorm prologue",
                      "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind,
                      "bytes_per_launch": bytes_k, "ms_per_launch": ms_k,

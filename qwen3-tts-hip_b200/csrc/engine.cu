@@ -29,6 +29,7 @@
 #include <vector>
 
 #include "frame_kernel.h"
+#include "gemm_tc.h"
 #include "json.h"
 #include "kernels.h"
 #include "qtts_b200.h"
@@ -303,6 +304,21 @@ class Engine {
   std::map<SampleKey, std::pair<FrameOp*, int>> frame_ops;  // device op lists
   int frame_grid = 0;
   bool use_frame_kernel = true;
+  // tcgen05 projections for M >= tc_min_rows rows (QTTS_TC=0 disables)
+  // Which projections use it is fixed per call site, not per row count, so a
+  // row gets identical arithmetic however the rows are batched (one-shot vs
+  // streamed prompts): the talker prefill and the text MLP always, the
+  // CodePredictor's 2-row prefill only with QTTS_TC_CP=1.
+  TcActs tc{};
+  int* tc_err = nullptr;
+  bool tc_scope = false;
+  bool tc_cp = false;
+  struct TcScope {
+    bool& f;
+    bool old;
+    TcScope(bool& flag, bool on) : f(flag), old(flag) { f = on; }
+    ~TcScope() { f = old; }
+  };
   // CodePredictor attention inside the O projection (QTTS_FUSE_ATTN_O=0: separate kernels)
   bool fuse_attn_o = true;
   unsigned* frame_seq = nullptr;
@@ -339,6 +355,11 @@ class Engine {
               float* y, int ldy, const float* resid, int ldr, const float* bias, int M, int N,
               int K, Epilogue epi, const int* halt) {
     LinearArgs a{W, x, ldx, gamma, eps, y, ldy, resid, ldr, bias, M, N, K, halt};
+    if (tc_scope && tc_supported(a, epi, tc)) {
+      QCK(launch_linear_tc(a, epi, tc, tc_err, stream));  // split + tcgen05 GEMM
+      launches += 2;
+      return;
+    }
     static const char* kEpi[] = {"gemv", "gemv+resid", "gemv+swiglu", "gemv+bias", "gemv+bias+silu"};
     a.trace_id = trace_tag(kEpi[epi], N, K);
     a.trigger = trigger_mode;
@@ -559,6 +580,7 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   QCK(cudaSetDevice(dev));
   QCK(configure_kernels());
   QCK(configure_frame_kernel());
+  QCK(configure_tc_kernels());
   QCK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   QCK(cudaEventCreate(&ev0));
   QCK(cudaEventCreate(&ev1));
@@ -622,6 +644,25 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
 
   // workspaces
   const int rows = (int)mcs;
+  {
+    // split activations for the tcgen05 projections of many rows (prefill, text MLP)
+    const char* tz = std::getenv("QTTS_TC");
+    if (const char* tcp = std::getenv("QTTS_TC_CP")) tc_cp = tcp[0] == '1';
+    if (!(tz && tz[0] == '0')) {
+      int ld = std::max({T.hidden, T.q_heads * T.head_dim, T.intermediate, C.hidden,
+                         C.q_heads * C.head_dim, C.intermediate});
+      if (text_hidden) ld = std::max({ld, text_hidden, text_inter});
+      ld = (ld + 63) / 64 * 64;
+      tc.rows_cap = rows + 16;
+      tc.ld = ld;
+      tc.hi = arena.alloc<__nv_bfloat16>((size_t)tc.rows_cap * ld);
+      tc.lo = arena.alloc<__nv_bfloat16>((size_t)tc.rows_cap * ld);
+      tc.rms = arena.alloc<float>((size_t)tc.rows_cap);
+      tc_err = arena.alloc<int>(1);
+      QCK(cudaMemset(tc_err, 0, sizeof(int)));
+      if (!tc_make_acts(tc)) tc = TcActs{};
+    }
+  }
   tb = alloc_bufs(arena, talker, rows);
   cb = alloc_bufs(arena, cp, 2);
   {
@@ -737,6 +778,7 @@ void Engine::stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int 
                         const int* halt) {
   const StackCfg& c = S.c;
   const float scale = 1.0f / std::sqrt((float)c.head_dim);
+  TcScope tcs(tc_scope, &S == &talker || tc_cp);
   for (int l = 0; l < c.layers; ++l) {
     linear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr, M,
            S.qkv_w, c.hidden, EPI_STORE, halt);
@@ -1137,6 +1179,7 @@ void Engine::project_text(const std::vector<int>& ids, float* out) {
   if (n > tp_rows) invalid("too many text rows");
   QCK(cudaMemcpyAsync(tp_ids, ids.data(), n * 4, cudaMemcpyHostToDevice, stream));
   QCK(launch_gather_rows(text_emb, tp_ids, n, text_hidden, tp_a, stream));
+  TcScope tcs(tc_scope, true);
   linear(fc1, tp_a, text_hidden, nullptr, 0.f, tp_b, text_inter, nullptr, 0, fc1_b, n,
          text_inter, text_hidden, EPI_BIAS_SILU, nullptr);
   linear(fc2, tp_b, text_inter, nullptr, 0.f, out, cfg.talker.hidden, nullptr, 0, fc2_b, n,
@@ -1256,6 +1299,12 @@ void Engine::sync_state() {
   QCK(cudaStreamSynchronize(stream));
   if (st_host->error)
     fail(QTTS_ERR_DEVICE_STATE, "cannot sample from logits with no finite values");
+  if (tc_err) {
+    int e = 0;
+    QCK(cudaMemcpy(&e, tc_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) fail(QTTS_ERR_DEVICE_STATE, "tensor-core projection pipeline timed out (stage " +
+                                           std::to_string(e) + ")");
+  }
 }
 
 // Enqueues up to n frames (fewer if EOS stops the loop on the device) and

@@ -339,12 +339,15 @@ def test_full_size_0p6b(pkg, tmp_path_factory):
     e.close()
 
 
-@pytest.mark.parametrize("env_var,value", [("QTTS_FRAME_KERNEL", "1"), ("QTTS_FUSE_ATTN_O", "0")])
+@pytest.mark.parametrize("env_var,value", [("QTTS_FRAME_KERNEL", "1"), ("QTTS_FUSE_ATTN_O", "0"),
+                                           ("QTTS_TC_CP", "1"), ("QTTS_TC", "0")])
 def test_alternate_path_parity(model_dirs, tmp_path, env_var, value):
-    """The alternate frame paths against the oracle: the opt-in persistent
-    frame kernel (QTTS_FRAME_KERNEL=1) and the unfused CodePredictor attention
-    (QTTS_FUSE_ATTN_O=0). Run in a child process so the engine reads the
-    setting at load."""
+    """The alternate paths against the oracle: the opt-in persistent frame
+    kernel (QTTS_FRAME_KERNEL=1), the unfused CodePredictor attention
+    (QTTS_FUSE_ATTN_O=0), the tcgen05 projection also for the CodePredictor's
+    2-row prefill (QTTS_TC_CP=1) and the CUDA-core projections only
+    (QTTS_TC=0). Run in a child process so the engine reads
+    the setting at load."""
     import os
     import subprocess
     import sys
