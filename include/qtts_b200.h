@@ -137,6 +137,19 @@ int32_t qtts_generate_codes_from_ids(qtts_engine* engine, const uint32_t* conten
                                      int32_t* codes_out, size_t codes_capacity,
                                      size_t* frames_out, int32_t* ended_by_eos);
 
+/* Batched serving (no reference counterpart; the reference serves one
+ * sequence per engine): `batch` requests (1..16) generated together, their
+ * content ids concatenated in `ids` with lengths[b] ids each. opts[b] may
+ * differ only in seed, speaker and language. The requests are prefilled one
+ * by one, then stepped in lockstep, every projection a tensor-core GEMM over
+ * all rows. Codes of request b go to codes_out + b * cap_per_request
+ * ([frames x 16] i32), with frames_out[b] and ended_out[b] (EOS). */
+int32_t qtts_generate_codes_batch_from_ids(qtts_engine* engine, const uint32_t* ids,
+                                           const size_t* lengths, size_t batch,
+                                           const qtts_generate_options* opts, int32_t* codes_out,
+                                           size_t cap_per_request, size_t* frames_out,
+                                           int32_t* ended_out);
+
 /* HipTtsEngine::generate_voice_clone_codes (generation.rs:373-395), x-vector
  * mode: speaker_embedding[hidden] replaces the speaker codec row
  * (text.rs:432-514). */

@@ -88,4 +88,23 @@ __device__ __forceinline__ __nv_bfloat16* kv_ptr(const KvView& v, int layer, int
          ((long long)((kind * v.kv_heads + head) << v.page_shift) + inpage) * kHeadDim;
 }
 
+// Kernel launch with programmatic dependent launch allowed (the kernel's
+// griddepcontrol.wait orders it after its predecessor; work before the wait
+// may overlap the predecessor's tail).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 }  // namespace qtts

@@ -431,6 +431,41 @@ class Engine {
                    float* cp_prefix_dst);
   void cp_head(int group, const float* x, const SampleCfg& c, const int* halt);
   void enqueue_frame(const SampleKey& k);
+
+  // ---- batched serving: up to kBatchCap sequences stepped in lockstep ----
+  // Each request is prefilled alone (the validated single-sequence path,
+  // writing into its own slot of the batch KV pool), then every frame runs
+  // the CodePredictor pass and the talker step for all sequences at once:
+  // projections as tcgen05 GEMMs with M = B (weights read once per frame for
+  // the whole batch), attention and token selection per sequence.
+  static constexpr int kBatchCap = 16;
+  struct BatchBufs {
+    int cap = 0;
+    SeqState* st = nullptr;
+    SeqState* st_host = nullptr;
+    int *codes = nullptr, *history = nullptr;
+    float *trailing = nullptr, *cp_prefix = nullptr, *cp_next = nullptr, *emb_sum = nullptr,
+          *logits = nullptr;
+    StackBufs tb{}, cb{};
+    KvView tkv{}, ckv{};
+    int pages = 0;  // talker KV pages per sequence
+    TcActs acts{};
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};  // prefill start, frames start, end
+  } bt;
+  std::map<std::pair<SampleKey, int>, cudaGraphExec_t> batch_graphs;
+  std::map<std::pair<SampleKey, int>, size_t> batch_nodes;
+  void ensure_batch();
+  void blinear(const __nv_bfloat16* W, const float* x, int ldx, const float* gamma, float eps,
+               float* y, int ldy, const float* resid, int ldr, const float* bias, int M, int N,
+               int K, Epilogue epi);
+  void batch_stack_step(DevStack& S, StackBufs& B, const KvView& kv, int pt_stride,
+                        const int* pos_ptr, int pos_const, int nb);
+  void batch_head(int role, int group, const float* x, const SampleCfg& c, float penalty, int nb);
+  void enqueue_batch_frame(const SampleKey& k, int nb);
+  cudaGraphExec_t batch_graph(const SampleKey& k, int nb);
+  void generate_batch(const std::vector<std::vector<uint32_t>>& ids,
+                      const std::vector<qtts_generate_options>& opts, int32_t* codes_out,
+                      size_t cap_per_request, size_t* frames_out, int32_t* ended_out);
   void enqueue_frame_kernel(const SampleKey& k);
   std::vector<FrameOp> build_frame_ops(const SampleKey& k);
   bool frame_ops_fit(const std::vector<FrameOp>& ops) const;
@@ -655,6 +690,7 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
       ld = (ld + 63) / 64 * 64;
       tc.rows_cap = rows + 16;
       tc.ld = ld;
+      tc.box_rows = 128;
       tc.hi = arena.alloc<__nv_bfloat16>((size_t)tc.rows_cap * ld);
       tc.lo = arena.alloc<__nv_bfloat16>((size_t)tc.rows_cap * ld);
       tc.rms = arena.alloc<float>((size_t)tc.rows_cap);
@@ -766,7 +802,11 @@ Engine::~Engine() {
   cudaSetDevice(device);
   if (stream) cudaStreamSynchronize(stream);
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : batch_graphs) cudaGraphExecDestroy(kv.second);
   if (st_host) cudaFreeHost(st_host);
+  if (bt.st_host) cudaFreeHost(bt.st_host);
+  for (auto& ev : bt.ev)
+    if (ev) cudaEventDestroy(ev);
   if (ev0) cudaEventDestroy(ev0);
   if (ev1) cudaEventDestroy(ev1);
   if (ev2) cudaEventDestroy(ev2);
@@ -1372,6 +1412,313 @@ void Engine::dump_step_trace() {
   std::fclose(f);
 }
 
+// ---- batched serving -------------------------------------------------------
+void Engine::ensure_batch() {
+  if (bt.cap) return;
+  if (!tc.hi) fail(QTTS_ERR_UNSUPPORTED, "batched generation needs the tensor-core projections");
+  const StackCfg& T = cfg.talker;
+  const StackCfg& C = cfg.cp;
+  const int cap = kBatchCap;
+  const size_t mcs = max_cache_steps;
+  const size_t H = T.hidden;
+  bt.cap = cap;
+  bt.st = arena.alloc<SeqState>(cap);
+  QCK(cudaMallocHost(&bt.st_host, sizeof(SeqState) * cap));
+  bt.codes = arena.alloc<int>((size_t)cap * mcs * C.groups);
+  bt.history = arena.alloc<int>((size_t)cap * mcs);
+  bt.trailing = arena.alloc<float>((size_t)cap * (mcs + 1) * H);
+  bt.cp_prefix = arena.alloc<float>((size_t)cap * 2 * H);
+  bt.cp_next = arena.alloc<float>((size_t)cap * H);
+  bt.emb_sum = arena.alloc<float>((size_t)cap * H);
+  bt.logits = arena.alloc<float>((size_t)cap * std::max(T.vocab, C.vocab));
+  bt.tb = alloc_bufs(arena, talker, cap);
+  bt.cb = alloc_bufs(arena, cp, cap);
+  // talker KV: cap sequences x pages each; page table row b = its pages
+  bt.tkv = tkv;
+  bt.pages = (int)((mcs + (1u << tkv.page_shift) - 1) >> tkv.page_shift);
+  bt.tkv.pool = arena.alloc<__nv_bfloat16>((size_t)(tkv.page_stride * bt.pages * cap));
+  {
+    std::vector<int> pt((size_t)bt.pages * cap);
+    for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
+    int* d = arena.alloc<int>(pt.size());
+    QCK(cudaMemcpy(d, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice));
+    bt.tkv.page_table = d;
+  }
+  // CodePredictor KV: one page (all its positions) per sequence
+  bt.ckv = ckv;
+  bt.ckv.pool = arena.alloc<__nv_bfloat16>((size_t)(ckv.page_stride * cap));
+  {
+    std::vector<int> pt(cap);
+    for (int i = 0; i < cap; ++i) pt[i] = i;
+    int* d = arena.alloc<int>(cap);
+    QCK(cudaMemcpy(d, pt.data(), cap * 4, cudaMemcpyHostToDevice));
+    bt.ckv.page_table = d;
+  }
+  // split activations for M <= 16 rows, 16-row token tiles, split-K workspace
+  bt.acts.rows_cap = cap;
+  bt.acts.ld = tc.ld;
+  bt.acts.box_rows = 16;
+  bt.acts.hi = arena.alloc<__nv_bfloat16>((size_t)cap * tc.ld);
+  bt.acts.lo = arena.alloc<__nv_bfloat16>((size_t)cap * tc.ld);
+  bt.acts.rms = arena.alloc<float>(cap);
+  int sms = 148;
+  QCK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  bt.acts.sm_count = sms;
+  bt.acts.max_splits = 16;
+  bt.acts.ws_floats = (size_t)2 * sms * 128 * 16;
+  bt.acts.ws = arena.alloc<float>(bt.acts.ws_floats);
+  bt.acts.tickets = arena.alloc<unsigned>(4096);
+  QCK(cudaMemset(bt.acts.tickets, 0, 4096 * sizeof(unsigned)));
+  if (!tc_make_acts(bt.acts)) fail(QTTS_ERR_UNSUPPORTED, "tensor map encoding is unavailable");
+  for (auto& ev : bt.ev) QCK(cudaEventCreate(&ev));
+}
+
+void Engine::blinear(const __nv_bfloat16* W, const float* x, int ldx, const float* gamma,
+                     float eps, float* y, int ldy, const float* resid, int ldr, const float* bias,
+                     int M, int N, int K, Epilogue epi) {
+  LinearArgs a{W, x, ldx, gamma, eps, y, ldy, resid, ldr, bias, M, N, K, nullptr};
+  if (!tc_supported(a, epi, bt.acts))
+    fail(QTTS_ERR_UNSUPPORTED, "projection shape unsupported by the batched tensor-core path");
+  QCK(launch_linear_tc(a, epi, bt.acts, tc_err, stream));
+  launches += 2;
+}
+
+// One position through all layers for nb sequences (rows of B.x).
+void Engine::batch_stack_step(DevStack& S, StackBufs& B, const KvView& kv, int pt_stride,
+                              const int* pos_ptr, int pos_const, int nb) {
+  const StackCfg& c = S.c;
+  const float scale = 1.0f / std::sqrt((float)c.head_dim);
+  for (int l = 0; l < c.layers; ++l) {
+    blinear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr, nb,
+            S.qkv_w, c.hidden, EPI_STORE);
+    AttnDecodeArgs da{};
+    da.qkv = B.qkv;
+    da.q_gamma = S.q_g[l];
+    da.k_gamma = S.k_g[l];
+    da.eps = c.eps;
+    da.rope_cos = S.rope_cos;
+    da.rope_sin = S.rope_sin;
+    da.kv = kv;
+    da.layer = l;
+    da.pos_ptr = pos_ptr;
+    da.pos_const = pos_const;
+    da.q_heads = c.q_heads;
+    da.scale = scale;
+    da.out = B.attn;
+    da.nsplit = 1;
+    da.halt = &bt.st[0].halt;
+    da.qkv_ld = S.qkv_w;
+    da.out_ld = S.q_out;
+    da.pos_stride = (int)(sizeof(SeqState) / sizeof(int));
+    da.halt_stride = (int)(sizeof(SeqState) / sizeof(int));
+    da.pt_stride = pt_stride;
+    da.batch = nb;
+    QCK(launch_attn_decode(da, stream));
+    ++launches;
+    blinear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, nb,
+            c.hidden, S.q_out, EPI_RESID);
+    blinear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
+            nullptr, nb, c.intermediate, c.hidden, EPI_SWIGLU);
+    blinear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.x, c.hidden, B.h1, c.hidden,
+            nullptr, nb, c.hidden, c.intermediate, EPI_RESID);
+  }
+}
+
+void Engine::batch_head(int role, int group, const float* x, const SampleCfg& c, float penalty,
+                        int nb) {
+  const StackCfg& T = cfg.talker;
+  const StackCfg& C = cfg.cp;
+  const bool talker_role = role != ROLE_CP_GROUP;
+  const StackCfg& S = talker_role ? T : C;
+  const __nv_bfloat16* W = talker_role ? head : cp_heads + (size_t)group * C.vocab * C.hidden;
+  const float* gamma = talker_role ? norm_g : cp_norm_g;
+  blinear(W, x, S.hidden, gamma, S.eps, bt.logits, S.vocab, nullptr, 0, nullptr, nb, S.vocab,
+          S.hidden, EPI_STORE);
+  BatchHeadArgs bh{};
+  HeadArgs& a = bh.h;
+  a.role = role;
+  a.cfg = c;
+  a.st = bt.st;
+  a.penalty = talker_role ? penalty : 1.0f;
+  a.history = bt.history;
+  a.history_out = bt.history;
+  a.eos_token = cfg.codec_eos;
+  a.suppress = talker_role ? 1 : 0;
+  a.talker_codec_emb = codec_emb;
+  a.H = T.hidden;
+  a.groups = C.groups;
+  a.codes = bt.codes;
+  a.lin = LinearArgs{W, x, S.hidden, gamma, S.eps, bt.logits, S.vocab, nullptr, 0, nullptr, 1,
+                     S.vocab, S.hidden, nullptr};
+  if (talker_role) {
+    a.cp_prefix = bt.cp_prefix;
+  } else {
+    a.group = group;
+    a.last_group = C.groups - 2;
+    a.cp_emb = cp_embs + (size_t)group * C.vocab * T.hidden;
+    a.cp_next = has_proj() ? bt.cp_next : bt.cb.x;
+    a.emb_sum = bt.emb_sum;
+    a.step_in = bt.tb.x;
+    a.trailing = bt.trailing;
+    a.tts_pad = tts_pad;
+  }
+  bh.logits = bt.logits;
+  bh.logits_ld = S.vocab;
+  bh.rms = bt.acts.rms;
+  bh.hist_stride = (long long)max_cache_steps;
+  bh.codes_stride = (long long)max_cache_steps * C.groups;
+  bh.next_stride = has_proj() ? T.hidden : C.hidden;
+  bh.step_stride = T.hidden;
+  bh.trail_stride = (long long)(max_cache_steps + 1) * T.hidden;
+  QCK(launch_select_batch(bh, nb, stream));
+  ++launches;
+}
+
+// One frame for nb sequences: CodePredictor positions 0 and 1 (its 2-row
+// prefill, as two decode steps), head 0, groups 1..14, then unless last the
+// talker step and its token (same order as enqueue_frame).
+void Engine::enqueue_batch_frame(const SampleKey& k, int nb) {
+  const StackCfg& T = cfg.talker;
+  const StackCfg& C = cfg.cp;
+  const size_t H = T.hidden;
+  for (int j = 0; j < 2; ++j) {
+    if (has_proj()) {
+      blinear(proj_w, bt.cp_prefix + j * H, 2 * (int)H, nullptr, 0.f, bt.cb.x, C.hidden, nullptr,
+              0, proj_b, nb, C.hidden, (int)H, EPI_BIAS);
+    } else {
+      QCK(cudaMemcpy2DAsync(bt.cb.x, C.hidden * sizeof(float), bt.cp_prefix + j * H,
+                            2 * H * sizeof(float), H * sizeof(float), nb,
+                            cudaMemcpyDeviceToDevice, stream));
+    }
+    batch_stack_step(cp, bt.cb, bt.ckv, 1, nullptr, j, nb);
+  }
+  batch_head(ROLE_CP_GROUP, 0, bt.cb.x, k.s, 1.0f, nb);
+  for (int g = 1; g < C.groups - 1; ++g) {
+    if (has_proj())
+      blinear(proj_w, bt.cp_next, (int)H, nullptr, 0.f, bt.cb.x, C.hidden, nullptr, 0, proj_b, nb,
+              C.hidden, (int)H, EPI_BIAS);
+    batch_stack_step(cp, bt.cb, bt.ckv, 1, nullptr, g + 1, nb);
+    batch_head(ROLE_CP_GROUP, g, bt.cb.x, k.s, 1.0f, nb);
+  }
+  if (!k.last) {
+    batch_stack_step(talker, bt.tb, bt.tkv, bt.pages, &bt.st[0].talker_pos, 0, nb);
+    batch_head(ROLE_TALKER_STEP, 0, bt.tb.x, k.t, k.penalty, nb);
+  }
+}
+
+cudaGraphExec_t Engine::batch_graph(const SampleKey& k, int nb) {
+  auto key = std::make_pair(k, nb);
+  auto it = batch_graphs.find(key);
+  if (it != batch_graphs.end()) return it->second;
+  cudaGraph_t g = nullptr;
+  const size_t before = launches;
+  QCK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    enqueue_batch_frame(k, nb);
+  } catch (...) {
+    cudaStreamEndCapture(stream, &g);
+    if (g) cudaGraphDestroy(g);
+    launches = before;
+    throw;
+  }
+  QCK(cudaStreamEndCapture(stream, &g));
+  batch_nodes[key] = launches - before;
+  launches = before;
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+  cudaGraphDestroy(g);
+  QCK(e);
+  batch_graphs[key] = exec;
+  return exec;
+}
+
+void Engine::generate_batch(const std::vector<std::vector<uint32_t>>& ids,
+                            const std::vector<qtts_generate_options>& opts, int32_t* codes_out,
+                            size_t cap_per_request, size_t* frames_out, int32_t* ended_out) {
+  const int nb = (int)ids.size();
+  if (nb < 1 || nb > kBatchCap)
+    invalid("batch size must be in [1, " + std::to_string(kBatchCap) + "]");
+  const qtts_generate_options& o0 = opts[0];
+  for (const auto& o : opts) {
+    validate(o);
+    if (o.max_frames != o0.max_frames || o.do_sample != o0.do_sample || o.top_k != o0.top_k ||
+        o.top_p != o0.top_p || o.temperature != o0.temperature ||
+        o.repetition_penalty != o0.repetition_penalty ||
+        o.subtalker_dosample != o0.subtalker_dosample ||
+        o.subtalker_top_k != o0.subtalker_top_k || o.subtalker_top_p != o0.subtalker_top_p ||
+        o.subtalker_temperature != o0.subtalker_temperature || o.rng != o0.rng)
+      invalid("batched requests must share every option except seed, speaker and language");
+  }
+  const size_t G = cfg.cp.groups;
+  if (cap_per_request < (size_t)o0.max_frames * G) invalid("codes_out capacity too small");
+  ensure_batch();
+  const size_t H = cfg.talker.hidden;
+  // prefill each request into its slot (the single-sequence path on the slot's KV view)
+  const KvView saved = tkv;
+  QCK(cudaEventRecord(bt.ev[0], stream));
+  try {
+    for (int b = 0; b < nb; ++b) {
+      int ntr = 0;
+      const int P = prepare(ids[b].data(), ids[b].size(), 0, opts[b].speaker, opts[b].language,
+                            nullptr, &ntr);
+      tkv = bt.tkv;
+      tkv.page_table = bt.tkv.page_table + (size_t)b * bt.pages;
+      begin(P, ntr, opts[b]);
+      tkv = saved;
+      QCK(cudaMemcpyAsync(bt.st + b, st, sizeof(SeqState), cudaMemcpyDeviceToDevice, stream));
+      QCK(cudaMemcpyAsync(bt.cp_prefix + (size_t)b * 2 * H, cp_prefix_target(),
+                          2 * H * sizeof(float), cudaMemcpyDeviceToDevice, stream));
+      QCK(cudaMemcpyAsync(bt.trailing + (size_t)b * (max_cache_steps + 1) * H, trailing,
+                          (size_t)ntr * H * sizeof(float), cudaMemcpyDeviceToDevice, stream));
+    }
+  } catch (...) {
+    tkv = saved;
+    throw;
+  }
+  SampleKey full{talker_cfg(o0), sub_cfg(o0), o0.repetition_penalty, 0};
+  SampleKey last = full;
+  last.last = 1;
+  const size_t max_frames = o0.max_frames;
+  cudaGraphExec_t gf = max_frames > 1 ? batch_graph(full, nb) : nullptr;
+  cudaGraphExec_t gl = batch_graph(last, nb);
+  size_t done = 0;
+  last_launches = 0;
+  QCK(cudaEventRecord(bt.ev[1], stream));
+  while (done < max_frames) {
+    const size_t burst = std::min<size_t>(16, max_frames - done);
+    for (size_t i = 0; i < burst; ++i) {
+      const bool is_last = done + i + 1 >= max_frames;
+      QCK(cudaGraphLaunch(is_last ? gl : gf, stream));
+      last_launches += batch_nodes[std::make_pair(is_last ? last : full, nb)];
+    }
+    done += burst;
+    QCK(cudaMemcpyAsync(bt.st_host, bt.st, sizeof(SeqState) * nb, cudaMemcpyDeviceToHost,
+                        stream));
+    QCK(cudaStreamSynchronize(stream));
+    bool all_halted = true;
+    for (int b = 0; b < nb; ++b) all_halted = all_halted && bt.st_host[b].halt;
+    if (all_halted) break;
+  }
+  QCK(cudaEventRecord(bt.ev[2], stream));
+  QCK(cudaStreamSynchronize(stream));
+  QCK(cudaEventElapsedTime(&last_prefill_ms, bt.ev[0], bt.ev[1]));
+  QCK(cudaEventElapsedTime(&last_frames_ms, bt.ev[1], bt.ev[2]));
+  int tc_e = 0;
+  QCK(cudaMemcpy(&tc_e, tc_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (tc_e) fail(QTTS_ERR_DEVICE_STATE, "tensor-core projection pipeline timed out");
+  last_frames = 0;
+  for (int b = 0; b < nb; ++b) {
+    const SeqState& s = bt.st_host[b];
+    if (s.error) fail(QTTS_ERR_DEVICE_STATE, "cannot sample from logits with no finite values");
+    const size_t f = (size_t)s.frames;
+    QCK(cudaMemcpy(codes_out + (size_t)b * cap_per_request, bt.codes + (size_t)b * max_cache_steps * G,
+                   f * G * sizeof(int32_t), cudaMemcpyDeviceToHost));
+    if (frames_out) frames_out[b] = f;
+    if (ended_out) ended_out[b] = s.halt ? 1 : 0;
+    last_frames += f;
+  }
+}
+
 void Engine::read_codes(size_t from, size_t to, int32_t* out) {
   if (to <= from) return;
   const size_t g = cfg.cp.groups;
@@ -1575,6 +1922,29 @@ int32_t qtts_generate_codes_from_ids(qtts_engine* h, const uint32_t* ids, size_t
     const int P = e.prepare(ids, n, 0, o->speaker, o->language, nullptr, &ntr);
     e.begin(P, ntr, *o);
     finish_generation(e, codes_out, cap, frames_out, ended);
+  });
+}
+
+int32_t qtts_generate_codes_batch_from_ids(qtts_engine* h, const uint32_t* ids,
+                                           const size_t* lengths, size_t batch,
+                                           const qtts_generate_options* opts, int32_t* codes_out,
+                                           size_t cap_per_request, size_t* frames_out,
+                                           int32_t* ended_out) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(lengths, "lengths");
+    need(opts, "options");
+    need(codes_out, "codes_out");
+    if (batch == 0) qtts::invalid("batch must be non-zero");
+    std::vector<std::vector<uint32_t>> reqs(batch);
+    size_t off = 0;
+    for (size_t b = 0; b < batch; ++b) {
+      if (lengths[b]) need(ids, "content_ids");
+      reqs[b].assign(ids + off, ids + off + lengths[b]);
+      off += lengths[b];
+    }
+    std::vector<qtts_generate_options> o(opts, opts + batch);
+    e.generate_batch(reqs, o, codes_out, cap_per_request, frames_out, ended_out);
   });
 }
 

@@ -9,6 +9,7 @@
 // completed) decouples loads from MMAs. Every wait is bounded.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 
@@ -19,13 +20,20 @@
 namespace qtts {
 namespace {
 
-constexpr int kTcStages = 4;
 constexpr int kTcThreads = 192;
 constexpr unsigned kTcSpin = 1u << 22;
-constexpr int kStageA = kTcRows * kTcBlockK * 2;        // 16 KB
-constexpr int kStageB = kTcTokens * kTcBlockK * 2;      // 16 KB (hi or lo)
-constexpr int kStageBytes = kStageA + 2 * kStageB;      // 48 KB
-constexpr size_t kTcSmem = (size_t)kTcStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kStageA = kTcRows * kTcBlockK * 2;  // 16 KB: 128 weight rows x 64 K
+
+// Per token-tile width BN (MMA N): stage ring depth and sizes.
+template <int BN>
+struct TcCfg {
+  static constexpr int kStages = BN >= 128 ? 4 : 8;
+  static constexpr int kStageB = BN * kTcBlockK * 2;         // hi or lo
+  static constexpr int kStageBytes = kStageA + 2 * kStageB;  // multiple of 1024
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256;
+  static_assert(kStageBytes % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
+};
 
 struct TcArgs {
   int M, N, K;
@@ -39,124 +47,182 @@ struct TcArgs {
   const float* rms;
   int* err;
   const int* halt;
+  int splits;            // K split over blockIdx.z; > 1 uses ws + tickets
+  float* ws;             // [tiles][splits][128][BN] partial tiles
+  unsigned* tickets;     // [tiles], zero at rest (reset by the last CTA)
 };
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
+template <int BN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap hmap,
               const __grid_constant__ CUtensorMap lmap, TcArgs a) {
+  using Cfg = TcCfg<BN>;
+  constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t tc_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcStages * kStageBytes);
-  uint64_t* empty = full + kTcStages;
-  uint64_t* done = empty + kTcStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* done = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool swiglu = a.epi == EPI_SWIGLU;
   const int n0 = blockIdx.x * (swiglu ? kTcRows / 2 : kTcRows);   // first output column
   const int row_a0 = n0;                                          // weight rows, box 0
   const int row_a1 = swiglu ? a.up_off + n0 : n0 + kTcRows / 2;   // box 1
-  const int m0 = blockIdx.y * kTcTokens;
+  const int m0 = blockIdx.y * BN;
   const int KB = a.K / kTcBlockK;
+  const int kb0 = (int)((long long)KB * blockIdx.z / a.splits);
+  const int kb1 = (int)((long long)KB * (blockIdx.z + 1) / a.splits);
+  const int nk = kb1 - kb0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
-    *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kTcTokens);
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  pdl_wait();
-  const bool halted = a.halt && __ldcg(a.halt);
-
-  if (!halted && warp == 0 && lane == 0) {
-    // producer
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % kTcStages;
-      if (kb >= kTcStages && !mbar_wait(&empty[s], ((kb / kTcStages) & 1) ^ 1, kTcSpin)) {
-        atomicExch(a.err, 1);
-        *abort_flag = 1;
-        break;
-      }
-      uint8_t* st = smem + s * kStageBytes;
-      mbar_expect_tx(&full[s], kStageBytes);
-      const int kx = kb * kTcBlockK;
-      tma_load_2d(st, &wmap, kx, row_a0, &full[s]);
-      tma_load_2d(st + kStageA / 2, &wmap, kx, row_a1, &full[s]);
-      tma_load_2d(st + kStageA, &hmap, kx, m0, &full[s]);
-      tma_load_2d(st + kStageA + kStageB, &lmap, kx, m0, &full[s]);
+  if (warp == 0 && lane == 0) {
+    // producer: weight tiles of the first stages do not depend on the previous
+    // kernel, so they are requested before the dependency wait.
+    const int pre = min(S, nk);
+    for (int i = 0; i < pre; ++i) {
+      uint8_t* st = smem + i * Cfg::kStageBytes;
+      mbar_expect_tx(&full[i], Cfg::kStageBytes);
+      const int kx = (kb0 + i) * kTcBlockK;
+      tma_load_2d(st, &wmap, kx, row_a0, &full[i]);
+      tma_load_2d(st + kStageA / 2, &wmap, kx, row_a1, &full[i]);
     }
-  } else if (!halted && warp == 1 && lane == 0) {
+    pdl_wait();
+    const bool halted = a.halt && __ldcg(a.halt);
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % S;
+      uint8_t* st = smem + s * Cfg::kStageBytes;
+      const int kx = (kb0 + i) * kTcBlockK;
+      if (i >= S) {
+        if (!mbar_wait(&empty[s], ((i / S) & 1) ^ 1, kTcSpin)) {
+          atomicExch(a.err, 1);
+          break;
+        }
+        mbar_expect_tx(&full[s], Cfg::kStageBytes);
+        tma_load_2d(st, &wmap, kx, row_a0, &full[s]);
+        tma_load_2d(st + kStageA / 2, &wmap, kx, row_a1, &full[s]);
+      }
+      // when halted the activation tiles are still fetched (the stage byte
+      // counts must complete) but the epilogue writes nothing
+      (void)halted;
+      tma_load_2d(st + kStageA, &hmap, kx, m0, &full[s]);
+      tma_load_2d(st + kStageA + Cfg::kStageB, &lmap, kx, m0, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
     // MMA issuer
-    constexpr uint32_t idesc = umma_idesc_bf16(kTcRows, kTcTokens);
-    bool ok = true;
-    for (int kb = 0; kb < KB && ok; ++kb) {
-      const int s = kb % kTcStages;
-      if (!mbar_wait(&full[s], (kb / kTcStages) & 1, kTcSpin)) {
+    constexpr uint32_t idesc = umma_idesc_bf16(kTcRows, BN);
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % S;
+      if (!mbar_wait(&full[s], (i / S) & 1, kTcSpin)) {
         atomicExch(a.err, 2);
-        ok = false;
         break;
       }
       tc_fence_after();
-      uint8_t* st = smem + s * kStageBytes;
+      uint8_t* st = smem + s * Cfg::kStageBytes;
       const uint64_t da = umma_desc_sw128(st);
       const uint64_t dh = umma_desc_sw128(st + kStageA);
-      const uint64_t dl = umma_desc_sw128(st + kStageA + kStageB);
+      const uint64_t dl = umma_desc_sw128(st + kStageA + Cfg::kStageB);
 #pragma unroll
       for (int kk = 0; kk < kTcBlockK / 16; ++kk) {
         // +32 bytes per 16-element K step inside the swizzled 128-byte row
-        umma_bf16(tmem, da + 2 * kk, dh + 2 * kk, idesc, (kb | kk) != 0);
+        umma_bf16(tmem, da + 2 * kk, dh + 2 * kk, idesc, (i | kk) != 0);
         umma_bf16(tmem, da + 2 * kk, dl + 2 * kk, idesc, 1u);
       }
       umma_commit(&empty[s]);
     }
     umma_commit(done);  // also fires when nothing was issued
-  } else if (!halted && warp >= 2) {
-    // epilogue: this warp's 32 TMEM lanes = weight rows lane_base..lane_base+31
+  } else if (warp >= 2) {
+    pdl_wait();
+    const bool halted = a.halt && __ldcg(a.halt);
+    // this warp's 32 TMEM lanes = tile rows lane_base..lane_base+31
     const int lane_base = 32 * (warp & 3);
     const bool got = mbar_wait(done, 0, kTcSpin * 4);
     if (!got) atomicExch(a.err, 3);
     tc_fence_after();
-    const int r = lane_base + lane;  // tile row
+    const int r = lane_base + lane;
+    const int cols = min(BN, a.M - m0);
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    bool final_cta = true;
+    if (a.splits > 1) {
+      // partial tile -> workspace; the last CTA of the tile reduces in split order
+      float* part = a.ws + ((long long)tile * a.splits + blockIdx.z) * kTcRows * BN;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        if (c0 >= cols) break;
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0, v);
+#pragma unroll
+        for (int j = 0; j < 16; j += 4)
+          __stcg(reinterpret_cast<float4*>(part + r * BN + c0 + j),
+                 make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (warp == 2 && lane == 0) {
+        const unsigned t = atomicAdd(&a.tickets[tile], 1u);
+        *last_flag = t == (unsigned)a.splits - 1u;
+        if (*last_flag) a.tickets[tile] = 0u;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      final_cta = *last_flag != 0;
+      if (final_cta) __threadfence();
+    }
     float* xbuf = reinterpret_cast<float*>(smem);  // SWIGLU: up rows, after the mainloop
-    const int cols = min(kTcTokens, a.M - m0);
-    for (int c0 = 0; c0 < kTcTokens; c0 += 16) {
-      if (c0 >= cols) break;  // uniform over the warp
+    for (int c0 = 0; final_cta && c0 < BN; c0 += 16) {
+      if (c0 >= cols) break;  // uniform over the epilogue warps
       float v[16];
-      tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0, v);
-      if (!got) continue;
+      if (a.splits > 1) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+        for (int s = 0; s < a.splits; ++s) {
+          const float* part = a.ws + ((long long)tile * a.splits + s) * kTcRows * BN;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            const float4 q = __ldcg(reinterpret_cast<const float4*>(part + r * BN + c0 + j));
+            v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
+          }
+        }
+      } else {
+        tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0, v);
+      }
+      const bool write = got && !halted;
       if (swiglu) {
         if (r >= kTcRows / 2) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) xbuf[(r - kTcRows / 2) * kTcTokens + c0 + j] = v[j];
+          for (int j = 0; j < 16; ++j) xbuf[(r - kTcRows / 2) * BN + c0 + j] = v[j];
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (r < kTcRows / 2) {
+        if (r < kTcRows / 2 && write) {
           const int n = n0 + r;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = m0 + c0 + j;
             if (c0 + j < cols && n < a.N) {
-              const float s = a.rms ? __ldg(a.rms + m) : 1.0f;
-              const float g = v[j] * s, u = xbuf[r * kTcTokens + c0 + j] * s;
+              const float sc = a.rms ? __ldg(a.rms + m) : 1.0f;
+              const float g = v[j] * sc, u = xbuf[r * BN + c0 + j] * sc;
               a.y[(long long)m * a.ldy + n] = g / (1.0f + expf(-g)) * u;
             }
           }
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
-      } else {
+      } else if (write) {
         const int n = n0 + r;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -176,7 +242,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_free(tmem, kTcTokens);
+    tmem_free(tmem, Cfg::kTmemCols);
   }
 }
 
@@ -250,10 +316,10 @@ bool make_map(const void* base, uint64_t inner, uint64_t rows, uint64_t pitch_by
 }  // namespace
 
 bool tc_make_acts(TcActs& a) {
-  return make_map(a.hi, (uint64_t)a.ld, (uint64_t)a.rows_cap, (uint64_t)a.ld * 2, kTcTokens,
-                  &a.hi_map) &&
-         make_map(a.lo, (uint64_t)a.ld, (uint64_t)a.rows_cap, (uint64_t)a.ld * 2, kTcTokens,
-                  &a.lo_map);
+  return make_map(a.hi, (uint64_t)a.ld, (uint64_t)a.rows_cap, (uint64_t)a.ld * 2,
+                  (uint32_t)a.box_rows, &a.hi_map) &&
+         make_map(a.lo, (uint64_t)a.ld, (uint64_t)a.rows_cap, (uint64_t)a.ld * 2,
+                  (uint32_t)a.box_rows, &a.lo_map);
 }
 
 bool tc_weight_map(const __nv_bfloat16* W, int rows, int K, CUtensorMap* out) {
@@ -275,14 +341,17 @@ bool tc_weight_map(const __nv_bfloat16* W, int rows, int K, CUtensorMap* out) {
 
 bool tc_supported(const LinearArgs& a, int epi, const TcActs& acts) {
   if (!acts.hi || a.M > acts.rows_cap || a.K > acts.ld || a.K % kTcBlockK) return false;
+  if (acts.box_rows != 16 && acts.box_rows != 128) return false;
   if (a.ldx % 4 || (reinterpret_cast<uintptr_t>(a.x) & 15)) return false;
-  if (epi == EPI_SWIGLU) return a.N % (kTcRows / 2) == 0;
-  return a.N % (kTcRows / 2) == 0;
+  return a.N % (kTcRows / 2) == 0 && (epi != EPI_SWIGLU || a.N >= kTcRows / 2);
 }
 
 cudaError_t configure_tc_kernels() {
-  return cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)kTcSmem);
+  cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)TcCfg<128>::kSmem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(k_gemm_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)TcCfg<16>::kSmem);
 }
 
 cudaError_t launch_linear_tc(const LinearArgs& a, int epi, const TcActs& acts, int* err,
@@ -291,16 +360,29 @@ cudaError_t launch_linear_tc(const LinearArgs& a, int epi, const TcActs& acts, i
   const int w_rows = epi == EPI_SWIGLU ? 2 * a.N : a.N;
   CUtensorMap wmap;
   if (!tc_weight_map(a.W, w_rows, a.K, &wmap)) return cudaErrorInvalidValue;
-  k_split_rows<<<a.M, 256, 0, stream>>>(a.x, a.ldx, a.gamma, a.eps, a.K, acts.hi, acts.lo, acts.ld,
-                                        acts.rms, a.halt);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch(k_split_rows, dim3(a.M), dim3(256), 0, stream, a.x, a.ldx, a.gamma,
+                         a.eps, a.K, acts.hi, acts.lo, acts.ld, acts.rms, a.halt);
   if (e != cudaSuccess) return e;
-  TcArgs t{a.M, a.N, a.K, epi, a.N, a.y, a.ldy, a.resid, a.ldr, a.bias,
-           a.gamma ? acts.rms : nullptr, err, a.halt};
+  const int BN = acts.box_rows;
   const int cols_per_cta = epi == EPI_SWIGLU ? kTcRows / 2 : kTcRows;
-  dim3 grid((a.N + cols_per_cta - 1) / cols_per_cta, (a.M + kTcTokens - 1) / kTcTokens);
-  k_gemm_tc<<<grid, kTcThreads, kTcSmem, stream>>>(wmap, acts.hi_map, acts.lo_map, t);
-  return cudaGetLastError();
+  dim3 grid((a.N + cols_per_cta - 1) / cols_per_cta, (a.M + BN - 1) / BN, 1);
+  // split K so that a skinny GEMM still spreads over the SMs (deterministic
+  // reduction by the last CTA of each tile)
+  int splits = 1;
+  const int tiles = (int)(grid.x * grid.y);
+  if (acts.ws && tiles < acts.sm_count) {
+    splits = std::min(acts.sm_count / tiles, (a.K / kTcBlockK) / 4);
+    splits = std::max(1, std::min(splits, acts.max_splits));
+    while (splits > 1 && (size_t)tiles * splits * kTcRows * BN > acts.ws_floats) --splits;
+  }
+  grid.z = splits;
+  TcArgs t{a.M, a.N, a.K, epi, a.N, a.y, a.ldy, a.resid, a.ldr, a.bias,
+           a.gamma ? acts.rms : nullptr, err, a.halt, splits, acts.ws, acts.tickets};
+  if (BN == 16)
+    return launch(k_gemm_tc<16>, grid, dim3(kTcThreads), TcCfg<16>::kSmem, stream, wmap,
+                  acts.hi_map, acts.lo_map, t);
+  return launch(k_gemm_tc<128>, grid, dim3(kTcThreads), TcCfg<128>::kSmem, stream, wmap,
+                acts.hi_map, acts.lo_map, t);
 }
 
 }  // namespace qtts

@@ -14,7 +14,6 @@ namespace qtts {
 
 constexpr int kTcBlockK = 64;     // K per stage: one 128-byte swizzle row of bf16
 constexpr int kTcRows = 128;      // weight rows per CTA (MMA M)
-constexpr int kTcTokens = 128;    // activation rows per CTA (MMA N)
 
 // Split activations: hi/lo bf16 [rows, ld] of gamma * x, and rms[m] (1 when no gamma).
 struct TcActs {
@@ -23,7 +22,14 @@ struct TcActs {
   float* rms;
   int rows_cap;   // rows allocated
   int ld;         // row pitch in elements (>= every K used)
-  CUtensorMap hi_map, lo_map;  // box: 64 elements x kTcTokens rows
+  int box_rows;   // activation rows per CTA tile (MMA N): 128 (prefill) or 16 (batched decode)
+  CUtensorMap hi_map, lo_map;  // box: 64 elements x box_rows rows
+  // optional split-K workspace (skinny GEMMs): partial tiles and per-tile tickets
+  float* ws;
+  size_t ws_floats;
+  unsigned* tickets;
+  int max_splits;
+  int sm_count;
 };
 
 // Host: builds the maps of an activation buffer pair; false if the driver

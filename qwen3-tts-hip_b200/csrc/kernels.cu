@@ -443,32 +443,19 @@ __global__ void __launch_bounds__(kThreads) k_gemv1(LinearArgs a, int epi) {
   gemv1_body<KCH, NR>(a, epi, xs, nullptr);
 }
 
-// Head: final/group RMSNorm + LM head GEMV over all CTAs; the last CTA to
-// finish applies penalty/suppression, selects the token and performs the
-// gathers the next stage needs (so no logits or tokens visit the host).
-template <int KCH>
-__global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
-  extern __shared__ float4 dyn4[];
-  float* smem = reinterpret_cast<float*>(dyn4);
-  __shared__ float s_inv[1];
-  __shared__ bool s_last;
+// Token selection and the gathers the next stage needs, for one sequence:
+// penalty / suppression, selection, then (talker roles) the CodePredictor
+// prefix and halt on EOS, or (CodePredictor groups) the next group input,
+// the embedding sum, codes and, after the last group, the talker step input.
+// `inv` is the RMS scale of the head input row `a.lin.x`.
+__device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* logits, float inv,
+                                                float* smem) {
   __shared__ int s_frame, s_sem;
-  if (!gemv1_body<KCH, 1>(a.lin, EPI_STORE, smem, s_inv)) return;
-  __syncthreads();  // the selector reuses the staged activation buffer
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!s_last) return;
-  if (threadIdx.x == 0) *a.ticket = 0u;
-  __threadfence();
-  if (a.role == ROLE_LOGITS_ONLY) return;
 
-  trace_mark(a.lin.trace_id, 4);
   const int V = a.lin.N;
   Selector<SyncBlock> sel{smem, reinterpret_cast<int*>(smem + kSelMaxVocab)};
   const int tid = threadIdx.x;
-  for (int v = tid; v < V; v += kThreads) sel.val[v] = __ldcg(a.lin.y + v);
+  for (int v = tid; v < V; v += kThreads) sel.val[v] = __ldcg(logits + v);
   if (tid == 0) { s_frame = a.st->frames; s_sem = a.st->semantic; }
   __syncthreads();
   if (a.role == ROLE_TALKER_STEP)
@@ -482,11 +469,9 @@ __global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
     a.st->rng_counter = rng.counter;
   }
   if (a.token_out && tid == 0) *a.token_out = tok;
-  trace_mark(a.lin.trace_id, 5);
 
   const int H = a.H;
   if (a.role == ROLE_TALKER_PREFILL || a.role == ROLE_TALKER_STEP) {
-    const float inv = s_inv[0];
     const float* x = a.lin.x;
     const float* g = a.lin.gamma;
     const __nv_bfloat16* e = a.talker_codec_emb + (long long)tok * H;
@@ -524,7 +509,53 @@ __global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
       }
     }
   }
-  trace_mark(a.lin.trace_id, 2);
+}
+
+// Head: final/group RMSNorm + LM head GEMV over all CTAs; the last CTA to
+// finish selects the token (head_select_act), so no logits or tokens visit
+// the host.
+template <int KCH>
+__global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
+  extern __shared__ float4 dyn4[];
+  float* smem = reinterpret_cast<float*>(dyn4);
+  __shared__ float s_inv[1];
+  __shared__ bool s_last;
+  if (!gemv1_body<KCH, 1>(a.lin, EPI_STORE, smem, s_inv)) return;
+  __syncthreads();  // the selector reuses the staged activation buffer
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  if (threadIdx.x == 0) *a.ticket = 0u;
+  __threadfence();
+  if (a.role == ROLE_LOGITS_ONLY) return;
+  trace_mark(a.lin.trace_id, 4);
+  head_select_act(a, a.lin.y, s_inv[0], smem);
+  trace_mark(a.lin.trace_id, 5);
+}
+
+// Batched heads: the logits of B sequences come from one tensor-core
+// projection; CTA b selects sequence b's token (skipped once it has halted).
+__global__ void __launch_bounds__(kThreads) k_select_batch(BatchHeadArgs bh) {
+  extern __shared__ float4 dyn4[];
+  float* smem = reinterpret_cast<float*>(dyn4);
+  pdl_wait();
+  const int b = blockIdx.x;
+  HeadArgs a = bh.h;
+  a.st += b;
+  if (__ldcg(&a.st->halt)) return;
+  a.history += (long long)b * bh.hist_stride;
+  a.history_out += (long long)b * bh.hist_stride;
+  a.codes += (long long)b * bh.codes_stride;
+  if (a.cp_prefix) a.cp_prefix += (long long)b * 2 * a.H;
+  a.lin.x += (long long)b * a.lin.ldx;
+  if (a.cp_next) a.cp_next += (long long)b * bh.next_stride;
+  if (a.emb_sum) a.emb_sum += (long long)b * a.H;
+  if (a.step_in) a.step_in += (long long)b * bh.step_stride;
+  if (a.trailing) a.trailing += (long long)b * bh.trail_stride;
+  a.token_out = nullptr;
+  head_select_act(a, bh.logits + (long long)b * bh.logits_ld, __ldcg(bh.rms + b), smem);
 }
 
 // ---------------------------------------------------------------------------
@@ -548,10 +579,14 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
   pdl_wait();
   trace_mark(a.trace_id, 1);
   // halt, position and the projections are independent loads: issue together
-  const int halted = a.halt ? __ldcg(a.halt) : 0;
+  const int seq = blockIdx.y;
+  const int halted = a.halt ? __ldcg(a.halt + seq * a.halt_stride) : 0;
   const int h = blockIdx.x, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int pos = a.pos_ptr ? __ldcg(a.pos_ptr) : a.pos_const;
+  const int pos = a.pos_ptr ? __ldcg(a.pos_ptr + seq * a.pos_stride) : a.pos_const;
+  a.qkv += (long long)seq * a.qkv_ld;
+  a.out += (long long)seq * a.out_ld;
+  a.kv.page_table += (long long)seq * a.pt_stride;
   const int T = pos + 1;
   const int kvh = a.kv.kv_heads;
   const int q_out = a.q_heads * kHeadDim, kv_out = kvh * kHeadDim;
@@ -814,21 +849,6 @@ __global__ void k_assemble_rows(const float* proj, const int* proj_index,
 }
 
 // ---------------------------------------------------------------------------
-template <typename... KArgs, typename... Args>
-cudaError_t launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                   Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k, args...);
-}
 
 constexpr size_t kLinearSmem = sizeof(float) * (size_t)kXFloats;
 constexpr size_t kHeadSmem = sizeof(float) * 2 * (size_t)kMaxVocab;  // selector scratch
@@ -945,6 +965,7 @@ cudaError_t configure_kernels() {
   if ((e = cudaFuncSetAttribute(k_head<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(k_head<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(k_head<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(k_select_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem)) != cudaSuccess) return e;
   return cudaFuncSetAttribute(k_head<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem);
 }
 
@@ -967,12 +988,17 @@ cudaError_t set_step_trace(unsigned long long* buf, int capacity, cudaStream_t s
   return cudaMemcpyToSymbolAsync(g_trace, &t, sizeof(t), 0, cudaMemcpyHostToDevice, stream);
 }
 
+cudaError_t launch_select_batch(const BatchHeadArgs& a, int B, cudaStream_t stream) {
+  if (a.h.lin.N > kMaxVocab) return cudaErrorInvalidValue;
+  return launch(k_select_batch, dim3(B), dim3(kThreads), kHeadSmem, stream, a);
+}
+
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t stream) {
   const int G = a.q_heads / a.kv.kv_heads;
   // Fixed positions (CodePredictor, <= 17 rows): 4 warps; a position read on
   // the device (talker): 16 warps (8 with four q heads per kv head).
   const bool small = !a.pos_ptr && a.pos_const < 4 * 4 * kAttnBatch;
-  dim3 grid(a.kv.kv_heads);
+  dim3 grid(a.kv.kv_heads, std::max(1, a.batch));
 #define QTTS_ATTN(GG)                                                                    \
   return small ? launch(k_attn_decode<GG, 4>, grid, dim3(128), 0, stream, a)             \
                : launch(k_attn_decode<GG, (GG > 2 ? 8 : 16)>, grid,              \

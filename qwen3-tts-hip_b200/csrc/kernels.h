@@ -105,6 +105,16 @@ struct HeadArgs {
   int* token_out;          // optional: selected token
 };
 
+// Batched heads: per-sequence views of `h` at the given element strides;
+// `rms` holds each sequence's RMS scale of its head input row.
+struct BatchHeadArgs {
+  HeadArgs h;
+  const float* logits;     // [B, logits_ld]
+  int logits_ld;
+  const float* rms;        // [B]
+  long long hist_stride, codes_stride, next_stride, step_stride, trail_stride;
+};
+
 struct AttnDecodeArgs {
   const float* qkv;        // raw projections of the current position [q_out + 2 kv_out]
   const float* q_gamma;
@@ -124,6 +134,11 @@ struct AttnDecodeArgs {
   int nsplit;
   const int* halt;
   int trace_id;
+  // Batched decode (sequence b = blockIdx.y; all zero for one sequence):
+  // element strides between sequences of qkv rows and output rows, int
+  // strides of the position and halt words, and page-table entries per sequence.
+  int qkv_ld, out_ld, pos_stride, halt_stride, pt_stride;
+  int batch;               // sequences (0 or 1: one)
 };
 
 struct QkPrepArgs {
@@ -162,6 +177,7 @@ cudaError_t launch_head(const HeadArgs& a, cudaStream_t stream);
 bool attn_o_fusable(const AttnDecodeArgs& at, const LinearArgs& o);
 cudaError_t launch_attn_o(const AttnDecodeArgs& at, const LinearArgs& o, cudaStream_t stream);
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t stream);
+cudaError_t launch_select_batch(const BatchHeadArgs& a, int B, cudaStream_t stream);
 // Step trace buffer: [6][capacity] u64 globaltimer values (first entry, first
 // post-wait, last exit, last post-wait, head selection start/end) indexed by
 // trace_id; nullptr disables. Stream-ordered.

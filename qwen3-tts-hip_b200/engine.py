@@ -17,7 +17,7 @@ import ctypes as C
 import os
 from dataclasses import dataclass, field
 from pathlib import Path
-from typing import Optional, Sequence
+from typing import List, Optional, Sequence
 
 import numpy as np
 
@@ -102,6 +102,7 @@ SIGNATURES = {
     "qtts_engine_destroy": (None, [_P]),
     "qtts_engine_get_info": (C.c_int32, [_P, C.POINTER(_Info)]),
     "qtts_generate_codes_from_ids": (C.c_int32, [_P, _U32, C.c_size_t, C.POINTER(_Options), _I32, C.c_size_t, _SZ, _I32]),
+    "qtts_generate_codes_batch_from_ids": (C.c_int32, [_P, _U32, _SZ, C.c_size_t, C.POINTER(_Options), _I32, C.c_size_t, _SZ, _I32]),
     "qtts_generate_voice_clone_codes_from_ids": (C.c_int32, [_P, _U32, C.c_size_t, _F, C.POINTER(_Options), _I32, C.c_size_t, _SZ, _I32]),
     "qtts_generate_codes_from_rows": (C.c_int32, [_P, _F, C.c_size_t, _F, C.c_size_t, _F, C.POINTER(_Options), _I32, C.c_size_t, _SZ, _I32]),
     "qtts_prepare_inputs_from_ids": (C.c_int32, [_P, _U32, C.c_size_t, C.c_size_t, C.c_char_p, C.c_char_p, _F, _SZ, _F, _SZ, _F]),
@@ -322,6 +323,32 @@ class HipTtsEngine:
             out.ctypes.data_as(_I32), out.size, C.byref(frames), C.byref(ended)))
         n = frames.value * self.code_groups
         return GeneratedCodes(out[:n].tolist(), frames.value, bool(ended.value))
+
+    def generate_codes_batch_from_ids(self, requests: Sequence[Sequence[int]],
+                                      options: Sequence[GenerateOptions]) -> List[GeneratedCodes]:
+        """Batched serving (no reference counterpart): up to 16 requests
+        generated together; options may differ only in seed, speaker and
+        language. Returns one GeneratedCodes per request."""
+        reqs = [_ids(r) for r in requests]
+        if len(options) != len(reqs):
+            raise InvalidInput(ERR_INVALID_INPUT, "one GenerateOptions per request")
+        ids = np.concatenate(reqs) if reqs else np.zeros(0, np.uint32)
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        lens = np.array([r.size for r in reqs], dtype=np.uintp)
+        opts = (_Options * len(reqs))(*[o._c() for o in options])
+        cap = max(1, max((o.max_frames for o in options), default=1)) * self.code_groups
+        out = np.zeros(len(reqs) * cap, dtype=np.int32)
+        frames = np.zeros(len(reqs), dtype=np.uintp)
+        ended = np.zeros(len(reqs), dtype=np.int32)
+        _check(lib().qtts_generate_codes_batch_from_ids(
+            self._h, ids.ctypes.data_as(_U32), lens.ctypes.data_as(_SZ), len(reqs), opts,
+            out.ctypes.data_as(_I32), cap, frames.ctypes.data_as(_SZ), ended.ctypes.data_as(_I32)))
+        res = []
+        for b in range(len(reqs)):
+            n = int(frames[b]) * self.code_groups
+            res.append(GeneratedCodes(out[b * cap: b * cap + n].tolist(), int(frames[b]),
+                                      bool(ended[b])))
+        return res
 
     def generate_voice_clone_codes_from_ids(self, content_ids, speaker_embedding,
                                             options: Optional[GenerateOptions] = None) -> GeneratedCodes:
