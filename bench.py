@@ -41,6 +41,16 @@ CONFIGS = {
     "1.7b-greedy": dict(shape="1.7b", n_ids=128, frames=240, do_sample=False, top_k=50, top_p=1.0,
                         temperature=0.9, penalty=1.0, sub_sample=False, sub_top_k=50,
                         sub_temperature=0.9, rng="lcg"),
+    # streaming text, 8-id pushes to 256 ids, generation starts
+    # after 1 id (text_lookahead 1), 6-frame code chunks up to 480 frames
+    "0.6b-stream": dict(shape="0.6b", n_ids=256, stream=True, push=8, chunk=6, frames=480,
+                        do_sample=True, top_k=50, top_p=1.0, temperature=0.9, penalty=1.05,
+                        sub_sample=True, sub_top_k=50, sub_temperature=0.9, rng="philox"),
+    # batched serving, 16 concurrent requests per GPU,
+    # prompt lengths uniform in [16, 256], config-1 sampling, seed = request index
+    "1.7b-batch16": dict(shape="1.7b", n_ids=(16, 256), batch=16, frames=240, do_sample=True,
+                         top_k=50, top_p=1.0, temperature=0.9, penalty=1.05, sub_sample=True,
+                         sub_top_k=50, sub_temperature=0.9, rng="philox"),
 }
 FRAME_SECONDS = 0.08
 
@@ -58,10 +68,11 @@ def model_dir(shape: str) -> Path:
     return base / shape
 
 
-def frame_bytes(shape_name: str, P: int, frames: int) -> float:
-    """Algorithmic HBM bytes of one average frame: every weight read once per
-    pass (talker step once, CodePredictor layers + head once per group pass),
-    plus the talker KV cache read (positions 0..pos) and append, all bf16."""
+def frame_bytes(shape_name: str, P: int, frames: int, batch: int = 1) -> float:
+    """Algorithmic HBM bytes of one average (batch) frame: every weight read
+    once per pass (talker step once, CodePredictor layers + head once per group
+    pass) for the whole batch, plus each sequence's talker KV cache read
+    (positions 0..pos) and append, all bf16."""
     from oracle import synth
 
     s = synth.SHAPES[shape_name]
@@ -73,7 +84,7 @@ def frame_bytes(shape_name: str, P: int, frames: int) -> float:
     talker = s.layers * layer(s.hidden, s.intermediate) + 2 * s.vocab * s.hidden
     kv_per_pos = 2 * s.layers * 2 * kv_out  # K and V, bf16
     avg_pos = P + (frames - 1) / 2.0 + 1
-    talker += kv_per_pos * (avg_pos + 1)
+    talker += kv_per_pos * (avg_pos + 1) * batch
     cp_pass = s.cp_layers * layer(s.cp_hidden, s.cp_intermediate) + 2 * s.cp_vocab * s.cp_hidden
     if s.cp_hidden != s.hidden:
         cp_pass += 2 * s.cp_hidden * s.hidden
@@ -219,8 +230,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     metric = "codec_frames_per_s"
+    batch = c.get("batch", 1)
     workload = {"workload": f"{args.config}: {c['shape']}-shaped talker+CodePredictor, "
-                            f"{c['n_ids']} random text ids, {c['frames']} frames, batch 1 per GPU",
+                            f"{c['n_ids']} random text ids, {c['frames']} frames, "
+                            f"batch {batch} per GPU",
                 "shape": c["shape"], "frames_per_request": c["frames"], "text_ids": c["n_ids"],
                 "sampling": "top_k=50 T=0.9 penalty=1.05, subtalker top_k=50 T=0.9"
                 if c["do_sample"] else "greedy", "rng": c["rng"],
@@ -230,8 +243,16 @@ def main():
     from oracle import synth
 
     mdir = model_dir(c["shape"])
-    ids = np.random.default_rng(0).integers(0, synth.SHAPES[c["shape"]].text_vocab - 1000,
-                                            c["n_ids"]).astype(np.uint32)
+    vocab = synth.SHAPES[c["shape"]].text_vocab - 1000
+    rng0 = np.random.default_rng(0)
+    if batch > 1:
+        lo, hi = c["n_ids"]
+        reqs = [rng0.integers(0, vocab, int(rng0.integers(lo, hi + 1))).astype(np.uint32)
+                for _ in range(batch)]
+        ids = reqs[0]
+    else:
+        reqs = None
+        ids = rng0.integers(0, vocab, c["n_ids"]).astype(np.uint32)
 
     if args.impl == "reference":
         if rank != 0:
@@ -271,8 +292,55 @@ def main():
 
     eng = pkg.HipTtsEngine.load_with_options(mdir, pkg.EngineOptions(local, 512))
     opts = options(pkg, c, seed=rank)
+    if reqs is not None:
+        bopts = [options(pkg, c, seed=b) for b in range(batch)]
+
+    stream_stats = []
+
+    def run_stream():
+        """One streamed request: text pushed 8 ids at a time whenever the
+        stream asks for more, codes pulled in 6-frame chunks. Records the time
+        to the first chunk and the steady-state RTF after it (host wall clock,
+        everything through the public API)."""
+        ts = eng.start_text_stream_polling(
+            opts, pkg.TextStreamOptions(min_start_tokens=1, min_resume_tokens=1))
+        pos, frames, first, t_first = 0, 0, None, None
+        t0 = time.perf_counter()
+        ts.push_ids(ids[pos:pos + c["push"]])
+        pos += c["push"]
+        while True:
+            r = ts.next_codes_chunk(c["chunk"])
+            if isinstance(r, pkg.NeedMoreText):
+                if pos < len(ids):
+                    ts.push_ids(ids[pos:pos + c["push"]])
+                    pos += c["push"]
+                else:
+                    ts.finish_text()
+                continue
+            if isinstance(r, pkg.Finished) or r is None:
+                break
+            frames += r.frames
+            if first is None:
+                t_first, first = time.perf_counter(), r.frames
+        t_end = time.perf_counter()
+        out = ts.finish_codes()
+        ts.close()
+        stream_stats.append({"ttfc_ms": 1e3 * (t_first - t0),
+                             "steady_rtf": (t_end - t_first) / max(1, (frames - first)) / FRAME_SECONDS,
+                             "frames": frames, "wall_s": t_end - t0})
+        return out
+
+    def run_step():
+        if c.get("stream"):
+            return run_stream()
+        if reqs is None:
+            return eng.generate_codes_from_ids(ids, opts)
+        outs = eng.generate_codes_batch_from_ids(reqs, bopts)
+        return type(outs[0])(sum((o.codes for o in outs), []), sum(o.frames for o in outs),
+                             all(o.ended_by_eos for o in outs))
+
     for _ in range(args.warmup):
-        eng.generate_codes_from_ids(ids, opts)
+        run_step()
 
     dev_ms, wall_s, frames, launches, last = 0.0, 0.0, 0, 0, None
     if world > 1:
@@ -281,9 +349,14 @@ def main():
     with ClockSampler(local) as clk:
         for _ in range(args.steps):
             t0 = time.perf_counter()
-            out = eng.generate_codes_from_ids(ids, opts)
+            out = run_step()
             wall_s += time.perf_counter() - t0
             tm = eng.last_timings()
+            if c.get("stream"):
+                # a stream interleaves host polling with device bursts: its
+                # time is the wall clock of the whole stream
+                tm = dict(tm, prefill_ms=0.0, frames_ms=1e3 * (time.perf_counter() - t0),
+                          frames=out.frames)
             dev_ms += tm["prefill_ms"] + tm["frames_ms"]
             frames += out.frames
             launches += tm["kernels"]
@@ -299,12 +372,28 @@ def main():
     ms_k, bytes_k = eng.profile_projection(0, 280)
     peaks, peak_kind = measured_peaks()
     achieved = bytes_k / (ms_k * 1e-3) / 1e9
-    P = 9 + c["n_ids"]
+    P = 9 + (int(np.mean([r.size for r in reqs])) if reqs is not None else c["n_ids"])
     out, tm = last
-    fb = frame_bytes(c["shape"], P, c["frames"])
-    frame_ms = tm["frames_ms"] / max(1, tm["frames"])
+    # one batch frame reads every weight once for all `batch` sequences, plus each one's KV
+    fb = frame_bytes(c["shape"], P, c["frames"], batch)
+    frame_ms = tm["frames_ms"] / max(1, tm["frames"]) * batch
     frame_gbs = fb / (frame_ms * 1e-3) / 1e9
 
+    if batch > 1:
+        # batched serving: the batch frame (all tcgen05 projections at M=batch,
+        # attention and selection) against HBM, weights read once per batch frame
+        roofline = {"bound": "hbm", "kernel": f"batch frame (tcgen05 projections at M={batch}, "
+                                              f"attention, selection)",
+                    "achieved": frame_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": frame_gbs / peaks["hbm_gbs"], "peak_kind": peak_kind,
+                    "bytes_per_launch": fb, "ms_per_launch": frame_ms, "traffic": None}
+    else:
+        roofline = {"bound": "hbm",
+                    "kernel": "k_gemv1<4,2> talker gate|up + SwiGLU (1024->2x3072), RMSNorm prologue",
+                    "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind,
+                    "bytes_per_launch": bytes_k, "ms_per_launch": ms_k,
+                    "traffic": committed_traffic()}
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -316,19 +405,15 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init N(0,0.02) bf16 weights, seed 0; random text ids)",
-        "rtf": (dev_ms_max / 1000.0) / (frames_all / world * FRAME_SECONDS),
+        "rtf": (dev_ms_max / 1000.0) / (frames_all / world / batch * FRAME_SECONDS),
         "frames_per_step": frames_all / world / args.steps,
         "config": workload,
         "e2e": {"value": e2e, "unit": "frames/s",
-                "rtf": wall_max / (frames_all / world * FRAME_SECONDS),
-                "h2d_bytes_per_step": int(ids.nbytes),
+                "rtf": wall_max / (frames_all / world / batch * FRAME_SECONDS),
+                "h2d_bytes_per_step": int(sum(r.nbytes for r in reqs) if reqs else ids.nbytes),
                 "d2h_bytes_per_step": int(out.frames * 16 * 4 + 64)},
         "gpu_launches": launches_all,
-        "roofline": {"bound": "hbm", "kernel": "k_gemv1<4,2> talker gate|up + SwiGLU (1024->2x3072), RMSNorm prologue",
-                     "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind,
-                     "bytes_per_launch": bytes_k, "ms_per_launch": ms_k,
-                     "traffic": committed_traffic()},
+        "roofline": roofline,
         "frame_roofline": {"bytes_per_frame": fb, "ms_per_frame": frame_ms,
                            "achieved": frame_gbs, "unit": "GB/s",
                            "frac": frame_gbs / peaks["hbm_gbs"], "peak_kind": peak_kind,
@@ -336,6 +421,13 @@ def main():
         "clocks": clk.summary(),
         "prefill_ms": tm["prefill_ms"],
     }
+    if stream_stats:
+        st_last = stream_stats[-len(stream_stats) // 2:] if len(stream_stats) > 1 else stream_stats
+        line["streaming"] = {
+            "ttfc_ms": statistics.median(x["ttfc_ms"] for x in stream_stats[args.warmup:] or stream_stats),
+            "steady_rtf": statistics.median(x["steady_rtf"] for x in stream_stats[args.warmup:] or stream_stats),
+            "frames_per_stream": stream_stats[-1]["frames"],
+            "note": "host wall clock through the polling text-stream API; chunks of 6 frames"}
     if world == 1 and not args.no_cpu_baseline:
         fps, cf, total, cores, _ = cpu_reference_run(c, mdir, ids, args.cpu_frames, 1, 0)
         line["cpu_baseline"] = {"value": fps, "unit": "frames/s", "cores": cores, "kind": "port",

@@ -694,6 +694,14 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
       tc.hi = arena.alloc<__nv_bfloat16>((size_t)tc.rows_cap * ld);
       tc.lo = arena.alloc<__nv_bfloat16>((size_t)tc.rows_cap * ld);
       tc.rms = arena.alloc<float>((size_t)tc.rows_cap);
+      // split-K for prefill GEMMs with few 128 x 128 tiles (short prompts)
+      int sms = 148;
+      QCK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+      tc.sm_count = sms;
+      tc.max_splits = 8;
+      tc.ws_floats = (size_t)sms * 128 * 128;
+      tc.ws = arena.alloc<float>(tc.ws_floats);
+      tc.tickets = arena.alloc<unsigned>(4096);
       tc_err = arena.alloc<int>(1);
       QCK(cudaMemset(tc_err, 0, sizeof(int)));
       if (!tc_make_acts(tc)) tc = TcActs{};

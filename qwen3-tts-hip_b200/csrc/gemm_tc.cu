@@ -189,15 +189,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (c0 >= cols) break;  // uniform over the epilogue warps
       float v[16];
       if (a.splits > 1) {
+        // sum the partial tiles in split order; four splits' loads in flight at once
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = 0.f;
-        for (int s = 0; s < a.splits; ++s) {
-          const float* part = a.ws + ((long long)tile * a.splits + s) * kTcRows * BN;
+        const float* base = a.ws + (long long)tile * a.splits * kTcRows * BN + r * BN + c0;
+        for (int s0 = 0; s0 < a.splits; s0 += 4) {
+          float4 q[4][4];
 #pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            const float4 q = __ldcg(reinterpret_cast<const float4*>(part + r * BN + c0 + j));
-            v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
-          }
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              q[u][j] = s0 + u < a.splits
+                            ? __ldcg(reinterpret_cast<const float4*>(
+                                  base + (long long)(s0 + u) * kTcRows * BN + 4 * j))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              v[4 * j] += q[u][j].x; v[4 * j + 1] += q[u][j].y;
+              v[4 * j + 2] += q[u][j].z; v[4 * j + 3] += q[u][j].w;
+            }
         }
       } else {
         tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0, v);
