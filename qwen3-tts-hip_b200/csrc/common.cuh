@@ -88,6 +88,21 @@ __device__ __forceinline__ __nv_bfloat16* kv_ptr(const KvView& v, int layer, int
          ((long long)((kind * v.kv_heads + head) << v.page_shift) + inpage) * kHeadDim;
 }
 
+// Debugging aid (QTTS_CRUMBS=1): each kernel's first thread records its id in
+// mapped host memory at entry ([0]) and exit ([1]), so after a device fault
+// the host can still tell which kernel was running. Null when off.
+struct Crumbs {
+  volatile unsigned* p;
+};
+#define QTTS_CRUMB(slot, id)                                                         \
+  do {                                                                               \
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 &&  \
+        g_crumbs.p) {                                                                \
+      g_crumbs.p[slot] = (unsigned)(id);                                             \
+      __threadfence_system();                                                        \
+    }                                                                                \
+  } while (0)
+
 // Kernel launch with programmatic dependent launch allowed (the kernel's
 // griddepcontrol.wait orders it after its predecessor; work before the wait
 // may overlap the predecessor's tail).

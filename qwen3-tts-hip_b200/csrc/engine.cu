@@ -309,7 +309,7 @@ class Engine {
   // row gets identical arithmetic however the rows are batched (one-shot vs
   // streamed prompts): the talker prefill and the text MLP always, the
   // CodePredictor's 2-row prefill only with QTTS_TC_CP=1.
-  TcActs tc{};
+  TcPlan tc{};  // tokens == 0: unavailable
   int* tc_err = nullptr;
   bool tc_scope = false;
   bool tc_cp = false;
@@ -355,9 +355,9 @@ class Engine {
               float* y, int ldy, const float* resid, int ldr, const float* bias, int M, int N,
               int K, Epilogue epi, const int* halt) {
     LinearArgs a{W, x, ldx, gamma, eps, y, ldy, resid, ldr, bias, M, N, K, halt};
-    if (tc_scope && tc_supported(a, epi, tc)) {
-      QCK(launch_linear_tc(a, epi, tc, tc_err, stream));  // split + tcgen05 GEMM
-      launches += 2;
+    if (tc_scope && tc.tokens && tc_supported(a, epi, tc)) {
+      QCK(launch_linear_tc(a, epi, tc, nullptr, tc_err, stream));  // tcgen05 GEMM
+      launches += 1;
       return;
     }
     static const char* kEpi[] = {"gemv", "gemv+resid", "gemv+swiglu", "gemv+bias", "gemv+bias+silu"};
@@ -394,6 +394,7 @@ class Engine {
   // measured faster than at entry (0), which floods the memory queues with
   // weight loads of several launches at once. QTTS_TRIGGER overrides.
   int trigger_mode = 1;
+  unsigned* crumbs_host = nullptr;  // QTTS_CRUMBS=1: last kernel ids entered / left
   size_t pf_ahead = 0;                          // QTTS_L2_PREFETCH=<MB> enables
   int pf_mode = 0;                              // 0 off, 1 record, 2 apply
   std::vector<std::pair<const char*, size_t>> pf_ops;
@@ -449,7 +450,8 @@ class Engine {
     StackBufs tb{}, cb{};
     KvView tkv{}, ckv{};
     int pages = 0;  // talker KV pages per sequence
-    TcActs acts{};
+    TcPlan plan{};
+    float* rms = nullptr;  // [cap] RMS scale of each head input row
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};  // prefill start, frames start, end
   } bt;
   std::map<std::pair<SampleKey, int>, cudaGraphExec_t> batch_graphs;
@@ -457,7 +459,7 @@ class Engine {
   void ensure_batch();
   void blinear(const __nv_bfloat16* W, const float* x, int ldx, const float* gamma, float eps,
                float* y, int ldy, const float* resid, int ldr, const float* bias, int M, int N,
-               int K, Epilogue epi);
+               int K, Epilogue epi, float* rms_out = nullptr);
   void batch_stack_step(DevStack& S, StackBufs& B, const KvView& kv, int pt_stride,
                         const int* pos_ptr, int pos_const, int nb);
   void batch_head(int role, int group, const float* x, const SampleCfg& c, float penalty, int nb);
@@ -683,28 +685,18 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
     // split activations for the tcgen05 projections of many rows (prefill, text MLP)
     const char* tz = std::getenv("QTTS_TC");
     if (const char* tcp = std::getenv("QTTS_TC_CP")) tc_cp = tcp[0] == '1';
-    if (!(tz && tz[0] == '0')) {
-      int ld = std::max({T.hidden, T.q_heads * T.head_dim, T.intermediate, C.hidden,
-                         C.q_heads * C.head_dim, C.intermediate});
-      if (text_hidden) ld = std::max({ld, text_hidden, text_inter});
-      ld = (ld + 63) / 64 * 64;
-      tc.rows_cap = rows + 16;
-      tc.ld = ld;
-      tc.box_rows = 128;
-      tc.hi = arena.alloc<__nv_bfloat16>((size_t)tc.rows_cap * ld);
-      tc.lo = arena.alloc<__nv_bfloat16>((size_t)tc.rows_cap * ld);
-      tc.rms = arena.alloc<float>((size_t)tc.rows_cap);
-      // split-K for prefill GEMMs with few 128 x 128 tiles (short prompts)
+    if (!(tz && tz[0] == '0') && tc_available()) {
+      // split-K workspace for prefill GEMMs with few 128 x 128 tiles (short prompts)
       int sms = 148;
       QCK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+      tc.tokens = 128;
       tc.sm_count = sms;
       tc.max_splits = 8;
-      tc.ws_floats = (size_t)sms * 128 * 128;
+      tc.ws_floats = tc_workspace_floats(128, sms);
       tc.ws = arena.alloc<float>(tc.ws_floats);
       tc.tickets = arena.alloc<unsigned>(4096);
       tc_err = arena.alloc<int>(1);
       QCK(cudaMemset(tc_err, 0, sizeof(int)));
-      if (!tc_make_acts(tc)) tc = TcActs{};
     }
   }
   tb = alloc_bufs(arena, talker, rows);
@@ -764,6 +756,13 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
     if (const char* tp = std::getenv("QTTS_STEP_TRACE")) {
       step_trace_path = tp;
       step_trace = arena.alloc<unsigned long long>(6 * (size_t)kTraceCap);
+    }
+    if (const char* cr = std::getenv("QTTS_CRUMBS"); cr && cr[0] == '1') {
+      QCK(cudaHostAlloc(&crumbs_host, 64, cudaHostAllocMapped));
+      unsigned* d = nullptr;
+      QCK(cudaHostGetDevicePointer(&d, crumbs_host, 0));
+      QCK(set_crumbs_kernels(d));
+      QCK(set_crumbs_gemm(d));
     }
     if (const char* tg = std::getenv("QTTS_TRIGGER")) trigger_mode = std::atoi(tg);
     if (const char* pa = std::getenv("QTTS_L2_PREFETCH"))
@@ -1423,7 +1422,7 @@ void Engine::dump_step_trace() {
 // ---- batched serving -------------------------------------------------------
 void Engine::ensure_batch() {
   if (bt.cap) return;
-  if (!tc.hi) fail(QTTS_ERR_UNSUPPORTED, "batched generation needs the tensor-core projections");
+  if (!tc.tokens) fail(QTTS_ERR_UNSUPPORTED, "batched generation needs the tensor-core projections");
   const StackCfg& T = cfg.talker;
   const StackCfg& C = cfg.cp;
   const int cap = kBatchCap;
@@ -1462,33 +1461,25 @@ void Engine::ensure_batch() {
     QCK(cudaMemcpy(d, pt.data(), cap * 4, cudaMemcpyHostToDevice));
     bt.ckv.page_table = d;
   }
-  // split activations for M <= 16 rows, 16-row token tiles, split-K workspace
-  bt.acts.rows_cap = cap;
-  bt.acts.ld = tc.ld;
-  bt.acts.box_rows = 16;
-  bt.acts.hi = arena.alloc<__nv_bfloat16>((size_t)cap * tc.ld);
-  bt.acts.lo = arena.alloc<__nv_bfloat16>((size_t)cap * tc.ld);
-  bt.acts.rms = arena.alloc<float>(cap);
-  int sms = 148;
-  QCK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
-  bt.acts.sm_count = sms;
-  bt.acts.max_splits = 16;
-  bt.acts.ws_floats = (size_t)2 * sms * 128 * 16;
-  bt.acts.ws = arena.alloc<float>(bt.acts.ws_floats);
-  bt.acts.tickets = arena.alloc<unsigned>(4096);
-  QCK(cudaMemset(bt.acts.tickets, 0, 4096 * sizeof(unsigned)));
-  if (!tc_make_acts(bt.acts)) fail(QTTS_ERR_UNSUPPORTED, "tensor map encoding is unavailable");
+  // 16-row token tiles with a split-K workspace
+  bt.rms = arena.alloc<float>(cap);
+  bt.plan.tokens = 16;
+  bt.plan.sm_count = tc.sm_count;
+  bt.plan.max_splits = 16;
+  bt.plan.ws_floats = tc_workspace_floats(16, tc.sm_count);
+  bt.plan.ws = arena.alloc<float>(bt.plan.ws_floats);
+  bt.plan.tickets = arena.alloc<unsigned>(4096);
   for (auto& ev : bt.ev) QCK(cudaEventCreate(&ev));
 }
 
 void Engine::blinear(const __nv_bfloat16* W, const float* x, int ldx, const float* gamma,
                      float eps, float* y, int ldy, const float* resid, int ldr, const float* bias,
-                     int M, int N, int K, Epilogue epi) {
+                     int M, int N, int K, Epilogue epi, float* rms_out) {
   LinearArgs a{W, x, ldx, gamma, eps, y, ldy, resid, ldr, bias, M, N, K, nullptr};
-  if (!tc_supported(a, epi, bt.acts))
+  if (!tc_supported(a, epi, bt.plan))
     fail(QTTS_ERR_UNSUPPORTED, "projection shape unsupported by the batched tensor-core path");
-  QCK(launch_linear_tc(a, epi, bt.acts, tc_err, stream));
-  launches += 2;
+  QCK(launch_linear_tc(a, epi, bt.plan, rms_out, tc_err, stream));
+  launches += 1;
 }
 
 // One position through all layers for nb sequences (rows of B.x).
@@ -1541,7 +1532,7 @@ void Engine::batch_head(int role, int group, const float* x, const SampleCfg& c,
   const __nv_bfloat16* W = talker_role ? head : cp_heads + (size_t)group * C.vocab * C.hidden;
   const float* gamma = talker_role ? norm_g : cp_norm_g;
   blinear(W, x, S.hidden, gamma, S.eps, bt.logits, S.vocab, nullptr, 0, nullptr, nb, S.vocab,
-          S.hidden, EPI_STORE);
+          S.hidden, EPI_STORE, bt.rms);
   BatchHeadArgs bh{};
   HeadArgs& a = bh.h;
   a.role = role;
@@ -1558,6 +1549,8 @@ void Engine::batch_head(int role, int group, const float* x, const SampleCfg& c,
   a.codes = bt.codes;
   a.lin = LinearArgs{W, x, S.hidden, gamma, S.eps, bt.logits, S.vocab, nullptr, 0, nullptr, 1,
                      S.vocab, S.hidden, nullptr};
+  a.frames_cap = (int)max_cache_steps;
+  a.talker_vocab = T.vocab;
   if (talker_role) {
     a.cp_prefix = bt.cp_prefix;
   } else {
@@ -1572,7 +1565,7 @@ void Engine::batch_head(int role, int group, const float* x, const SampleCfg& c,
   }
   bh.logits = bt.logits;
   bh.logits_ld = S.vocab;
-  bh.rms = bt.acts.rms;
+  bh.rms = bt.rms;
   bh.hist_stride = (long long)max_cache_steps;
   bh.codes_stride = (long long)max_cache_steps * C.groups;
   bh.next_stride = has_proj() ? T.hidden : C.hidden;
@@ -1679,6 +1672,12 @@ void Engine::generate_batch(const std::vector<std::vector<uint32_t>>& ids,
       QCK(cudaMemcpyAsync(bt.trailing + (size_t)b * (max_cache_steps + 1) * H, trailing,
                           (size_t)ntr * H * sizeof(float), cudaMemcpyDeviceToDevice, stream));
     }
+  } catch (const QttsError& err) {
+    tkv = saved;
+    if (!crumbs_host) throw;
+    fail(err.code, std::string(err.what()) + " [prefill; last kernel entered " +
+                       std::to_string(crumbs_host[0]) + ", last gemm left " +
+                       std::to_string(crumbs_host[1]) + "]");
   } catch (...) {
     tkv = saved;
     throw;
@@ -1687,15 +1686,25 @@ void Engine::generate_batch(const std::vector<std::vector<uint32_t>>& ids,
   SampleKey last = full;
   last.last = 1;
   const size_t max_frames = o0.max_frames;
-  cudaGraphExec_t gf = max_frames > 1 ? batch_graph(full, nb) : nullptr;
-  cudaGraphExec_t gl = batch_graph(last, nb);
+  // QTTS_BATCH_EAGER=1: enqueue the kernels directly instead of replaying a
+  // graph (debugging aid: launch errors surface at the launch that caused them)
+  const char* eg = std::getenv("QTTS_BATCH_EAGER");
+  const bool eager = eg && eg[0] == '1';
+  cudaGraphExec_t gf = !eager && max_frames > 1 ? batch_graph(full, nb) : nullptr;
+  cudaGraphExec_t gl = eager ? nullptr : batch_graph(last, nb);
   size_t done = 0;
   last_launches = 0;
   QCK(cudaEventRecord(bt.ev[1], stream));
+  try {
   while (done < max_frames) {
     const size_t burst = std::min<size_t>(16, max_frames - done);
     for (size_t i = 0; i < burst; ++i) {
       const bool is_last = done + i + 1 >= max_frames;
+      if (eager) {
+        enqueue_batch_frame(is_last ? last : full, nb);
+        QCK(cudaStreamSynchronize(stream));
+        continue;
+      }
       QCK(cudaGraphLaunch(is_last ? gl : gf, stream));
       last_launches += batch_nodes[std::make_pair(is_last ? last : full, nb)];
     }
@@ -1707,6 +1716,22 @@ void Engine::generate_batch(const std::vector<std::vector<uint32_t>>& ids,
     for (int b = 0; b < nb; ++b) all_halted = all_halted && bt.st_host[b].halt;
     if (all_halted) break;
   }
+  } catch (const QttsError& err) {
+    if (!crumbs_host) throw;
+    std::string st_dump;
+    for (int b = 0; b < nb; ++b)
+      st_dump += " [" + std::to_string(b) + ": f" + std::to_string(bt.st_host[b].frames) + " s" +
+                 std::to_string(bt.st_host[b].semantic) + " p" +
+                 std::to_string(bt.st_host[b].talker_pos) + " h" +
+                 std::to_string(bt.st_host[b].halt) + "]";
+    fail(err.code, std::string(err.what()) + " [last kernel entered " +
+                       std::to_string(crumbs_host[0]) + ", last gemm left " +
+                       std::to_string(crumbs_host[1]) + ", check " +
+                       std::to_string(crumbs_host[2]) + " v " + std::to_string(crumbs_host[3]) +
+                       " " + std::to_string(crumbs_host[4]) + " seq " +
+                       std::to_string(crumbs_host[5]) + ", frames done " + std::to_string(done) +
+                       "; last synced state:" + st_dump + "]");
+  }
   QCK(cudaEventRecord(bt.ev[2], stream));
   QCK(cudaStreamSynchronize(stream));
   QCK(cudaEventElapsedTime(&last_prefill_ms, bt.ev[0], bt.ev[1]));
@@ -1717,7 +1742,16 @@ void Engine::generate_batch(const std::vector<std::vector<uint32_t>>& ids,
   last_frames = 0;
   for (int b = 0; b < nb; ++b) {
     const SeqState& s = bt.st_host[b];
-    if (s.error) fail(QTTS_ERR_DEVICE_STATE, "cannot sample from logits with no finite values");
+    if (s.error == 1) fail(QTTS_ERR_DEVICE_STATE, "cannot sample from logits with no finite values");
+    if (s.error)
+      fail(QTTS_ERR_DEVICE_STATE,
+           "batched head found an out-of-range sequence state (code " + std::to_string(s.error) +
+               (crumbs_host ? ", check " + std::to_string(crumbs_host[2]) + " v " +
+                                  std::to_string(crumbs_host[3]) + " " +
+                                  std::to_string(crumbs_host[4]) + " seq " +
+                                  std::to_string(crumbs_host[5])
+                            : std::string()) +
+               ")");
     const size_t f = (size_t)s.frames;
     QCK(cudaMemcpy(codes_out + (size_t)b * cap_per_request, bt.codes + (size_t)b * max_cache_steps * G,
                    f * G * sizeof(int32_t), cudaMemcpyDeviceToHost));

@@ -1,12 +1,20 @@
-// tcgen05 GEMM for the prefill projections (see gemm_tc.h).
+// tcgen05 GEMM for projections over many activation rows (see gemm_tc.h).
 //
-// CTA = 6 warps: warp 0 issues TMA loads (weights: two 64-row boxes; split
-// activations: hi and lo boxes of kTcTokens rows), warp 1 owns the TMEM
-// accumulator (128 lanes x kTcTokens fp32 columns) and issues the MMAs from
-// one thread, warps 2-5 read TMEM back (each warp may only touch the 32 lanes
-// of its warp-id modulo 4) and apply the epilogue. A kTcStages-deep ring of
-// mbarrier pairs (full: TMA bytes landed; empty: the MMAs reading the stage
-// completed) decouples loads from MMAs. Every wait is bounded.
+// CTA = 6 warps. Warp 0 streams the weight tile of each K step with TMA (two
+// 64-row boxes, 128-byte swizzle). Warps 2-5 build the activation tile of the
+// same step in shared memory: they read fp32 rows of x, multiply by gamma,
+// split each value into bf16 hi + lo and store both in the swizzled K-major
+// layout the MMA reads, accumulating each row's sum of squares on the way (so
+// no separate split kernel or launch). Warp 1 owns the TMEM accumulator
+// (128 lanes x BN fp32 columns) and issues two MMAs per 16-element K step
+// (W * hi, W * lo) from one thread. A ring of stages with three mbarriers
+// each (weights landed, activations written, MMAs done) decouples the three
+// roles; every wait is bounded, and the producer waits for the final release
+// of every stage before the CTA exits. Afterwards warps 2-5 read TMEM back (each warp
+// may only touch the 32 lanes of its warp id modulo 4) and apply the RMS scale
+// and the epilogue. Skinny shapes split K over blockIdx.z: partial tiles and
+// partial sums of squares go to a workspace and the last CTA of each tile
+// (ticket) adds them in split order, so results are deterministic.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -18,10 +26,15 @@
 #include "sm100.cuh"
 
 namespace qtts {
+__device__ Crumbs g_crumbs;
+cudaError_t set_crumbs_gemm(unsigned* host_mapped_dev_ptr) {
+  const Crumbs c{host_mapped_dev_ptr};
+  return cudaMemcpyToSymbol(g_crumbs, &c, sizeof(c));
+}
 namespace {
 
 constexpr int kTcThreads = 192;
-constexpr unsigned kTcSpin = 1u << 22;
+constexpr unsigned long long kTcWaitNs = 2000000000ull;  // 2 s: a stall, not a slow step
 constexpr int kStageA = kTcRows * kTcBlockK * 2;  // 16 KB: 128 weight rows x 64 K
 
 // Per token-tile width BN (MMA N): stage ring depth and sizes.
@@ -30,12 +43,19 @@ struct TcCfg {
   static constexpr int kStages = BN >= 128 ? 4 : 8;
   static constexpr int kStageB = BN * kTcBlockK * 2;         // hi or lo
   static constexpr int kStageBytes = kStageA + 2 * kStageB;  // multiple of 1024
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256;
+  // accumulator columns: [0, BN) = W * hi, [BN, 2 BN) = W * lo (one MMA with N = 2 BN)
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  // ring + 1024-byte alignment slack + barriers/flags (256 B) + row scales
+  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + 256 + BN * sizeof(float);
+  static_assert(3 * kStages * 8 + 8 + 8 <= 256, "barrier area");
   static_assert(kStageBytes % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
 };
 
 struct TcArgs {
+  const float* x;        // [M, ldx] fp32 activations
+  int ldx;
+  const float* gamma;    // optional RMSNorm gamma [K]
+  float eps;
   int M, N, K;
   int epi;
   int up_off;            // SWIGLU: row offset of the up half in W
@@ -44,30 +64,37 @@ struct TcArgs {
   const float* resid;
   int ldr;
   const float* bias;
-  const float* rms;
+  float* rms_out;        // optional [M]: the RMS scale of each row (head selection uses it)
   int* err;
   const int* halt;
   int splits;            // K split over blockIdx.z; > 1 uses ws + tickets
-  float* ws;             // [tiles][splits][128][BN] partial tiles
+  float* ws;             // [tiles][splits][128][BN] partial tiles, then [tiles][splits][BN] sums
   unsigned* tickets;     // [tiles], zero at rest (reset by the last CTA)
 };
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap hmap,
-              const __grid_constant__ CUtensorMap lmap, TcArgs a) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap wmap, TcArgs a) {
   using Cfg = TcCfg<BN>;
   constexpr int S = Cfg::kStages;
+  QTTS_CRUMB(0, 100000 + BN * 1000 + a.N / 64);
   extern __shared__ uint8_t tc_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
-  uint64_t* empty = full + S;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);  // weights landed
+  uint64_t* bready = full + S;                                                // activations written
+  uint64_t* empty = bready + S;                                               // MMAs done
   uint64_t* done = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* s_ss = reinterpret_cast<float*>(last_flag + 1);  // [BN] row sums of squares / RMS
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool swiglu = a.epi == EPI_SWIGLU;
@@ -83,6 +110,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&bready[s], 4);  // one arrival per activation warp
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
@@ -95,95 +123,203 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // producer: weight tiles of the first stages do not depend on the previous
-    // kernel, so they are requested before the dependency wait.
-    const int pre = min(S, nk);
-    for (int i = 0; i < pre; ++i) {
-      uint8_t* st = smem + i * Cfg::kStageBytes;
-      mbar_expect_tx(&full[i], Cfg::kStageBytes);
-      const int kx = (kb0 + i) * kTcBlockK;
-      tma_load_2d(st, &wmap, kx, row_a0, &full[i]);
-      tma_load_2d(st + kStageA / 2, &wmap, kx, row_a1, &full[i]);
-    }
-    pdl_wait();
-    const bool halted = a.halt && __ldcg(a.halt);
+    // weights: they never depend on the previous kernel, so the first stages
+    // are requested before the dependency wait
+    int issued = 0;
     for (int i = 0; i < nk; ++i) {
       const int s = i % S;
-      uint8_t* st = smem + s * Cfg::kStageBytes;
-      const int kx = (kb0 + i) * kTcBlockK;
-      if (i >= S) {
-        if (!mbar_wait(&empty[s], ((i / S) & 1) ^ 1, kTcSpin)) {
-          atomicExch(a.err, 1);
-          break;
-        }
-        mbar_expect_tx(&full[s], Cfg::kStageBytes);
-        tma_load_2d(st, &wmap, kx, row_a0, &full[s]);
-        tma_load_2d(st + kStageA / 2, &wmap, kx, row_a1, &full[s]);
+      if (i >= S && !mbar_wait_ns(&empty[s], ((i / S) & 1) ^ 1, kTcWaitNs)) {
+        atomicExch(a.err, 1);
+        break;
       }
-      // when halted the activation tiles are still fetched (the stage byte
-      // counts must complete) but the epilogue writes nothing
-      (void)halted;
-      tma_load_2d(st + kStageA, &hmap, kx, m0, &full[s]);
-      tma_load_2d(st + kStageA + Cfg::kStageB, &lmap, kx, m0, &full[s]);
+      uint8_t* st = smem + s * Cfg::kStageBytes;
+      mbar_expect_tx(&full[s], kStageA);
+      const int kx = (kb0 + i) * kTcBlockK;
+      tma_load_2d(st, &wmap, kx, row_a0, &full[s]);
+      tma_load_2d(st + kStageA / 2, &wmap, kx, row_a1, &full[s]);
+      ++issued;
+    }
+    // Tail: before the CTA exits, no weight copy may still be landing and no
+    // tensor-core commit may still be due to arrive on a stage barrier (a late
+    // arrival would hit shared memory that the SM has handed to the next CTA).
+    // So wait for the last fill of every stage and for its release.
+    for (int i = (issued > S ? issued - S : 0); i < issued; ++i) {
+      if (!mbar_wait_ns(&full[i % S], (i / S) & 1, kTcWaitNs)) atomicExch(a.err, 5);
+      if (!mbar_wait_ns(&empty[i % S], (i / S) & 1, kTcWaitNs)) atomicExch(a.err, 6);
     }
   } else if (warp == 1 && lane == 0) {
     // MMA issuer
-    constexpr uint32_t idesc = umma_idesc_bf16(kTcRows, BN);
+    // hi and lo activation tiles are contiguous rows of one K-major operand, so
+    // a single MMA with N = 2 BN multiplies both (half the MMA instructions)
+    constexpr uint32_t idesc = umma_idesc_bf16(kTcRows, 2 * BN);
     for (int i = 0; i < nk; ++i) {
       const int s = i % S;
-      if (!mbar_wait(&full[s], (i / S) & 1, kTcSpin)) {
+      const unsigned ph = (i / S) & 1;
+      if (!mbar_wait_ns(&full[s], ph, kTcWaitNs) || !mbar_wait_ns(&bready[s], ph, kTcWaitNs)) {
         atomicExch(a.err, 2);
         break;
       }
       tc_fence_after();
       uint8_t* st = smem + s * Cfg::kStageBytes;
       const uint64_t da = umma_desc_sw128(st);
-      const uint64_t dh = umma_desc_sw128(st + kStageA);
-      const uint64_t dl = umma_desc_sw128(st + kStageA + Cfg::kStageB);
+      const uint64_t db = umma_desc_sw128(st + kStageA);
 #pragma unroll
-      for (int kk = 0; kk < kTcBlockK / 16; ++kk) {
-        // +32 bytes per 16-element K step inside the swizzled 128-byte row
-        umma_bf16(tmem, da + 2 * kk, dh + 2 * kk, idesc, (i | kk) != 0);
-        umma_bf16(tmem, da + 2 * kk, dl + 2 * kk, idesc, 1u);
-      }
+      for (int kk = 0; kk < kTcBlockK / 16; ++kk)  // +32 bytes per 16-element K step
+        umma_bf16(tmem, da + 2 * kk, db + 2 * kk, idesc, (i | kk) != 0);
       umma_commit(&empty[s]);
     }
     umma_commit(done);  // also fires when nothing was issued
   } else if (warp >= 2) {
+    const int et = threadIdx.x - 64;  // 0..127 over the activation / epilogue warps
     pdl_wait();
     const bool halted = a.halt && __ldcg(a.halt);
-    // this warp's 32 TMEM lanes = tile rows lane_base..lane_base+31
+    // ---- activation producer: hi/lo tiles of gamma * x for every K step ----
+    // thread et owns 16-byte chunk c = et % 8 (8 consecutive K) of rows et / 8 + 16 j
+    constexpr int kRowsPerThread = BN / 16;
+    const int c = et & 7;
+    float ss[kRowsPerThread];
+#pragma unroll
+    for (int j = 0; j < kRowsPerThread; ++j) ss[j] = 0.f;
+    // rows of the next PF K steps are in flight while one is converted and
+    // stored (PF register buffers, rotated by a loop unrolled PF times)
+    constexpr int PF = BN <= 16 ? 4 : 1;
+    float4 xq[PF][kRowsPerThread][2], gq[PF][2];
+    auto load_step = [&](int i, float4 (&xr)[kRowsPerThread][2], float4 (&gr)[2]) {
+      const int k = (kb0 + i) * kTcBlockK + 8 * c;
+      if (a.gamma) {
+        gr[0] = __ldg(reinterpret_cast<const float4*>(a.gamma + k));
+        gr[1] = __ldg(reinterpret_cast<const float4*>(a.gamma + k + 4));
+      }
+#pragma unroll
+      for (int j = 0; j < kRowsPerThread; ++j) {
+        const int m = m0 + (et >> 3) + 16 * j;
+        if (m < a.M) {
+          const float* p = a.x + (long long)m * a.ldx + k;
+          xr[j][0] = __ldcg(reinterpret_cast<const float4*>(p));
+          xr[j][1] = __ldcg(reinterpret_cast<const float4*>(p + 4));
+        } else {
+          xr[j][0] = xr[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    };
+#pragma unroll
+    for (int u = 0; u < PF; ++u)
+      if (u < nk) load_step(u, xq[u], gq[u]);
+    bool ok = true;
+    for (int i0 = 0; i0 < nk && ok; i0 += PF) {
+#pragma unroll
+      for (int u = 0; u < PF; ++u) {
+        const int i = i0 + u;
+        if (i >= nk || !ok) break;
+        const int s = i % S;
+        if (i >= S && !mbar_wait_ns(&empty[s], ((i / S) & 1) ^ 1, kTcWaitNs)) {
+          atomicExch(a.err, 4);
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * Cfg::kStageBytes;
+        const float g[8] = {gq[u][0].x, gq[u][0].y, gq[u][0].z, gq[u][0].w,
+                            gq[u][1].x, gq[u][1].y, gq[u][1].z, gq[u][1].w};
+#pragma unroll
+        for (int j = 0; j < kRowsPerThread; ++j) {
+          const int r = (et >> 3) + 16 * j;
+          float v[8] = {xq[u][j][0].x, xq[u][j][0].y, xq[u][j][0].z, xq[u][j][0].w,
+                        xq[u][j][1].x, xq[u][j][1].y, xq[u][j][1].z, xq[u][j][1].w};
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            ss[j] = fmaf(v[q], v[q], ss[j]);
+            if (a.gamma) v[q] *= g[q];
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * q]);
+            const __nv_bfloat16 h1 = __float2bfloat16_rn(v[2 * q + 1]);
+            hw[q] = pack_bf16(__bfloat162float(h0), __bfloat162float(h1));
+            lw[q] = pack_bf16(v[2 * q] - __bfloat162float(h0), v[2 * q + 1] - __bfloat162float(h1));
+          }
+          // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8)
+          const int off = r * 128 + ((c ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(st + kStageA + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(st + kStageA + Cfg::kStageB + off) =
+              make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+        if (i + PF < nk) load_step(i + PF, xq[u], gq[u]);
+        // generic-proxy writes -> visible to the tensor core's async proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bready[s]);
+      }
+    }
+    // row sums of squares: the 8 lanes of a row group hold its partial sums
+#pragma unroll
+    for (int j = 0; j < kRowsPerThread; ++j) {
+      ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], 1);
+      ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], 2);
+      ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], 4);
+    }
+    if (c == 0) {
+#pragma unroll
+      for (int j = 0; j < kRowsPerThread; ++j) s_ss[(et >> 3) + 16 * j] = ss[j];
+    }
+
+    // ---- epilogue: this warp's 32 TMEM lanes = tile rows lane_base..lane_base+31 ----
     const int lane_base = 32 * (warp & 3);
-    const bool got = mbar_wait(done, 0, kTcSpin * 4);
+    // always wait for the MMAs (even after an error above): the CTA must not
+    // free TMEM or exit while tensor-core work is in flight
+    const bool got = mbar_wait_ns(done, 0, 2 * kTcWaitNs) && ok;
     if (!got) atomicExch(a.err, 3);
     tc_fence_after();
     const int r = lane_base + lane;
     const int cols = min(BN, a.M - m0);
     const int tile = blockIdx.y * gridDim.x + blockIdx.x;
     bool final_cta = true;
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // s_ss complete
     if (a.splits > 1) {
-      // partial tile -> workspace; the last CTA of the tile reduces in split order
+      // partial tile and partial row sums -> workspace; the last CTA of the
+      // tile reduces both in split order
       float* part = a.ws + ((long long)tile * a.splits + blockIdx.z) * kTcRows * BN;
       for (int c0 = 0; c0 < BN; c0 += 16) {
         if (c0 >= cols) break;
-        float v[16];
+        float v[16], w[16];
         tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0, v);
+        tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(c0 + BN), w);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] += w[j];
 #pragma unroll
         for (int j = 0; j < 16; j += 4)
           __stcg(reinterpret_cast<float4*>(part + r * BN + c0 + j),
                  make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
       }
+      float* ssw = a.ws + (long long)gridDim.x * gridDim.y * a.splits * kTcRows * BN;
+      if (et < BN) __stcg(ssw + ((long long)tile * a.splits + blockIdx.z) * BN + et, s_ss[et]);
       __threadfence();
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (warp == 2 && lane == 0) {
+      if (et == 0) {
         const unsigned t = atomicAdd(&a.tickets[tile], 1u);
         *last_flag = t == (unsigned)a.splits - 1u;
         if (*last_flag) a.tickets[tile] = 0u;
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
       final_cta = *last_flag != 0;
-      if (final_cta) __threadfence();
+      if (final_cta) {
+        __threadfence();
+        if (et < BN) {
+          float t = 0.f;
+          for (int s = 0; s < a.splits; ++s)
+            t += __ldcg(ssw + ((long long)tile * a.splits + s) * BN + et);
+          s_ss[et] = t;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
     }
+    // RMS scale per row (1 without gamma), published for the caller if asked
+    if (final_cta && et < BN) {
+      const float sc = a.gamma ? rsqrtf(s_ss[et] / (float)a.K + a.eps) : 1.0f;
+      s_ss[et] = sc;
+      if (a.rms_out && blockIdx.x == 0 && m0 + et < a.M && !halted) a.rms_out[m0 + et] = sc;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
     float* xbuf = reinterpret_cast<float*>(smem);  // SWIGLU: up rows, after the mainloop
     for (int c0 = 0; final_cta && c0 < BN; c0 += 16) {
       if (c0 >= cols) break;  // uniform over the epilogue warps
@@ -212,7 +348,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
       } else {
+        float w[16];
         tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0, v);
+        tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(c0 + BN), w);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] += w[j];
       }
       const bool write = got && !halted;
       if (swiglu) {
@@ -227,7 +367,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int j = 0; j < 16; ++j) {
             const int m = m0 + c0 + j;
             if (c0 + j < cols && n < a.N) {
-              const float sc = a.rms ? __ldg(a.rms + m) : 1.0f;
+              const float sc = s_ss[c0 + j];
               const float g = v[j] * sc, u = xbuf[r * BN + c0 + j] * sc;
               a.y[(long long)m * a.ldy + n] = g / (1.0f + expf(-g)) * u;
             }
@@ -240,7 +380,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int j = 0; j < 16; ++j) {
           const int m = m0 + c0 + j;
           if (c0 + j < cols && n < a.N) {
-            float out = v[j] * (a.rms ? __ldg(a.rms + m) : 1.0f);
+            float out = v[j] * s_ss[c0 + j];
             if (a.epi == EPI_RESID) out += a.resid[(long long)m * a.ldr + n];
             if (a.epi == EPI_BIAS) out += a.bias[n];
             if (a.epi == EPI_BIAS_SILU) out = silu_f(out + a.bias[n]);
@@ -256,46 +396,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     tmem_free(tmem, Cfg::kTmemCols);
   }
-}
-
-// gamma * x split into bf16 hi + lo, and the per-row RMS scale.
-__global__ void __launch_bounds__(256) k_split_rows(const float* x, int ldx, const float* gamma,
-                                                    float eps, int K, __nv_bfloat16* hi,
-                                                    __nv_bfloat16* lo, int ld, float* rms,
-                                                    const int* halt) {
-  __shared__ float red[8];
-  pdl_wait();
-  if (halt && __ldcg(halt)) return;
-  const int m = blockIdx.x;
-  const float* row = x + (long long)m * ldx;
-  float ss = 0.f;
-  for (int k = threadIdx.x * 4; k < K; k += 1024) {
-    float4 v = *reinterpret_cast<const float4*>(row + k);
-    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-    if (gamma) {
-      const float4 g = *reinterpret_cast<const float4*>(gamma + k);
-      v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
-    }
-    const float f[4] = {v.x, v.y, v.z, v.w};
-    __nv_bfloat16 h[4], l[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      h[i] = __float2bfloat16_rn(f[i]);
-      l[i] = __float2bfloat16_rn(f[i] - __bfloat162float(h[i]));
-    }
-    __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(hi + (long long)m * ld + k);
-    __nv_bfloat162* lw = reinterpret_cast<__nv_bfloat162*>(lo + (long long)m * ld + k);
-    ho[0] = __halves2bfloat162(h[0], h[1]); ho[1] = __halves2bfloat162(h[2], h[3]);
-    lw[0] = __halves2bfloat162(l[0], l[1]); lw[1] = __halves2bfloat162(l[2], l[3]);
-  }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
-    for (int i = 0; i < 8; ++i) t += red[i];
-    rms[m] = gamma ? rsqrtf(t / (float)K + eps) : 1.0f;
-  }
+  QTTS_CRUMB(1, 100000 + BN * 1000 + a.N / 64);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -327,12 +428,7 @@ bool make_map(const void* base, uint64_t inner, uint64_t rows, uint64_t pitch_by
 
 }  // namespace
 
-bool tc_make_acts(TcActs& a) {
-  return make_map(a.hi, (uint64_t)a.ld, (uint64_t)a.rows_cap, (uint64_t)a.ld * 2,
-                  (uint32_t)a.box_rows, &a.hi_map) &&
-         make_map(a.lo, (uint64_t)a.ld, (uint64_t)a.rows_cap, (uint64_t)a.ld * 2,
-                  (uint32_t)a.box_rows, &a.lo_map);
-}
+bool tc_available() { return encode_fn() != nullptr; }
 
 bool tc_weight_map(const __nv_bfloat16* W, int rows, int K, CUtensorMap* out) {
   static std::mutex mu;
@@ -351,11 +447,15 @@ bool tc_weight_map(const __nv_bfloat16* W, int rows, int K, CUtensorMap* out) {
   return true;
 }
 
-bool tc_supported(const LinearArgs& a, int epi, const TcActs& acts) {
-  if (!acts.hi || a.M > acts.rows_cap || a.K > acts.ld || a.K % kTcBlockK) return false;
-  if (acts.box_rows != 16 && acts.box_rows != 128) return false;
-  if (a.ldx % 4 || (reinterpret_cast<uintptr_t>(a.x) & 15)) return false;
-  return a.N % (kTcRows / 2) == 0 && (epi != EPI_SWIGLU || a.N >= kTcRows / 2);
+bool tc_supported(const LinearArgs& a, int epi, const TcPlan& p) {
+  if (p.tokens != 16 && p.tokens != 128) return false;
+  if (a.K % kTcBlockK || a.ldx % 4 || (reinterpret_cast<uintptr_t>(a.x) & 15)) return false;
+  return a.N % (kTcRows / 2) == 0 && a.M >= 1;
+}
+
+size_t tc_workspace_floats(int tokens, int sm_count) {
+  // partial tiles and row sums for up to 2 x sm_count (tile, split) pairs
+  return (size_t)2 * sm_count * ((size_t)kTcRows * tokens + tokens);
 }
 
 cudaError_t configure_tc_kernels() {
@@ -366,35 +466,32 @@ cudaError_t configure_tc_kernels() {
                               (int)TcCfg<16>::kSmem);
 }
 
-cudaError_t launch_linear_tc(const LinearArgs& a, int epi, const TcActs& acts, int* err,
-                             cudaStream_t stream) {
-  if (!tc_supported(a, epi, acts)) return cudaErrorInvalidValue;
+cudaError_t launch_linear_tc(const LinearArgs& a, int epi, const TcPlan& p, float* rms_out,
+                             int* err, cudaStream_t stream) {
+  if (!tc_supported(a, epi, p)) return cudaErrorInvalidValue;
   const int w_rows = epi == EPI_SWIGLU ? 2 * a.N : a.N;
   CUtensorMap wmap;
   if (!tc_weight_map(a.W, w_rows, a.K, &wmap)) return cudaErrorInvalidValue;
-  cudaError_t e = launch(k_split_rows, dim3(a.M), dim3(256), 0, stream, a.x, a.ldx, a.gamma,
-                         a.eps, a.K, acts.hi, acts.lo, acts.ld, acts.rms, a.halt);
-  if (e != cudaSuccess) return e;
-  const int BN = acts.box_rows;
+  const int BN = p.tokens;
   const int cols_per_cta = epi == EPI_SWIGLU ? kTcRows / 2 : kTcRows;
   dim3 grid((a.N + cols_per_cta - 1) / cols_per_cta, (a.M + BN - 1) / BN, 1);
   // split K so that a skinny GEMM still spreads over the SMs (deterministic
   // reduction by the last CTA of each tile)
   int splits = 1;
   const int tiles = (int)(grid.x * grid.y);
-  if (acts.ws && tiles < acts.sm_count) {
-    splits = std::min(acts.sm_count / tiles, (a.K / kTcBlockK) / 4);
-    splits = std::max(1, std::min(splits, acts.max_splits));
-    while (splits > 1 && (size_t)tiles * splits * kTcRows * BN > acts.ws_floats) --splits;
+  if (p.ws && tiles < p.sm_count) {
+    splits = std::min(p.sm_count / tiles, (a.K / kTcBlockK) / 4);
+    splits = std::max(1, std::min(splits, p.max_splits));
+    while (splits > 1 &&
+           (size_t)tiles * splits * ((size_t)kTcRows * BN + BN) > p.ws_floats)
+      --splits;
   }
   grid.z = splits;
-  TcArgs t{a.M, a.N, a.K, epi, a.N, a.y, a.ldy, a.resid, a.ldr, a.bias,
-           a.gamma ? acts.rms : nullptr, err, a.halt, splits, acts.ws, acts.tickets};
+  TcArgs t{a.x, a.ldx, a.gamma, a.eps, a.M, a.N, a.K, epi, a.N, a.y, a.ldy, a.resid, a.ldr,
+           a.bias, rms_out, err, a.halt, splits, p.ws, p.tickets};
   if (BN == 16)
-    return launch(k_gemm_tc<16>, grid, dim3(kTcThreads), TcCfg<16>::kSmem, stream, wmap,
-                  acts.hi_map, acts.lo_map, t);
-  return launch(k_gemm_tc<128>, grid, dim3(kTcThreads), TcCfg<128>::kSmem, stream, wmap,
-                acts.hi_map, acts.lo_map, t);
+    return launch(k_gemm_tc<16>, grid, dim3(kTcThreads), TcCfg<16>::kSmem, stream, wmap, t);
+  return launch(k_gemm_tc<128>, grid, dim3(kTcThreads), TcCfg<128>::kSmem, stream, wmap, t);
 }
 
 }  // namespace qtts

@@ -38,6 +38,8 @@ __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 // past the dependency wait and the last CTA exit, in globaltimer ns; slot 3
 // is the last CTA past the wait, slots 4/5 the head's selection start/end.
 // ---------------------------------------------------------------------------
+__device__ Crumbs g_crumbs;
+
 struct StepTrace {
   unsigned long long* buf;
   int cap;
@@ -210,6 +212,7 @@ __device__ __forceinline__ bool linear_body(const LinearArgs& a, float* sx, floa
 
 template <int MT, int RPW, int EPI>
 __global__ void __launch_bounds__(kThreads) k_linear(LinearArgs a) {
+  QTTS_CRUMB(0, 10);
   extern __shared__ float4 dyn4[];
   __shared__ float s_inv[MT];
   linear_body<MT, RPW, EPI>(a, reinterpret_cast<float*>(dyn4), s_inv);
@@ -433,12 +436,14 @@ __device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, flo
 
 template <int KCH>
 __global__ void __launch_bounds__(kThreads) k_gemv1_attn(LinearArgs a, AttnDecodeArgs at) {
+  QTTS_CRUMB(0, 11);
   __shared__ __align__(16) float xs[KCH * 256 + 32];
   gemv1_body<KCH, 1, true>(a, EPI_RESID, xs, nullptr, &at);
 }
 
 template <int KCH, int NR>
 __global__ void __launch_bounds__(kThreads) k_gemv1(LinearArgs a, int epi) {
+  QTTS_CRUMB(0, 6);
   __shared__ __align__(16) float xs[KCH * 256 + 32];
   gemv1_body<KCH, NR>(a, epi, xs, nullptr);
 }
@@ -458,6 +463,22 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
   for (int v = tid; v < V; v += kThreads) sel.val[v] = __ldcg(logits + v);
   if (tid == 0) { s_frame = a.st->frames; s_sem = a.st->semantic; }
   __syncthreads();
+  // batched heads check the per-sequence state they index with (a fault here
+  // would otherwise take the context down): record and skip
+  if (a.frames_cap > 0 &&
+      (s_frame < 0 || s_frame >= a.frames_cap || s_sem < -1 || s_sem >= a.talker_vocab)) {
+    if (tid == 0) {
+      a.st->error = 2;
+      if (g_crumbs.p) {
+        g_crumbs.p[2] = 1000 + a.role;
+        g_crumbs.p[3] = (unsigned)s_frame;
+        g_crumbs.p[4] = (unsigned)s_sem;
+        g_crumbs.p[5] = blockIdx.x;
+        __threadfence_system();
+      }
+    }
+    return;
+  }
   if (a.role == ROLE_TALKER_STEP)
     sel.penalise(V, a.history, s_frame, -1, a.penalty, a.suppress, a.eos_token);
   else
@@ -469,6 +490,19 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
     a.st->rng_counter = rng.counter;
   }
   if (a.token_out && tid == 0) *a.token_out = tok;
+  if (a.frames_cap > 0 && (tok < 0 || tok >= V)) {
+    if (tid == 0) {
+      a.st->error = 3;
+      if (g_crumbs.p) {
+        g_crumbs.p[2] = 2000 + a.role;
+        g_crumbs.p[3] = (unsigned)tok;
+        g_crumbs.p[4] = (unsigned)V;
+        g_crumbs.p[5] = blockIdx.x;
+        __threadfence_system();
+      }
+    }
+    return;
+  }
 
   const int H = a.H;
   if (a.role == ROLE_TALKER_PREFILL || a.role == ROLE_TALKER_STEP) {
@@ -516,6 +550,7 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
 // the host.
 template <int KCH>
 __global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
+  QTTS_CRUMB(0, 7);
   extern __shared__ float4 dyn4[];
   float* smem = reinterpret_cast<float*>(dyn4);
   __shared__ float s_inv[1];
@@ -538,6 +573,7 @@ __global__ void __launch_bounds__(kThreads) k_head(HeadArgs a) {
 // Batched heads: the logits of B sequences come from one tensor-core
 // projection; CTA b selects sequence b's token (skipped once it has halted).
 __global__ void __launch_bounds__(kThreads) k_select_batch(BatchHeadArgs bh) {
+  QTTS_CRUMB(0, 3);
   extern __shared__ float4 dyn4[];
   float* smem = reinterpret_cast<float*>(dyn4);
   pdl_wait();
@@ -570,6 +606,7 @@ constexpr int kAttnBatch = 8;
 
 template <int G, int NW>
 __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
+  QTTS_CRUMB(0, 2);
   __shared__ float sq[G][kHeadDim];
   __shared__ float sk[kHeadDim], sv[kHeadDim];
   __shared__ float red[4][G + 1];
@@ -757,6 +794,7 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
 // Prefill: QK-RMSNorm + RoPE for M rows at positions pos0.., K/V appended to
 // the cache as bf16; Q kept fp32 for the prefill attention.
 __global__ void __launch_bounds__(128) k_qk_prep(QkPrepArgs a) {
+  QTTS_CRUMB(0, 4);
   __shared__ float sx[kHeadDim];
   __shared__ float red[4];
   pdl_wait();
@@ -793,6 +831,7 @@ __global__ void __launch_bounds__(128) k_qk_prep(QkPrepArgs a) {
 
 // Prefill attention: one warp per (query row, q head), causal over the cache.
 __global__ void __launch_bounds__(128) k_attn_prefill(AttnPrefillArgs a) {
+  QTTS_CRUMB(0, 5);
   pdl_wait();
   if (a.halt && *a.halt) return;
   const int qh = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -826,6 +865,7 @@ __global__ void __launch_bounds__(128) k_attn_prefill(AttnPrefillArgs a) {
 }
 
 __global__ void k_gather_rows(const __nv_bfloat16* table, const int* ids, int width, float* out) {
+  QTTS_CRUMB(0, 8);
   pdl_wait();
   const int r = blockIdx.x;
   const __nv_bfloat16* src = table + (long long)ids[r] * width;
@@ -836,6 +876,7 @@ __global__ void k_gather_rows(const __nv_bfloat16* table, const int* ids, int wi
 __global__ void k_assemble_rows(const float* proj, const int* proj_index,
                                 const __nv_bfloat16* codec, const int* codec_ids,
                                 const float* xvec, int width, float* out) {
+  QTTS_CRUMB(0, 9);
   pdl_wait();
   const int r = blockIdx.x;
   const float* p = proj + (long long)proj_index[r] * width;
@@ -981,6 +1022,11 @@ cudaError_t launch_attn_o(const AttnDecodeArgs& at, const LinearArgs& o, cudaStr
   if (o.K == 512) return launch(k_gemv1_attn<2>, grid, dim3(kThreads), 0, stream, o, at);
   if (o.K == 1024) return launch(k_gemv1_attn<4>, grid, dim3(kThreads), 0, stream, o, at);
   return launch(k_gemv1_attn<8>, grid, dim3(kThreads), 0, stream, o, at);
+}
+
+cudaError_t set_crumbs_kernels(unsigned* host_mapped_dev_ptr) {
+  const Crumbs c{host_mapped_dev_ptr};
+  return cudaMemcpyToSymbol(g_crumbs, &c, sizeof(c));
 }
 
 cudaError_t set_step_trace(unsigned long long* buf, int capacity, cudaStream_t stream) {

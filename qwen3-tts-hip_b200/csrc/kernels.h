@@ -103,6 +103,8 @@ struct HeadArgs {
   int* history_out;        // semantic history
   int groups;
   int* token_out;          // optional: selected token
+  int frames_cap;          // > 0: checked bound of the frame counter (codes rows)
+  int talker_vocab;        // > 0: checked bound of the semantic token
 };
 
 // Batched heads: per-sequence views of `h` at the given element strides;
@@ -178,6 +180,9 @@ bool attn_o_fusable(const AttnDecodeArgs& at, const LinearArgs& o);
 cudaError_t launch_attn_o(const AttnDecodeArgs& at, const LinearArgs& o, cudaStream_t stream);
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_select_batch(const BatchHeadArgs& a, int B, cudaStream_t stream);
+// Debugging aid: device pointer of mapped host memory for kernel breadcrumbs.
+cudaError_t set_crumbs_kernels(unsigned* host_mapped_dev_ptr);
+cudaError_t set_crumbs_gemm(unsigned* host_mapped_dev_ptr);
 // Step trace buffer: [6][capacity] u64 globaltimer values (first entry, first
 // post-wait, last exit, last post-wait, head selection start/end) indexed by
 // trace_id; nullptr disables. Stream-ordered.

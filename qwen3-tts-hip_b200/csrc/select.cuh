@@ -208,6 +208,7 @@ struct Selector {
       // candidates are compacted and ranked exactly (value desc, index asc).
       stamp(1);
       if (tid == 0) { s_prefix = 0u; s_rem = K; s_lower = 0u; s_done = 0; s_above = 0u; s_ties = 0; }
+      Sync::sync();  // every thread reads the initial prefix in the first pass
       // Stop once at most `stop` keys are at or above the bucket: ranking is
       // quadratic in the candidate count.
       const int stop = min(kSelSmallK, max(2 * K, 64));

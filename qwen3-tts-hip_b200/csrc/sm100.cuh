@@ -31,6 +31,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, unsigned
     if (mbar_try(b, parity)) return true;
   return false;
 }
+// Bounded wait measured in time (%globaltimer ns), independent of how long a
+// single try_wait suspends.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* b, unsigned parity,
+                                             unsigned long long limit_ns) {
+  if (mbar_try(b, parity)) return true;
+  unsigned long long t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try(b, parity)) return true;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > limit_ns) return false;
+  }
+}
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
