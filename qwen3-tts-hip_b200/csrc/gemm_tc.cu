@@ -40,7 +40,8 @@ constexpr int kStageA = kTcRows * kTcBlockK * 2;  // 16 KB: 128 weight rows x 64
 // Per token-tile width BN (MMA N): stage ring depth and sizes.
 template <int BN>
 struct TcCfg {
-  static constexpr int kStages = BN >= 128 ? 4 : 8;
+  // 16-row tiles: 4 stages (~82 KB) so two CTAs share an SM and split K further
+  static constexpr int kStages = 4;
   static constexpr int kStageB = BN * kTcBlockK * 2;         // hi or lo
   static constexpr int kStageBytes = kStageA + 2 * kStageB;  // multiple of 1024
   // accumulator columns: [0, BN) = W * hi, [BN, 2 BN) = W * lo (one MMA with N = 2 BN)
@@ -80,7 +81,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 }
 
 template <int BN>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, BN <= 16 ? 2 : 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap wmap, TcArgs a) {
   using Cfg = TcCfg<BN>;
   constexpr int S = Cfg::kStages;
@@ -454,8 +455,8 @@ bool tc_supported(const LinearArgs& a, int epi, const TcPlan& p) {
 }
 
 size_t tc_workspace_floats(int tokens, int sm_count) {
-  // partial tiles and row sums for up to 2 x sm_count (tile, split) pairs
-  return (size_t)2 * sm_count * ((size_t)kTcRows * tokens + tokens);
+  // partial tiles and row sums for up to 4 x sm_count (tile, split) pairs
+  return (size_t)4 * sm_count * ((size_t)kTcRows * tokens + tokens);
 }
 
 cudaError_t configure_tc_kernels() {
@@ -479,8 +480,9 @@ cudaError_t launch_linear_tc(const LinearArgs& a, int epi, const TcPlan& p, floa
   // reduction by the last CTA of each tile)
   int splits = 1;
   const int tiles = (int)(grid.x * grid.y);
-  if (p.ws && tiles < p.sm_count) {
-    splits = std::min(p.sm_count / tiles, (a.K / kTcBlockK) / 4);
+  const int slots = p.sm_count * (BN <= 16 ? 2 : 1);  // resident CTAs
+  if (p.ws && tiles < slots) {
+    splits = std::min(slots / tiles, (a.K / kTcBlockK) / 4);
     splits = std::max(1, std::min(splits, p.max_splits));
     while (splits > 1 &&
            (size_t)tiles * splits * ((size_t)kTcRows * BN + BN) > p.ws_floats)
