@@ -231,9 +231,11 @@ __global__ void __launch_bounds__(kThreads) k_linear(LinearArgs a) {
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, float* xs, int halted);
 
-template <int KCH, int NR, bool ATTN = false>
+template <int KCH, int NR, bool ATTN = false, int MR = 1>
 __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* xs,
                                            float* inv_out, const AttnDecodeArgs* at = nullptr) {
+  // MR activation rows (1 for decode, 2 for the CodePredictor's 2-row
+  // prefill) share every weight load: MR dot products per weight row.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool swiglu = epi == EPI_SWIGLU;
   const int outs = swiglu ? 1 : NR;
@@ -260,74 +262,94 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
   // The halt flag is loaded alongside the input (not before it) and only
   // checked before the first write.
   const int halted = a.halt ? __ldcg(a.halt) : 0;
-  float* red = xs + K;
-  float ss = 0.f;
-  if (ATTN) stage_cp_attention(*at, xs, halted);
-  else
-  for (int k = threadIdx.x * 4; k < K; k += kThreads * 4) {
-    float4 v = __ldcg(reinterpret_cast<const float4*>(a.x + k));
-    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-    if (a.gamma) {
-      const float4 g = __ldg(reinterpret_cast<const float4*>(a.gamma + k));
-      v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+  float* red = xs + MR * K;  // [MR][kWarps] partial sums of squares
+  if (ATTN) {
+    stage_cp_attention(*at, xs, halted);
+  } else {
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      float ss = 0.f;
+      for (int k = threadIdx.x * 4; k < K; k += kThreads * 4) {
+        float4 v = __ldcg(reinterpret_cast<const float4*>(a.x + (long long)m * a.ldx + k));
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        if (a.gamma) {
+          const float4 g = __ldg(reinterpret_cast<const float4*>(a.gamma + k));
+          v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+        }
+        *reinterpret_cast<float4*>(xs + m * K + k) = v;
+      }
+      if (a.gamma) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[m * kWarps + warp] = ss;
+      }
     }
-    *reinterpret_cast<float4*>(xs + k) = v;
-  }
-  if (!ATTN && a.gamma) {
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
   }
   __syncthreads();
-  float sc = 1.0f;
-  if (!ATTN && a.gamma) {
-    float t = 0.f;
+  float sc[MR];
 #pragma unroll
-    for (int i = 0; i < kWarps; ++i) t += red[i];
-    sc = rsqrtf(t / (float)K + a.eps);
+  for (int m = 0; m < MR; ++m) {
+    sc[m] = 1.0f;
+    if (!ATTN && a.gamma) {
+      float t = 0.f;
+#pragma unroll
+      for (int i = 0; i < kWarps; ++i) t += red[m * kWarps + i];
+      sc[m] = rsqrtf(t / (float)K + a.eps);
+    }
   }
   if (halted) return false;
-  if (inv_out && threadIdx.x == 0) *inv_out = sc;
+  if (inv_out && threadIdx.x == 0) *inv_out = sc[0];
   if (a.trigger == 2) pdl_trigger();
   trace_mark(a.trace_id, 4);
-  float acc[NR];
+  float acc[MR][NR];
 #pragma unroll
-  for (int r = 0; r < NR; ++r) acc[r] = 0.f;
+  for (int m = 0; m < MR; ++m)
+#pragma unroll
+    for (int r = 0; r < NR; ++r) acc[m][r] = 0.f;
 #pragma unroll
   for (int j = 0; j < KCH; ++j) {
     const int k = j * 256 + lane * 8;
-    const float4 x0 = *reinterpret_cast<const float4*>(xs + k);
-    const float4 x1 = *reinterpret_cast<const float4*>(xs + k + 4);
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-      float f[8];
-      unpack8(w[r][j], f);
-      float t = acc[r];
-      t = fmaf(f[0], x0.x, t); t = fmaf(f[1], x0.y, t);
-      t = fmaf(f[2], x0.z, t); t = fmaf(f[3], x0.w, t);
-      t = fmaf(f[4], x1.x, t); t = fmaf(f[5], x1.y, t);
-      t = fmaf(f[6], x1.z, t); t = fmaf(f[7], x1.w, t);
-      acc[r] = t;
+    for (int m = 0; m < MR; ++m) {
+      const float4 x0 = *reinterpret_cast<const float4*>(xs + m * K + k);
+      const float4 x1 = *reinterpret_cast<const float4*>(xs + m * K + k + 4);
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        float f[8];
+        unpack8(w[r][j], f);
+        float t = acc[m][r];
+        t = fmaf(f[0], x0.x, t); t = fmaf(f[1], x0.y, t);
+        t = fmaf(f[2], x0.z, t); t = fmaf(f[3], x0.w, t);
+        t = fmaf(f[4], x1.x, t); t = fmaf(f[5], x1.y, t);
+        t = fmaf(f[6], x1.z, t); t = fmaf(f[7], x1.w, t);
+        acc[m][r] = t;
+      }
     }
   }
 #pragma unroll
-  for (int r = 0; r < NR; ++r) acc[r] = warp_sum(acc[r]);
+  for (int m = 0; m < MR; ++m)
+#pragma unroll
+    for (int r = 0; r < NR; ++r) acc[m][r] = warp_sum(acc[m][r]);
   trace_mark(a.trace_id, 5);
   if (lane == 0) {
-    if (swiglu) {
-      if (valid[0]) {
-        const float g = acc[0] * sc, u = acc[NR - 1] * sc;
-        a.y[c0] = g / (1.0f + expf(-g)) * u;
-      }
-    } else {
 #pragma unroll
-      for (int r = 0; r < NR; ++r) {
-        if (!valid[r]) continue;
-        const int c = c0 + r;
-        float out = acc[r] * sc;
-        if (epi == EPI_RESID) out += __ldcg(a.resid + c);
-        if (epi == EPI_BIAS) out += a.bias[c];
-        if (epi == EPI_BIAS_SILU) out = silu(out + a.bias[c]);
-        a.y[c] = out;
+    for (int m = 0; m < MR; ++m) {
+      float* y = a.y + (long long)m * a.ldy;
+      if (swiglu) {
+        if (valid[0]) {
+          const float g = acc[m][0] * sc[m], u = acc[m][NR - 1] * sc[m];
+          y[c0] = g / (1.0f + expf(-g)) * u;
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          if (!valid[r]) continue;
+          const int c = c0 + r;
+          float out = acc[m][r] * sc[m];
+          if (epi == EPI_RESID) out += __ldcg(a.resid + (long long)m * a.ldr + c);
+          if (epi == EPI_BIAS) out += a.bias[c];
+          if (epi == EPI_BIAS_SILU) out = silu(out + a.bias[c]);
+          y[c] = out;
+        }
       }
     }
   }
@@ -441,11 +463,11 @@ __global__ void __launch_bounds__(kThreads) k_gemv1_attn(LinearArgs a, AttnDecod
   gemv1_body<KCH, 1, true>(a, EPI_RESID, xs, nullptr, &at);
 }
 
-template <int KCH, int NR>
+template <int KCH, int NR, int MR>
 __global__ void __launch_bounds__(kThreads) k_gemv1(LinearArgs a, int epi) {
   QTTS_CRUMB(0, 6);
-  __shared__ __align__(16) float xs[KCH * 256 + 32];
-  gemv1_body<KCH, NR>(a, epi, xs, nullptr);
+  __shared__ __align__(16) float xs[MR * KCH * 256 + 32];
+  gemv1_body<KCH, NR, false, MR>(a, epi, xs, nullptr);
 }
 
 // Token selection and the gathers the next stage needs, for one sequence:
@@ -931,7 +953,13 @@ template <int KCH, int NR>
 cudaError_t launch_gemv1_t(const LinearArgs& a, int epi, cudaStream_t stream) {
   const int per_block = kWarps * (epi == EPI_SWIGLU ? 1 : NR);
   dim3 grid((a.N + per_block - 1) / per_block);
-  return launch(k_gemv1<KCH, NR>, grid, dim3(kThreads), 0, stream, a, epi);
+  if (a.M == 2) {
+    if constexpr (KCH <= 12)  // two rows of x must fit the 48 KB of static shared memory
+      return launch(k_gemv1<KCH, NR, 2>, grid, dim3(kThreads), 0, stream, a, epi);
+    else
+      return cudaErrorInvalidValue;
+  }
+  return launch(k_gemv1<KCH, NR, 1>, grid, dim3(kThreads), 0, stream, a, epi);
 }
 
 template <int KCH>
@@ -945,7 +973,8 @@ cudaError_t launch_gemv1_k(const LinearArgs& a, int epi, cudaStream_t stream) {
 
 // Decode GEMV dispatch on K (chunks of 256 per lane); false when K is unsupported.
 bool launch_gemv1(const LinearArgs& a, int epi, cudaStream_t stream, cudaError_t* err) {
-  if (a.M != 1 || a.K % 256 != 0) return false;
+  if (a.M < 1 || a.M > 2 || a.K % 256 != 0) return false;
+  if (a.M == 2 && a.K > 12 * 256) return false;  // two rows of x in 48 KB of static smem
   switch (a.K / 256) {
     case 1: *err = launch_gemv1_k<1>(a, epi, stream); return true;
     case 2: *err = launch_gemv1_k<2>(a, epi, stream); return true;
@@ -959,10 +988,10 @@ bool launch_gemv1(const LinearArgs& a, int epi, cudaStream_t stream, cudaError_t
 
 template <int EPI>
 cudaError_t launch_linear_epi(const LinearArgs& a, cudaStream_t stream) {
-  if (a.M == 1) {
+  if (a.M <= 2) {
     cudaError_t e;
     if (launch_gemv1(a, EPI, stream, &e)) return e;
-    return launch_linear_mt<1, EPI>(a, stream);
+    if (a.M == 1) return launch_linear_mt<1, EPI>(a, stream);
   }
   if (a.M == 2) return launch_linear_mt<2, EPI>(a, stream);
   return launch_linear_mt<8, EPI>(a, stream);
