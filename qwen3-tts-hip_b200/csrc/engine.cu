@@ -689,7 +689,10 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
       // split-K workspace for prefill GEMMs with few 128 x 128 tiles (short prompts)
       int sms = 148;
       QCK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-      tc.tokens = 128;
+      // 64-row token tiles: twice the CTAs of 128-row tiles for typical
+      // prompts, half the activation conversion per stage and CTA
+      tc.tokens = 64;
+      if (const char* tt = std::getenv("QTTS_TC_TOKENS")) tc.tokens = std::atoi(tt);
       tc.sm_count = sms;
       tc.max_splits = 8;
       tc.ws_floats = tc_workspace_floats(128, sms);

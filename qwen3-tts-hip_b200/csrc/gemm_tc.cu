@@ -449,7 +449,7 @@ bool tc_weight_map(const __nv_bfloat16* W, int rows, int K, CUtensorMap* out) {
 }
 
 bool tc_supported(const LinearArgs& a, int epi, const TcPlan& p) {
-  if (p.tokens != 16 && p.tokens != 128) return false;
+  if (p.tokens != 16 && p.tokens != 64 && p.tokens != 128) return false;
   if (a.K % kTcBlockK || a.ldx % 4 || (reinterpret_cast<uintptr_t>(a.x) & 15)) return false;
   return a.N % (kTcRows / 2) == 0 && a.M >= 1;
 }
@@ -462,6 +462,9 @@ size_t tc_workspace_floats(int tokens, int sm_count) {
 cudaError_t configure_tc_kernels() {
   cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)TcCfg<128>::kSmem);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)TcCfg<64>::kSmem);
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(k_gemm_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               (int)TcCfg<16>::kSmem);
@@ -493,6 +496,8 @@ cudaError_t launch_linear_tc(const LinearArgs& a, int epi, const TcPlan& p, floa
            a.bias, rms_out, err, a.halt, splits, p.ws, p.tickets};
   if (BN == 16)
     return launch(k_gemm_tc<16>, grid, dim3(kTcThreads), TcCfg<16>::kSmem, stream, wmap, t);
+  if (BN == 64)
+    return launch(k_gemm_tc<64>, grid, dim3(kTcThreads), TcCfg<64>::kSmem, stream, wmap, t);
   return launch(k_gemm_tc<128>, grid, dim3(kTcThreads), TcCfg<128>::kSmem, stream, wmap, t);
 }
 

@@ -18,7 +18,7 @@ constexpr int kTcRows = 128;      // weight rows per CTA (MMA M)
 
 // Launch plan of one engine's tensor-core projections.
 struct TcPlan {
-  int tokens;        // activation rows per CTA tile (MMA N): 128 (prefill) or 16 (batched decode)
+  int tokens;        // activation rows per CTA tile (MMA N): 64 or 128 (prefill), 16 (batched decode)
   // optional split-K workspace for skinny GEMMs (tc_workspace_floats) and
   // per-tile tickets (zero at rest)
   float* ws;
