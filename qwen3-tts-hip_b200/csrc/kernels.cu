@@ -865,21 +865,56 @@ __global__ void __launch_bounds__(128) k_attn_prefill(AttnPrefillArgs a) {
   const int q_out = a.q_heads * kHeadDim;
   float q[4], acc[4] = {0.f, 0.f, 0.f, 0.f};
   const float4 qv = *reinterpret_cast<const float4*>(a.q + (long long)m * q_out + qh * kHeadDim + 4 * lane);
-  q[0] = qv.x; q[1] = qv.y; q[2] = qv.z; q[3] = qv.w;
+  q[0] = qv.x * a.scale; q[1] = qv.y * a.scale; q[2] = qv.z * a.scale; q[3] = qv.w * a.scale;
   float mx = -INFINITY, l = 0.f;
-  for (int p = 0; p <= pos; ++p) {
-    const uint2 ku = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 0, kh, p) + 4 * lane);
-    const uint2 vu = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 1, kh, p) + 4 * lane);
-    float d = q[0] * bf16lo(ku.x) + q[1] * bf16hi(ku.x) + q[2] * bf16lo(ku.y) + q[3] * bf16hi(ku.y);
-    d = warp_sum(d) * a.scale;
-    const float mn = fmaxf(mx, d);
-    const float corr = expf(mx - mn), pe = expf(d - mn);
-    l = l * corr + pe;
-    acc[0] = acc[0] * corr + pe * bf16lo(vu.x);
-    acc[1] = acc[1] * corr + pe * bf16hi(vu.x);
-    acc[2] = acc[2] * corr + pe * bf16lo(vu.y);
-    acc[3] = acc[3] * corr + pe * bf16hi(vu.y);
-    mx = mn;
+  // positions 0..pos in batches of kAttnBatch: the next batch's K/V rows are
+  // loaded while this one is scored, and the softmax is updated once per batch
+  auto load = [&](int p0, uint2 (&ku)[kAttnBatch], uint2 (&vu)[kAttnBatch]) {
+#pragma unroll
+    for (int i = 0; i < kAttnBatch; ++i) {
+      const int p = p0 + i;
+      if (p <= pos) {
+        ku[i] = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 0, kh, p) + 4 * lane);
+        vu[i] = *reinterpret_cast<const uint2*>(kv_ptr(a.kv, a.layer, 1, kh, p) + 4 * lane);
+      } else {
+        ku[i] = vu[i] = make_uint2(0u, 0u);
+      }
+    }
+  };
+  uint2 ku[kAttnBatch], vu[kAttnBatch], nk[kAttnBatch], nv[kAttnBatch];
+  load(0, ku, vu);
+  for (int p0 = 0; p0 <= pos; p0 += kAttnBatch) {
+    if (p0 + kAttnBatch <= pos) load(p0 + kAttnBatch, nk, nv);
+    float d[kAttnBatch];
+#pragma unroll
+    for (int i = 0; i < kAttnBatch; ++i)
+      d[i] = q[0] * bf16lo(ku[i].x) + q[1] * bf16hi(ku[i].x) + q[2] * bf16lo(ku[i].y) +
+             q[3] * bf16hi(ku[i].y);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < kAttnBatch; ++i) d[i] += __shfl_xor_sync(0xffffffffu, d[i], o);
+    float mb = mx;
+#pragma unroll
+    for (int i = 0; i < kAttnBatch; ++i) {
+      if (p0 + i > pos) d[i] = -INFINITY;
+      mb = fmaxf(mb, d[i]);
+    }
+    const float corr = expf(mx - mb);  // mx = -inf on the first batch: corr = 0
+    float ls = 0.f, av[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < kAttnBatch; ++i) {
+      const float pe = expf(d[i] - mb);
+      ls += pe;
+      av[0] = fmaf(pe, bf16lo(vu[i].x), av[0]); av[1] = fmaf(pe, bf16hi(vu[i].x), av[1]);
+      av[2] = fmaf(pe, bf16lo(vu[i].y), av[2]); av[3] = fmaf(pe, bf16hi(vu[i].y), av[3]);
+    }
+    l = l * corr + ls;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] = acc[j] * corr + av[j];
+    mx = mb;
+#pragma unroll
+    for (int i = 0; i < kAttnBatch; ++i) { ku[i] = nk[i]; vu[i] = nv[i]; }
   }
   const float il = 1.0f / l;
   *reinterpret_cast<float4*>(a.out + (long long)m * q_out + qh * kHeadDim + 4 * lane) =
