@@ -339,6 +339,32 @@ def test_full_size_0p6b(pkg, tmp_path_factory):
     e.close()
 
 
+def test_full_size_1p7b(pkg, tmp_path_factory):
+    """BASELINE config 3 shapes (1.7B talker, CodePredictor behind the 2048->1024
+    projection): prefill logits, two greedy frames teacher-forced against the
+    oracle, and a two-request batch through the tensor-core path."""
+    d = synth.write_model(tmp_path_factory.mktemp("m17"), "1.7b", 0)
+    m = O.OracleModel(d, 128)
+    e = pkg.HipTtsEngine.load_with_options(d, pkg.EngineOptions(0, 128))
+    ids = np.random.default_rng(2).integers(0, 150000, 24)
+    pre, tr, pad = m.prepare(list(ids))
+    _, _, rl = m.talker_prefill(pre)
+    _, lg, _ = e.talker_prefill(pre.numpy())
+    assert np.abs(lg - rl).max() <= LOGIT_TOL
+    opts = pkg.GenerateOptions(decode_audio=False, do_sample=False, subtalker_dosample=False,
+                               repetition_penalty=1.0, max_frames=2)
+    out = e.generate_codes_from_ids(ids, opts)
+    codes, _, recs = m.rollout(pre, tr, pad, 2, GREEDY, GREEDY, forced_codes=out.codes)
+    assert_tokens_match(out.codes, codes, gaps_per_code(recs))
+    reqs = [ids, np.random.default_rng(3).integers(0, 150000, 40)]
+    outs = e.generate_codes_batch_from_ids(reqs, [opts, opts])
+    for r, o in zip(reqs, outs):
+        p2, t2, q2 = m.prepare(list(r))
+        c2, _, rec2 = m.rollout(p2, t2, q2, 2, GREEDY, GREEDY, forced_codes=o.codes)
+        assert_tokens_match(o.codes, c2, gaps_per_code(rec2))
+    e.close()
+
+
 @pytest.mark.parametrize("env_var,value", [("QTTS_FRAME_KERNEL", "1"), ("QTTS_FUSE_ATTN_O", "0"),
                                            ("QTTS_TC_CP", "1"), ("QTTS_TC", "0")])
 def test_alternate_path_parity(model_dirs, tmp_path, env_var, value):

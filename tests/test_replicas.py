@@ -33,7 +33,7 @@ def _rank(rank, world, port, out):
 def test_reduce_over_ranks_gloo():
     world = 2
     port = _free_port()
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         out = m.dict()
         mp.spawn(_rank, args=(world, port, out), nprocs=world, join=True)
         res = dict(out)
