@@ -108,6 +108,10 @@ __global__ void __launch_bounds__(kTcThreads, BN <= 16 ? 2 : 1)
   const int kb1 = (int)((long long)KB * (blockIdx.z + 1) / a.splits);
   const int nk = kb1 - kb0;
 
+  // Thread 0 (the weight producer) initialises the barriers and at once
+  // requests the first stages' weight tiles: they depend on nothing, and their
+  // latency then overlaps the TMEM allocation and the block barrier below.
+  const int pre = min(S, nk);
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -116,6 +120,12 @@ __global__ void __launch_bounds__(kTcThreads, BN <= 16 ? 2 : 1)
     }
     mbar_init(done, 1);
     fence_mbar_init();
+    for (int i = 0; i < pre; ++i) {
+      uint8_t* st = smem + i * Cfg::kStageBytes;
+      mbar_expect_tx(&full[i], kStageA);
+      tma_load_2d(st, &wmap, (kb0 + i) * kTcBlockK, row_a0, &full[i]);
+      tma_load_2d(st + kStageA / 2, &wmap, (kb0 + i) * kTcBlockK, row_a1, &full[i]);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_slot, Cfg::kTmemCols);
   tc_fence_before();
@@ -126,8 +136,8 @@ __global__ void __launch_bounds__(kTcThreads, BN <= 16 ? 2 : 1)
   if (warp == 0 && lane == 0) {
     // weights: they never depend on the previous kernel, so the first stages
     // are requested before the dependency wait
-    int issued = 0;
-    for (int i = 0; i < nk; ++i) {
+    int issued = pre;
+    for (int i = pre; i < nk; ++i) {
       const int s = i % S;
       if (i >= S && !mbar_wait_ns(&empty[s], ((i / S) & 1) ^ 1, kTcWaitNs)) {
         atomicExch(a.err, 1);
