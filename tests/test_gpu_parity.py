@@ -317,6 +317,16 @@ def test_eos_stops_generation(pkg, model_dirs, oracles, tmp_path):
         while (c := st.next_codes_chunk(3)) is not None:
             n += c.frames
         assert n == out.frames and st.finish_codes().ended_by_eos
+    # the same model served as a batch: each request halts on its own EOS
+    # while the others keep stepping (halted rows are skipped on the device)
+    reqs = [ids, ids_for(13, 9), ids_for(14, 6)]
+    outs = e.generate_codes_batch_from_ids(reqs, [opts] * len(reqs))
+    for r, o in zip(reqs, outs):
+        p2, t2, q2 = m.prepare(list(r))
+        c2, ended2, rec2 = m.rollout(p2, t2, q2, 20, GREEDY, GREEDY, forced_codes=o.codes)
+        assert o.ended_by_eos == ended2
+        assert o.frames == len(c2) // 16
+        assert_tokens_match(o.codes, c2, gaps_per_code(rec2))
     e.close()
 
 
