@@ -217,10 +217,11 @@ int32_t qtts_talker_decode_step(qtts_engine* engine, const float* input, size_t 
                                 float* hidden_out, float* logits_out, int32_t* token_out);
 /* Same computation as qtts_talker_decode_step, for callers that may not
  * allocate device memory while running (fixed-budget or real-time hosts):
- * this call allocates nothing. The decode attention's scratch (split-K
- * partials and completion counters) comes from a static device array of
- * 264 KiB held by every GPU that loads the library; talkers whose
- * q_heads * 16 * 130 floats exceed it are rejected with QTTS_ERR_INVALID_INPUT.
+ * this call allocates nothing. Its working memory (the input row and every
+ * layer's projections, attention output and MLP activations) comes from a
+ * static device array of 264 KiB held by every GPU that loads the library;
+ * talkers whose step activations exceed it are rejected with
+ * QTTS_ERR_INVALID_INPUT.
  * The first call on a device looks up the array's address (make it before
  * any stream capture). Calls share the array: calls that overlap on the GPU
  * race. No counterpart in the reference. */

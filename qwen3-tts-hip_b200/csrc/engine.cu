@@ -56,7 +56,6 @@ struct QttsError : std::runtime_error {
 constexpr uint64_t kSeedXor = 0x9e3779b97f4a7c15ull;  // generation.rs:667
 constexpr int kNewline = 198;                          // text.rs:15
 constexpr int kTalkerPageShift = 5;                    // 32 positions per KV page
-constexpr int kTalkerSplits = 16;                      // decode attention splits
 constexpr int kFrameTalkerSplits = 4;                  // frame kernel talker attention splits
 
 // ---------------------------------------------------------------------------
@@ -287,7 +286,7 @@ class Engine {
   // workspaces
   StackBufs tb{}, cb{};
   KvView tkv{}, ckv{};
-  float *partial = nullptr, *logits = nullptr, *dbg_logits = nullptr;
+  float *logits = nullptr, *dbg_logits = nullptr;
   unsigned* tickets = nullptr;
   SeqState* st = nullptr;
   SeqState* st_host = nullptr;  // pinned
@@ -426,7 +425,7 @@ class Engine {
   }
   void stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int pos0, const int* halt);
   void stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* pos_ptr, int pos_const,
-                  int nsplit, const int* halt);
+                  const int* halt);
   HeadArgs head_args(int role, const SampleCfg& c, const int* halt);
   void talker_head(int role, const float* x, const SampleCfg& c, float penalty, const int* halt,
                    float* cp_prefix_dst);
@@ -728,8 +727,6 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
     ckv.pool = arena.alloc<__nv_bfloat16>((size_t)ckv.page_stride);
     ckv.page_table = arena.alloc<int>(1);
   }
-  partial = arena.alloc<float>((size_t)std::max(T.q_heads, C.q_heads) * kTalkerSplits *
-                               (2 + kHeadDim));
   logits = arena.alloc<float>(std::max(T.vocab, C.vocab));
   dbg_logits = arena.alloc<float>((size_t)na * C.vocab);
   tickets = arena.alloc<unsigned>(64);
@@ -849,7 +846,7 @@ void Engine::stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int 
 
 // One position through all layers (decode_step_layer_on_stream, decode.rs:1694-1894).
 void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* pos_ptr,
-                        int pos_const, int nsplit, const int* halt) {
+                        int pos_const, const int* halt) {
   const StackCfg& c = S.c;
   const float scale = 1.0f / std::sqrt((float)c.head_dim);
   for (int l = 0; l < c.layers; ++l) {
@@ -857,7 +854,7 @@ void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* 
            S.qkv_w, c.hidden, EPI_STORE, halt);
     AttnDecodeArgs da{B.qkv,   S.q_g[l],  S.k_g[l], c.eps,   S.rope_cos, S.rope_sin,
                       kv,      l,         pos_ptr,  pos_const, c.q_heads, scale,
-                      partial, tickets + 8, B.attn, nsplit,  halt};
+                      B.attn,  halt};
     LinearArgs o{S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden,
                  nullptr, 1, c.hidden, S.q_out, halt};
     if (fuse_attn_o && attn_o_fusable(da, o)) {
@@ -867,7 +864,7 @@ void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* 
       QCK(launch_attn_o(da, o, stream));  // attention inside the O projection's staging
       ++launches;
     } else {
-      da.trace_id = trace_tag("attn", c.q_heads, nsplit);
+      da.trace_id = trace_tag("attn", c.q_heads, 1);
       QCK(launch_attn_decode(da, stream));
       ++launches;
       linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, 1,
@@ -951,11 +948,11 @@ void Engine::enqueue_frame(const SampleKey& k) {
     if (has_proj())
       linear(proj_w, cp_next, H, nullptr, 0.f, cb.x, C.hidden, nullptr, 0, proj_b, 1, C.hidden,
              H, EPI_BIAS, halt);
-    stack_step(cp, cb, ckv, nullptr, g + 1, 1, halt);
+    stack_step(cp, cb, ckv, nullptr, g + 1, halt);
     cp_head(g, cb.x, k.s, halt);
   }
   if (!k.last) {
-    stack_step(talker, tb, tkv, &st->talker_pos, 0, kTalkerSplits, halt);
+    stack_step(talker, tb, tkv, &st->talker_pos, 0, halt);
     talker_head(ROLE_TALKER_STEP, tb.x, k.t, k.penalty, halt, cp_prefix_target());
   }
 }
@@ -1507,7 +1504,6 @@ void Engine::batch_stack_step(DevStack& S, StackBufs& B, const KvView& kv, int p
     da.q_heads = c.q_heads;
     da.scale = scale;
     da.out = B.attn;
-    da.nsplit = 1;
     da.halt = &bt.st[0].halt;
     da.qkv_ld = S.qkv_w;
     da.out_ld = S.q_out;
@@ -2290,7 +2286,7 @@ int32_t qtts_talker_decode_step(qtts_engine* h, const float* input, size_t offse
     e.st_host->frames = 0;
     QCK(cudaMemcpy(e.st, e.st_host, sizeof(qtts::SeqState), cudaMemcpyHostToDevice));
     qtts::SampleCfg greedy{0, 0, 1.f, 1.f};
-    e.stack_step(e.talker, e.tb, e.tkv, &e.st->talker_pos, 0, qtts::kTalkerSplits, nullptr);
+    e.stack_step(e.talker, e.tb, e.tkv, &e.st->talker_pos, 0, nullptr);
     e.talker_head(qtts::ROLE_TALKER_STEP, e.tb.x, greedy, 1.0f, nullptr, e.cp_prefix_target());
     e.sync_state();
     if (token_out) *token_out = e.st_host->semantic;
@@ -2309,19 +2305,20 @@ int32_t qtts_talker_decode_step(qtts_engine* h, const float* input, size_t offse
 // once they are running: a caller that owns a fixed memory budget carved out
 // up front (a real-time audio process, a pool-managed serving runtime, or a
 // host that forbids cudaMalloc outside start-up because it synchronises the
-// device). For them, the talker decode step's only per-call scratch -- the
-// split-K partials and the completion counters of the decode attention kernel
-// -- lives in this file-scope device array instead of engine-owned memory.
-// The array is fixed at kStaticAttnScratchBytes and is held by every GPU that
-// loads the library until the process exits. All calls share it and it keeps
-// the last call's contents; calls that overlap on the GPU (two streams, two
-// engines, two threads) race on it and must be serialised by the caller.
+// device). For them, the talker decode step's per-call working memory -- the
+// input row, the QKV projections, the attention output and the MLP
+// activations of every layer -- lives in this file-scope device array instead
+// of engine-owned memory (the KV cache, weights and logits are the engine's,
+// allocated at load). The array is fixed at kStaticScratchBytes and is held by
+// every GPU that loads the library until the process exits. All calls share it
+// and it keeps the last call's contents; calls that overlap on the GPU (two
+// streams, two engines, two threads) race on it and must be serialised by the
+// caller.
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr size_t kStaticAttnScratchBytes = 270336;  // 264 KiB
-constexpr size_t kStaticTicketBytes = 256;          // 64 counters at the front
-static __device__ __align__(256) unsigned char g_attn_scratch[kStaticAttnScratchBytes];
+constexpr size_t kStaticScratchBytes = 270336;  // 264 KiB
+static __device__ __align__(256) float g_step_scratch[kStaticScratchBytes / sizeof(float)];
 
 std::mutex g_static_mu;
 void* g_static_ptr[128] = {};
@@ -2333,7 +2330,7 @@ void* static_scratch_for_device(int device) {
   if (device < 0 || device >= 128) qtts::invalid("device index out of range");
   if (!g_static_ptr[device]) {
     void* ptr = nullptr;
-    QCK(cudaGetSymbolAddress(&ptr, g_attn_scratch));
+    QCK(cudaGetSymbolAddress(&ptr, g_step_scratch));
     g_static_ptr[device] = ptr;
   }
   return g_static_ptr[device];
@@ -2351,33 +2348,47 @@ int32_t qtts_talker_decode_step_static(qtts_engine* h, const float* input, size_
     need(input, "input");
     if (offset >= e.max_cache_steps) qtts::invalid("offset outside cache length");
     const auto& c = e.talker.c;
-    const size_t need_bytes =
-        (size_t)c.q_heads * qtts::kTalkerSplits * (2 + qtts::kHeadDim) * sizeof(float);
-    if (need_bytes > kStaticAttnScratchBytes - kStaticTicketBytes || c.kv_heads > 64)
-      qtts::invalid("talker needs " + std::to_string(need_bytes) +
-                    " bytes of attention scratch; the static array holds " +
-                    std::to_string(kStaticAttnScratchBytes - kStaticTicketBytes));
-    unsigned char* base = static_cast<unsigned char*>(static_scratch_for_device(e.device));
-    unsigned* tick = reinterpret_cast<unsigned*>(base);
-    float* part = reinterpret_cast<float*>(base + kStaticTicketBytes);
+    qtts::DevStack& S = e.talker;
     const size_t H = c.hidden;
-    // counters must start at zero; a previous call may have been interrupted
-    QCK(cudaMemsetAsync(tick, 0, kStaticTicketBytes, e.stream));
-    QCK(cudaMemcpy(e.tb.x, input, H * 4, cudaMemcpyHostToDevice));
+    // step activations, each 64-float aligned: x, qkv, attention, h1, MLP
+    auto up = [](size_t n) { return (n + 63) / 64 * 64; };
+    const size_t nx = up(H), nqkv = up(S.qkv_w), nattn = up(S.q_out), nh1 = up(H),
+                 nact = up(c.intermediate);
+    const size_t need_bytes = (nx + nqkv + nattn + nh1 + nact) * sizeof(float);
+    if (need_bytes > kStaticScratchBytes)
+      qtts::invalid("talker step needs " + std::to_string(need_bytes) +
+                    " bytes of activations; the static array holds " +
+                    std::to_string(kStaticScratchBytes));
+    float* base = static_cast<float*>(static_scratch_for_device(e.device));
+    qtts::StackBufs B{};
+    B.x = base;
+    B.qkv = B.x + nx;
+    B.attn = B.qkv + nqkv;
+    B.h1 = B.attn + nattn;
+    B.act = B.h1 + nh1;
+    QCK(cudaMemcpy(B.x, input, H * 4, cudaMemcpyHostToDevice));
     e.st_host->talker_pos = (int)offset;
     e.st_host->halt = 0;
     e.st_host->frames = 0;
     QCK(cudaMemcpy(e.st, e.st_host, sizeof(qtts::SeqState), cudaMemcpyHostToDevice));
     const float scale = 1.0f / std::sqrt((float)c.head_dim);
-    qtts::DevStack& S = e.talker;
-    qtts::StackBufs& B = e.tb;
     for (int l = 0; l < c.layers; ++l) {
       e.linear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr, 1,
                S.qkv_w, c.hidden, qtts::EPI_STORE, nullptr);
-      qtts::AttnDecodeArgs da{B.qkv, S.q_g[l], S.k_g[l], c.eps, S.rope_cos, S.rope_sin,
-                              e.tkv, l, &e.st->talker_pos, 0, c.q_heads, scale,
-                              part, tick, B.attn, qtts::kTalkerSplits, nullptr};
-      QCK(qtts::launch_attn_decode(da, e.stream));
+      qtts::AttnDecodeArgs da{};
+      da.qkv = B.qkv;
+      da.q_gamma = S.q_g[l];
+      da.k_gamma = S.k_g[l];
+      da.eps = c.eps;
+      da.rope_cos = S.rope_cos;
+      da.rope_sin = S.rope_sin;
+      da.kv = e.tkv;
+      da.layer = l;
+      da.pos_ptr = &e.st->talker_pos;
+      da.q_heads = c.q_heads;
+      da.scale = scale;
+      da.out = B.attn;
+        QCK(qtts::launch_attn_decode(da, e.stream));
       e.linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, 1,
                c.hidden, S.q_out, qtts::EPI_RESID, nullptr);
       e.linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
@@ -2386,7 +2397,7 @@ int32_t qtts_talker_decode_step_static(qtts_engine* h, const float* input, size_
                nullptr, 1, c.hidden, c.intermediate, qtts::EPI_RESID, nullptr);
     }
     qtts::SampleCfg greedy{0, 0, 1.f, 1.f};
-    e.talker_head(qtts::ROLE_TALKER_STEP, e.tb.x, greedy, 1.0f, nullptr, e.cp_prefix_target());
+    e.talker_head(qtts::ROLE_TALKER_STEP, B.x, greedy, 1.0f, nullptr, e.cp_prefix_target());
     e.sync_state();
     if (token_out) *token_out = e.st_host->semantic;
     if (hidden_out) QCK(cudaMemcpy(hidden_out, e.cp_prefix_target(), H * 4, cudaMemcpyDeviceToHost));
@@ -2431,7 +2442,7 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
       if (e.has_proj())
         e.linear(e.proj_w, e.cp_next, H, nullptr, 0.f, e.cb.x, C.hidden, nullptr, 0, e.proj_b, 1,
                  C.hidden, H, qtts::EPI_BIAS, nullptr);
-      e.stack_step(e.cp, e.cb, e.ckv, nullptr, g + 1, 1, nullptr);
+      e.stack_step(e.cp, e.cb, e.ckv, nullptr, g + 1, nullptr);
       e.cp_head(g, e.cb.x, sc, nullptr);
       QCK(cudaMemcpyAsync(e.dbg_logits + (size_t)g * C.vocab, e.logits, C.vocab * 4,
                                 cudaMemcpyDeviceToDevice, e.stream));

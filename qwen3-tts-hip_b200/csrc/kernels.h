@@ -130,10 +130,7 @@ struct AttnDecodeArgs {
   int pos_const;
   int q_heads;
   float scale;
-  float* partial;          // [q_heads, nsplit, 2 + 128]
-  unsigned* tickets;       // [kv_heads]
   float* out;              // [q_heads * 128]
-  int nsplit;
   const int* halt;
   int trace_id;
   // Batched decode (sequence b = blockIdx.y; all zero for one sequence):

@@ -2,8 +2,8 @@
 
 It exists for hosts that may not allocate device memory once running; it must
 give the same hidden state, logits and token as qtts_talker_decode_step. Two
-calls in a row are checked, so the second call sees the static scratch the
-first one left behind. Collected last on purpose (file name)."""
+calls in a row are checked, so the second call sees the static working
+memory the first one left behind. Collected last on purpose (file name)."""
 import numpy as np
 import pytest
 
