@@ -291,6 +291,7 @@ def main():
         dist.barrier()
 
     eng = pkg.HipTtsEngine.load_with_options(mdir, pkg.EngineOptions(local, 512))
+    workload["fused_mlp_cluster"] = list(eng.info.fused_mlp_cluster)  # talker, CodePredictor
     opts = options(pkg, c, seed=rank)
     if reqs is not None:
         bopts = [options(pkg, c, seed=b) for b in range(batch)]

@@ -107,6 +107,9 @@ typedef struct {
   uint32_t codec_eos;
   size_t max_cache_steps;
   size_t device_bytes; /* weights + KV + workspaces held on the device */
+  /* Decode MLP of the talker [0] and the CodePredictor [1]: CTAs per cluster of
+   * the fused gate|up + down kernel, 0 when it runs as two GEMVs. */
+  int32_t fused_mlp_cluster[2];
 } qtts_engine_info;
 
 const char* qtts_last_error(void);

@@ -239,6 +239,7 @@ struct DevStack {
   StackCfg c;
   int q_out, kv_out, qkv_w;
   std::vector<__nv_bfloat16*> wqkv, wo, wgu, wdown;
+  std::vector<__nv_bfloat16*> wdownT;  // [I, H] copies for the fused decode MLP (empty: unused)
   std::vector<float*> in_g, post_g, q_g, k_g;
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
@@ -320,6 +321,13 @@ class Engine {
   };
   // CodePredictor attention inside the O projection (QTTS_FUSE_ATTN_O=0: separate kernels)
   bool fuse_attn_o = true;
+  // Fused decode MLP (QTTS_FUSE_MLP=1; default: gate|up and down as two
+  // GEMVs); used for a stack when its shape fits and all its clusters can be
+  // resident at once.
+  float* mlp_ws = nullptr;
+  unsigned* mlp_tickets = nullptr;
+  int* mlp_err = nullptr;
+  int mlp_cluster[2] = {0, 0};  // talker, CodePredictor: cluster size, 0 = not fused
   unsigned* frame_seq = nullptr;
   int* frame_error = nullptr;
   unsigned* frame_counters = nullptr;
@@ -365,6 +373,25 @@ class Engine {
     plan_prefetch(a, (size_t)(epi == EPI_SWIGLU ? 2 : 1) * N * K * sizeof(__nv_bfloat16));
     QCK(launch_linear(a, epi, stream));
     ++launches;
+  }
+
+  // Post-attention half of a decode layer for one row: B.x = B.h1 + MLP(B.h1).
+  void mlp(const DevStack& S, int l, StackBufs& B, const int* halt) {
+    const StackCfg& c = S.c;
+    if (!S.wdownT.empty()) {
+      MlpArgs m{S.wgu[l], S.wdownT[l], B.h1, S.post_g[l], c.eps, B.x, mlp_ws, mlp_tickets,
+                c.hidden, c.intermediate, halt, mlp_err};
+      m.trace_id = trace_tag("mlp", c.intermediate, c.hidden);
+      m.cluster = &S == &talker ? mlp_cluster[0] : mlp_cluster[1];
+      m.trigger = trigger_mode;
+      QCK(launch_mlp_fused(m, stream));
+      ++launches;
+      return;
+    }
+    linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
+           nullptr, 1, c.intermediate, c.hidden, EPI_SWIGLU, halt);
+    linear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.x, c.hidden, B.h1, c.hidden,
+           nullptr, 1, c.hidden, c.intermediate, EPI_RESID, halt);
   }
 
   // ---- L2 prefetch plan ----
@@ -755,7 +782,7 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
     use_frame_kernel = env && env[0] == '1';
     if (const char* tp = std::getenv("QTTS_STEP_TRACE")) {
       step_trace_path = tp;
-      step_trace = arena.alloc<unsigned long long>(6 * (size_t)kTraceCap);
+      step_trace = arena.alloc<unsigned long long>(8 * (size_t)kTraceCap);
     }
     if (const char* cr = std::getenv("QTTS_CRUMBS"); cr && cr[0] == '1') {
       QCK(cudaHostAlloc(&crumbs_host, 64, cudaHostAllocMapped));
@@ -769,6 +796,36 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
       pf_ahead = (size_t)std::max(0, std::atoi(pa)) << 20;
     const char* fz = std::getenv("QTTS_FUSE_ATTN_O");
     fuse_attn_o = !(fz && fz[0] == '0');
+    // Opt-in: measured slower than the two GEMVs on B200 (its cross-CTA
+    // reduction adds more L2 round trips than the launch it removes).
+    const char* fm = std::getenv("QTTS_FUSE_MLP");
+    if (fm && fm[0] == '1') {
+      for (DevStack* S : {&talker, &cp}) {
+        const int H = S->c.hidden, I = S->c.intermediate;
+        if (!mlp_fused_supported(H, I)) continue;
+        // Largest cluster size whose clusters all fit on the GPU at once.
+        int& cl = &*S == &talker ? mlp_cluster[0] : mlp_cluster[1];
+        for (int c : {8, 4, 2}) {
+          int resident = 0;
+          QCK(configure_mlp_fused(H, I, c, &resident));
+          if (resident >= kMlpCtas / c) { cl = c; break; }
+        }
+        if (!cl) continue;
+        for (int l = 0; l < S->c.layers; ++l) {
+          __nv_bfloat16* t = arena.alloc<__nv_bfloat16>((size_t)I * H);
+          QCK(launch_transpose_bf16(S->wdown[l], H, I, t, stream));
+          S->wdownT.push_back(t);
+        }
+        if (!mlp_ws) {
+          mlp_ws = arena.alloc<float>((size_t)(kMlpCtas / 2) * std::max(T.hidden, C.hidden));
+          mlp_tickets = arena.alloc<unsigned>(kMlpMaxCluster);
+          mlp_err = arena.alloc<int>(1);
+          QCK(cudaMemsetAsync(mlp_tickets, 0, kMlpMaxCluster * sizeof(unsigned), stream));
+          QCK(cudaMemsetAsync(mlp_err, 0, sizeof(int), stream));
+        }
+      }
+      QCK(cudaStreamSynchronize(stream));
+    }
     frame_grid = frame_grid_size(dev);
     if (const char* g = std::getenv("QTTS_FRAME_GRID"))  // profiling aid: fewer CTAs
       frame_grid = std::min(frame_grid, std::atoi(g));
@@ -870,10 +927,7 @@ void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* 
       linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, 1,
              c.hidden, S.q_out, EPI_RESID, halt);
     }
-    linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
-           nullptr, 1, c.intermediate, c.hidden, EPI_SWIGLU, halt);
-    linear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.x, c.hidden, B.h1, c.hidden,
-           nullptr, 1, c.hidden, c.intermediate, EPI_RESID, halt);
+    mlp(S, l, B, halt);
   }
 }
 
@@ -1346,6 +1400,11 @@ void Engine::sync_state() {
   QCK(cudaStreamSynchronize(stream));
   if (st_host->error)
     fail(QTTS_ERR_DEVICE_STATE, "cannot sample from logits with no finite values");
+  if (mlp_err) {
+    int e = 0;
+    QCK(cudaMemcpy(&e, mlp_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) fail(QTTS_ERR_DEVICE_STATE, "fused MLP weight copies timed out");
+  }
   if (tc_err) {
     int e = 0;
     QCK(cudaMemcpy(&e, tc_err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -1374,7 +1433,7 @@ size_t Engine::run_frames(size_t n) {
     if (trace_now) {
       QCK(cudaMemsetAsync(step_trace, 0xff, 2 * kTraceCap * sizeof(unsigned long long), stream));
       QCK(cudaMemsetAsync(step_trace + 2 * kTraceCap, 0,
-                          4 * kTraceCap * sizeof(unsigned long long), stream));
+                          6 * kTraceCap * sizeof(unsigned long long), stream));
       QCK(set_step_trace(step_trace, kTraceCap, stream));
     }
     QCK(cudaGraphLaunch(is_last ? gl : gf, stream));
@@ -1402,19 +1461,21 @@ size_t Engine::run_frames(size_t n) {
 }
 
 void Engine::dump_step_trace() {
-  std::vector<unsigned long long> t(6 * (size_t)kTraceCap);
+  std::vector<unsigned long long> t(8 * (size_t)kTraceCap);
   QCK(cudaMemcpy(t.data(), step_trace, t.size() * sizeof(unsigned long long),
                  cudaMemcpyDeviceToHost));
   FILE* f = std::fopen(step_trace_path.c_str(), "w");
   if (!f) return;
-  std::fprintf(f, "# id entry wait exit last_wait sel_start sel_end name (ns after the first entry)\n");
+  std::fprintf(f, "# id entry wait exit last_wait mark4 mark5 (ns after the first entry) "
+                  "dur6 dur7 (ns after a CTA's own wait, max over CTAs) name\n");
   unsigned long long t0 = ~0ull;
   for (size_t i = 1; i <= trace_names.size(); ++i) t0 = std::min(t0, t[i]);
   for (size_t i = 1; i <= trace_names.size(); ++i) {
     auto rel = [&](unsigned long long v) { return v == ~0ull || v == 0 ? -1LL : (long long)(v - t0); };
-    std::fprintf(f, "%zu %lld %lld %lld %lld %lld %lld %s\n", i, rel(t[i]), rel(t[kTraceCap + i]),
-                 rel(t[2 * kTraceCap + i]), rel(t[3 * kTraceCap + i]), rel(t[4 * kTraceCap + i]),
-                 rel(t[5 * kTraceCap + i]), trace_names[i - 1].c_str());
+    std::fprintf(f, "%zu %lld %lld %lld %lld %lld %lld %llu %llu %s\n", i, rel(t[i]),
+                 rel(t[kTraceCap + i]), rel(t[2 * kTraceCap + i]), rel(t[3 * kTraceCap + i]),
+                 rel(t[4 * kTraceCap + i]), rel(t[5 * kTraceCap + i]), t[6 * kTraceCap + i],
+                 t[7 * kTraceCap + i], trace_names[i - 1].c_str());
   }
   std::fclose(f);
 }
@@ -1876,7 +1937,7 @@ long long next_trailing_id(qtts::TextStream& s) {
 extern "C" {
 
 const char* qtts_last_error(void) { return qtts::g_last_error.c_str(); }
-int32_t qtts_abi_version(void) { return 1; }
+int32_t qtts_abi_version(void) { return 2; }
 
 void qtts_generate_options_default(qtts_generate_options* o) {
   if (!o) return;
@@ -1947,6 +2008,8 @@ int32_t qtts_engine_get_info(const qtts_engine* h, qtts_engine_info* out) {
     out->codec_eos = e.cfg.codec_eos;
     out->max_cache_steps = e.max_cache_steps;
     out->device_bytes = e.arena.bytes();
+    out->fused_mlp_cluster[0] = e.mlp_cluster[0];
+    out->fused_mlp_cluster[1] = e.mlp_cluster[1];
   });
 }
 

@@ -57,6 +57,19 @@ __device__ __forceinline__ void trace_mark(int id, int slot) {
   else atomicMin(t.buf + slot * t.cap + id, now);
 }
 
+__device__ __forceinline__ unsigned long long trace_clock(int id) {
+  unsigned long long now = 0;
+  if (id > 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+  return now;
+}
+// Slots 6 and 7: max over CTAs of the time since t0 (the CTA's own wait).
+__device__ __forceinline__ void trace_dur(int id, int slot, unsigned long long t0) {
+  if (id <= 0 || threadIdx.x != 0) return;
+  const StepTrace t = g_trace;
+  if (!t.buf || id >= t.cap) return;
+  atomicMax(t.buf + slot * t.cap + id, trace_clock(id) - t0);
+}
+
 // This CTA's share of the op's L2 prefetch ranges (warp 0, 4 KB per bulk
 // prefetch; fire-and-forget, so it never delays the kernel).
 __device__ __forceinline__ void l2_prefetch_share(const LinearArgs& a, int cta, int ncta) {
@@ -229,7 +242,8 @@ __global__ void __launch_bounds__(kThreads) k_linear(LinearArgs a) {
 // SWIGLU: the warp's two rows are gate row c and up row N + c.
 // `xs` holds KCH * 256 floats + 32 words of reduction scratch.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, float* xs, int halted);
+__device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, float* xs, int halted,
+                                                   int trace_id, unsigned long long tw);
 
 template <int KCH, int NR, bool ATTN = false, int MR = 1>
 __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* xs,
@@ -258,13 +272,14 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
   if (a.trigger == 0) pdl_trigger();
   pdl_wait();
   trace_mark(a.trace_id, 1);
+  const unsigned long long tw = trace_clock(a.trace_id);
   if (a.trigger == 1) pdl_trigger();
   // The halt flag is loaded alongside the input (not before it) and only
   // checked before the first write.
   const int halted = a.halt ? __ldcg(a.halt) : 0;
   float* red = xs + MR * K;  // [MR][kWarps] partial sums of squares
   if (ATTN) {
-    stage_cp_attention(*at, xs, halted);
+    stage_cp_attention(*at, xs, halted, a.trace_id, tw);
   } else {
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
@@ -364,7 +379,8 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
 // the standalone decode-attention kernel; CTA 0 appends the row to the cache.
 constexpr int kCpFusedPositions = 16;
 
-__device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, float* xs, int halted) {
+__device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, float* xs, int halted,
+                                                   int trace_id, unsigned long long tw) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pos = at.pos_const, T = pos + 1;
   const int kvh = at.kv.kv_heads;
@@ -426,6 +442,7 @@ __device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, flo
         d[j][p] = (q[j].x * at.scale) * k0 + (q[j].y * at.scale) * k1 +
                   (q[j].z * at.scale) * k2 + (q[j].w * at.scale) * k3;
     }
+    trace_dur(trace_id, 6, tw);  // cached rows and projections in registers
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
@@ -454,6 +471,7 @@ __device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, flo
           make_float4(acc[0] * il, acc[1] * il, acc[2] * il, acc[3] * il);
     }
   }
+  trace_dur(trace_id, 7, tw);  // warp 0's heads done
 }
 
 template <int KCH>
@@ -1148,3 +1166,5 @@ cudaError_t launch_assemble_rows(const float* proj, const int* proj_index,
 }
 
 }  // namespace qtts
+
+#include "mlp.cuh"

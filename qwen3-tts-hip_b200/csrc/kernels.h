@@ -168,7 +168,40 @@ struct AttnPrefillArgs {
   const int* halt;
 };
 
+// Fused decode MLP (gate|up GEMV, SwiGLU, down GEMV + residual in one
+// kernel): kMlpCtas CTAs in clusters of 8, 4 or 2, CTA j owning intermediate
+// channels [j*I/kMlpCtas, (j+1)*I/kMlpCtas).
+constexpr int kMlpCtas = 128;
+constexpr int kMlpMaxCluster = 8;
+constexpr size_t kMlpMaxSmem = 200 * 1024;
+
+struct MlpArgs {
+  const __nv_bfloat16* Wgu;  // [2I, H]: gate rows then up rows
+  const __nv_bfloat16* WdT;  // [I, H]: down_proj.weight transposed
+  const float* x;            // [H] residual input r (normalised inside)
+  const float* gamma;        // [H] post-attention RMSNorm gamma
+  float eps;
+  float* y;                  // [H] r + down(silu(gate) * up); must not alias x
+  float* ws;                 // [kMlpCtas / cluster, H] cluster partial sums
+  unsigned* tickets;         // [cluster] zero-initialised, reset by the kernel
+  int H, I;
+  const int* halt;
+  int* err;                  // set to 7 if the weight copies never land
+  int trace_id;
+  int trigger;
+  int cluster;               // CTAs per cluster: 8, 4 or 2
+};
+
 cudaError_t launch_linear(const LinearArgs& a, Epilogue epi, cudaStream_t stream);
+bool mlp_fused_supported(int H, int I);
+size_t mlp_fused_smem(int H, int I);
+// Sets the shared-memory limit of the kernel for this shape and cluster size;
+// reports how many such clusters can be resident at once.
+cudaError_t configure_mlp_fused(int H, int I, int cluster, int* active_clusters);
+cudaError_t launch_mlp_fused(const MlpArgs& a, cudaStream_t stream);
+// dst[c, r] = src[r, c] of a [rows x cols] bf16 matrix.
+cudaError_t launch_transpose_bf16(const __nv_bfloat16* src, int rows, int cols,
+                                  __nv_bfloat16* dst, cudaStream_t stream);
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t stream);
 // CodePredictor decode attention fused into the O projection (o.x unused,
 // o.resid = residual); only for a fixed position below 16 and two q heads per
@@ -180,9 +213,11 @@ cudaError_t launch_select_batch(const BatchHeadArgs& a, int B, cudaStream_t stre
 // Debugging aid: device pointer of mapped host memory for kernel breadcrumbs.
 cudaError_t set_crumbs_kernels(unsigned* host_mapped_dev_ptr);
 cudaError_t set_crumbs_gemm(unsigned* host_mapped_dev_ptr);
-// Step trace buffer: [6][capacity] u64 globaltimer values (first entry, first
-// post-wait, last exit, last post-wait, head selection start/end) indexed by
-// trace_id; nullptr disables. Stream-ordered.
+// Step trace buffer: [8][capacity] u64 indexed by trace_id: globaltimer values
+// (first entry, first post-wait, last exit, last post-wait, two kernel-specific
+// marks taken by the last CTA) and two kernel-specific durations (max over
+// CTAs of the time since the CTA's own dependency wait); nullptr disables.
+// Stream-ordered.
 cudaError_t set_step_trace(unsigned long long* buf, int capacity, cudaStream_t stream);
 cudaError_t launch_qk_prep(const QkPrepArgs& a, cudaStream_t stream);
 cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t stream);

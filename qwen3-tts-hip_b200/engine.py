@@ -81,7 +81,7 @@ class _Info(C.Structure):
                 ("cp_vocab", C.c_uint32), ("num_code_groups", C.c_uint32),
                 ("talker_layers", C.c_uint32), ("cp_layers", C.c_uint32),
                 ("codec_eos", C.c_uint32), ("max_cache_steps", C.c_size_t),
-                ("device_bytes", C.c_size_t)]
+                ("device_bytes", C.c_size_t), ("fused_mlp_cluster", C.c_int32 * 2)]
 
 
 # Exported symbols and their signatures (mirrors include/qtts_b200.h).

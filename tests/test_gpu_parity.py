@@ -346,6 +346,10 @@ def test_full_size_0p6b(pkg, tmp_path_factory):
     assert np.abs(lg - rl).max() <= LOGIT_TOL
     codes, _, recs = m.rollout(pre, tr, pad, 4, GREEDY, GREEDY, forced_codes=out.codes)
     assert_tokens_match(out.codes, codes, gaps_per_code(recs))
+    # Cross-CTA reductions sum in a fixed order: a sampled run repeats bit for bit.
+    s = pkg.GenerateOptions(decode_audio=False, max_frames=8, seed=7)
+    a, b = e.generate_codes_from_ids(ids, s), e.generate_codes_from_ids(ids, s)
+    assert a.frames == b.frames and list(a.codes) == list(b.codes)
     e.close()
 
 
@@ -376,11 +380,13 @@ def test_full_size_1p7b(pkg, tmp_path_factory):
 
 
 @pytest.mark.parametrize("env_var,value", [("QTTS_FRAME_KERNEL", "1"), ("QTTS_FUSE_ATTN_O", "0"),
-                                           ("QTTS_TC_CP", "1"), ("QTTS_TC", "0")])
+                                           ("QTTS_FUSE_MLP", "1"), ("QTTS_TC_CP", "1"),
+                                           ("QTTS_TC", "0")])
 def test_alternate_path_parity(model_dirs, tmp_path, env_var, value):
     """The alternate paths against the oracle: the opt-in persistent frame
     kernel (QTTS_FRAME_KERNEL=1), the unfused CodePredictor attention
-    (QTTS_FUSE_ATTN_O=0), the tcgen05 projection also for the CodePredictor's
+    (QTTS_FUSE_ATTN_O=0), the fused decode MLP (QTTS_FUSE_MLP=1: gate|up,
+    SwiGLU and down in one kernel, a cluster reduction), the tcgen05 projection also for the CodePredictor's
     2-row prefill (QTTS_TC_CP=1) and the CUDA-core projections only
     (QTTS_TC=0). Run in a child process so the engine reads
     the setting at load."""
@@ -411,6 +417,7 @@ for shape, d in [('tiny', {str(model_dirs['tiny'])!r}), ('tiny_proj', {str(model
     assert out.frames == 12 and not bad, (shape, bad)
     s = pkg.GenerateOptions(decode_audio=False, max_frames=12, seed=4)
     out2 = e.generate_codes_from_ids(ids, s)
+    assert list(e.generate_codes_from_ids(ids, s).codes) == list(out2.codes), shape  # repeatable
     sc = O.SamplingConfig(True, 50, 1.0, 0.9)
     codes2, _, _ = m.rollout(pre, tr, pad, 12, sc, sc, penalty=1.05, seed=4, forced_codes=out2.codes)
     agree = np.mean(np.asarray(out2.codes) == np.asarray(codes2[: len(out2.codes)]))
