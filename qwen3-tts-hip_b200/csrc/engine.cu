@@ -655,6 +655,7 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   if (T.vocab > max_sample_vocab() || C.vocab > max_sample_vocab())
     invalid("vocab larger than the sampler supports");
   if (T.vocab <= 1024) invalid("talker vocab must exceed the 1024 suppressed control ids");
+  if (T.hidden > 2048) invalid("talker hidden sizes above 2048 are not supported");
 
   SafeTensors sf(dir + "/model.safetensors");
   const SafeTensors& st_ = sf;

@@ -496,13 +496,17 @@ __global__ void __launch_bounds__(kThreads) k_gemv1(LinearArgs a, int epi) {
 __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* logits, float inv,
                                                 float* smem) {
   __shared__ int s_frame, s_sem;
+  const unsigned long long t_sel = trace_clock(a.lin.trace_id);
 
   const int V = a.lin.N;
   Selector<SyncBlock> sel{smem, reinterpret_cast<int*>(smem + kSelMaxVocab)};
   const int tid = threadIdx.x;
+  // The RNG state is read alongside the logits (the sampler draws early).
+  Rng rng{a.st->rng_kind, a.st->rng_state, a.st->rng_seed, a.st->rng_counter};
   for (int v = tid; v < V; v += kThreads) sel.val[v] = __ldcg(logits + v);
   if (tid == 0) { s_frame = a.st->frames; s_sem = a.st->semantic; }
   __syncthreads();
+  trace_dur(a.lin.trace_id, 6, t_sel);  // logits and sequence state reloaded
   // batched heads check the per-sequence state they index with (a fault here
   // would otherwise take the context down): record and skip
   if (a.frames_cap > 0 &&
@@ -523,8 +527,8 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
     sel.penalise(V, a.history, s_frame, -1, a.penalty, a.suppress, a.eos_token);
   else
     sel.penalise(V, a.history, 0, -1, 1.0f, a.suppress, a.eos_token);
-  Rng rng{a.st->rng_kind, a.st->rng_state, a.st->rng_seed, a.st->rng_counter};
   const int tok = sel.select(V, a.cfg, rng, &a.st->error);
+  trace_dur(a.lin.trace_id, 7, t_sel);  // token chosen
   if (tid == 0) {
     a.st->rng_state = rng.state;
     a.st->rng_counter = rng.counter;
@@ -544,34 +548,87 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
     return;
   }
 
+  // The tail's inputs are loaded in one batch with the token's embedding row
+  // (4 consecutive elements per thread and pass): one L2 round trip.
   const int H = a.H;
+  constexpr int kIt = 2;  // H <= kIt * 4 * kThreads (checked at engine load)
+  const bool cp = a.role == ROLE_CP_GROUP;
+  const bool last = cp && a.group == a.last_group;
+  const float* tr = nullptr;
+  const __nv_bfloat16* se = nullptr;
+  if (last) {
+    tr = s_frame < __ldcg(&a.st->n_trailing) ? a.trailing + (long long)s_frame * H : a.tts_pad;
+    se = a.talker_codec_emb + (long long)s_sem * H;
+  }
+  // pre_a: CodePredictor running embedding sum / talker normed hidden;
+  // pre_b, pre_c: the last group's trailing row and semantic embedding.
+  float4 pre_a[kIt], pre_b[kIt];
+  uint2 pre_c[kIt];
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
+    const int i = (it * kThreads + tid) * 4;
+    pre_a[it] = pre_b[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+    pre_c[it] = make_uint2(0u, 0u);
+    if (i >= H) continue;
+    if (cp) {
+      if (a.group != 0) pre_a[it] = __ldcg(reinterpret_cast<const float4*>(a.emb_sum + i));
+      if (last) {
+        pre_b[it] = __ldcg(reinterpret_cast<const float4*>(tr + i));
+        pre_c[it] = *reinterpret_cast<const uint2*>(se + i);
+      }
+    } else {
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(a.lin.x + i));
+      const float4 g = __ldg(reinterpret_cast<const float4*>(a.lin.gamma + i));
+      pre_a[it] = make_float4(x.x * inv * g.x, x.y * inv * g.y, x.z * inv * g.z, x.w * inv * g.w);
+    }
+  }
+
   if (a.role == ROLE_TALKER_PREFILL || a.role == ROLE_TALKER_STEP) {
-    const float* x = a.lin.x;
-    const float* g = a.lin.gamma;
     const __nv_bfloat16* e = a.talker_codec_emb + (long long)tok * H;
-    for (int i = tid; i < H; i += kThreads) {
-      a.cp_prefix[i] = x[i] * inv * g[i];
-      a.cp_prefix[H + i] = __bfloat162float(e[i]);
+    uint2 ev[kIt];
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+      const int i = (it * kThreads + tid) * 4;
+      if (i < H) ev[it] = *reinterpret_cast<const uint2*>(e + i);
+    }
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+      const int i = (it * kThreads + tid) * 4;
+      if (i >= H) continue;
+      *reinterpret_cast<float4*>(a.cp_prefix + i) = pre_a[it];
+      *reinterpret_cast<float4*>(a.cp_prefix + H + i) =
+          make_float4(bf16lo(ev[it].x), bf16hi(ev[it].x), bf16lo(ev[it].y), bf16hi(ev[it].y));
     }
     if (tid == 0) {
       a.st->semantic = tok;
       if (tok == a.eos_token) a.st->halt = 1;
     }
-  } else if (a.role == ROLE_CP_GROUP) {
+  } else if (cp) {
     const __nv_bfloat16* e = a.cp_emb + (long long)tok * H;
-    const bool last = a.group == a.last_group;
-    const float* tr = nullptr;
-    const __nv_bfloat16* se = nullptr;
-    if (last) {
-      tr = s_frame < a.st->n_trailing ? a.trailing + (long long)s_frame * H : a.tts_pad;
-      se = a.talker_codec_emb + (long long)s_sem * H;
+    uint2 ev[kIt];
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+      const int i = (it * kThreads + tid) * 4;
+      if (i < H) ev[it] = *reinterpret_cast<const uint2*>(e + i);
     }
-    for (int i = tid; i < H; i += kThreads) {
-      const float ev = __bfloat162float(e[i]);
-      a.cp_next[i] = ev;
-      const float sum = a.group == 0 ? ev : a.emb_sum[i] + ev;
-      a.emb_sum[i] = sum;
-      if (last) a.step_in[i] = (__bfloat162float(se[i]) + sum) + tr[i];
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+      const int i = (it * kThreads + tid) * 4;
+      if (i >= H) continue;
+      const float4 ef = make_float4(bf16lo(ev[it].x), bf16hi(ev[it].x), bf16lo(ev[it].y),
+                                    bf16hi(ev[it].y));
+      const float4 sm = a.group == 0 ? ef
+                                     : make_float4(pre_a[it].x + ef.x, pre_a[it].y + ef.y,
+                                                   pre_a[it].z + ef.z, pre_a[it].w + ef.w);
+      *reinterpret_cast<float4*>(a.cp_next + i) = ef;
+      *reinterpret_cast<float4*>(a.emb_sum + i) = sm;
+      if (last) {
+        const uint2 q = pre_c[it];
+        const float4 t = pre_b[it];
+        *reinterpret_cast<float4*>(a.step_in + i) =
+            make_float4((bf16lo(q.x) + sm.x) + t.x, (bf16hi(q.x) + sm.y) + t.y,
+                        (bf16lo(q.y) + sm.z) + t.z, (bf16hi(q.y) + sm.w) + t.w);
+      }
     }
     if (tid == 0) {
       a.codes[(long long)s_frame * a.groups + 1 + a.group] = tok;

@@ -168,6 +168,10 @@ struct Selector {
     }
 
     const bool device_path = cfg.top_k > 0 && cfg.top_k <= 256 && cfg.top_p >= 0.999999f;
+    // The device path always draws once (drawn before the kernel in the
+    // reference), so the draw can run here, off the serial tail.
+    float u_dev = 0.f;
+    if (device_path && tid == 0) u_dev = rng.next();
     stamp(0);
     // Keys of this thread's entries (v = j * 256 + tid) stay in registers;
     // 0 marks an ineligible entry (no finite float maps to 0). The device
@@ -376,9 +380,9 @@ struct Selector {
       // (adding the zero padding leaves the sum unchanged).
       const float4* p4 = reinterpret_cast<const float4*>(prob);
       const int K4 = (K + 3) >> 2;
-      const float u = rng.next();  // drawn before the kernel in the reference
+      const float u = u_dev;
       float sum = 0.f;
-#pragma unroll 4
+#pragma unroll 8
       for (int c = 0; c < K4; ++c) {
         const float4 q = p4[c];
         sum += q.x; sum += q.y; sum += q.z; sum += q.w;
@@ -387,8 +391,9 @@ struct Selector {
       if (isfinite(sum) && sum > 0.f) {
         float target = u * sum;
         pick = K - 1;
+        float4 q = p4[0];
         for (int c = 0; c < K4; ++c) {
-          const float4 q = p4[c];
+          const float4 nq = p4[c + 1 < K4 ? c + 1 : c];  // next group's read in flight
           const float pv[4] = {q.x, q.y, q.z, q.w};
           bool found = false;
 #pragma unroll
@@ -400,6 +405,7 @@ struct Selector {
             }
           }
           if (found) break;
+          q = nq;
         }
       }
       s_res = si[pick];
@@ -411,7 +417,7 @@ struct Selector {
       for (int i = 0; i < K; ++i) sum += p_at(i);
       int tok;
       if (device_path) {
-        const float u = rng.next();  // drawn before the kernel in the reference
+        const float u = u_dev;
         if (!isfinite(sum) || sum <= 0.f) {
           tok = si[0];
         } else {
