@@ -753,7 +753,7 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
     ckv.layer_stride = (long long)2 * C.kv_heads * (1 << shift) * kHeadDim;
     ckv.page_stride = ckv.layer_stride * C.layers;
     ckv.pool = arena.alloc<__nv_bfloat16>((size_t)ckv.page_stride);
-    ckv.page_table = arena.alloc<int>(1);
+    ckv.page_table = arena.alloc<int>(1);  // one entry: page 0 (zeroed)
   }
   logits = arena.alloc<float>(std::max(T.vocab, C.vocab));
   dbg_logits = arena.alloc<float>((size_t)na * C.vocab);
@@ -916,6 +916,7 @@ void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* 
     LinearArgs o{S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden,
                  nullptr, 1, c.hidden, S.q_out, halt};
     if (fuse_attn_o && attn_o_fusable(da, o)) {
+      if (&S == &cp) da.page0 = 0;  // the CodePredictor cache is one page (page 0)
       o.trace_id = trace_tag("attn+o+resid", c.hidden, S.q_out);
       o.trigger = trigger_mode;
       plan_prefetch(o, (size_t)c.hidden * S.q_out * sizeof(__nv_bfloat16));

@@ -388,11 +388,20 @@ __device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, flo
   const int d0 = 4 * lane;
   for (int g = warp; g < kvh; g += kWarps) {
     uint2 kc[kCpFusedPositions], vc[kCpFusedPositions];
+    // With a known page the cached rows are read without the table lookup.
+    const __nv_bfloat16* kbase =
+        at.page0 >= 0 ? at.kv.pool + (long long)at.page0 * at.kv.page_stride +
+                            (long long)at.layer * at.kv.layer_stride +
+                            ((long long)g << at.kv.page_shift) * kHeadDim
+                      : nullptr;
+    const long long vofs = ((long long)at.kv.kv_heads << at.kv.page_shift) * kHeadDim;
 #pragma unroll
     for (int p = 0; p < kCpFusedPositions; ++p) {
       if (p < pos) {
-        kc[p] = *reinterpret_cast<const uint2*>(kv_ptr(at.kv, at.layer, 0, g, p) + d0);
-        vc[p] = *reinterpret_cast<const uint2*>(kv_ptr(at.kv, at.layer, 1, g, p) + d0);
+        const __nv_bfloat16* kp = kbase ? kbase + (long long)p * kHeadDim : kv_ptr(at.kv, at.layer, 0, g, p);
+        const __nv_bfloat16* vp = kbase ? kbase + vofs + (long long)p * kHeadDim : kv_ptr(at.kv, at.layer, 1, g, p);
+        kc[p] = *reinterpret_cast<const uint2*>(kp + d0);
+        vc[p] = *reinterpret_cast<const uint2*>(vp + d0);
       }
     }
     float4 q[2];

@@ -138,6 +138,10 @@ struct AttnDecodeArgs {
   // strides of the position and halt words, and page-table entries per sequence.
   int qkv_ld, out_ld, pos_stride, halt_stride, pt_stride;
   int batch;               // sequences (0 or 1: one)
+  // Fused CodePredictor attention only: when >= 0, the physical page that
+  // holds every position of the sequence (no page-table read before the
+  // cache reads); -1 reads the table.
+  int page0;
 };
 
 struct QkPrepArgs {
