@@ -51,6 +51,9 @@ CONFIGS = {
     "1.7b-batch16": dict(shape="1.7b", n_ids=(16, 256), batch=16, frames=240, do_sample=True,
                          top_k=50, top_p=1.0, temperature=0.9, penalty=1.05, sub_sample=True,
                          sub_top_k=50, sub_temperature=0.9, rng="philox"),
+    # codec decoder (speech tokenizer, HipCodecInitial): 240 frames of random codes
+    # decoded to 24 kHz audio per step; the talker shape is irrelevant (tiny)
+    "codec-decode": dict(shape="tiny", codec=True, frames=240),
 }
 FRAME_SECONDS = 0.08
 
@@ -211,6 +214,156 @@ def reduce_over_ranks(maxed, summed, world, device):
     return t.tolist(), f.tolist()
 
 
+def codec_flops_per_frame(T: int) -> float:
+    """Algorithmic FLOPs (2 per multiply-add) of decoding one frame in a
+    T-frame window: every convolution / projection of the decoder at its
+    sample rate, plus the causal attention of the pre-transformer."""
+    from oracle import codec as K
+
+    f = 2.0 * K.PROJECTED * 2 * K.CODEBOOK_DIM                      # RVQ projections
+    f += 2.0 * K.PRE_CONV_OUT * K.PROJECTED * 3                      # pre_conv
+    f += 2 * 2.0 * K.HIDDEN * K.PRE_CONV_OUT                         # input/output proj
+    qo = K.HEADS * K.HEAD_DIM
+    per_layer = 2.0 * (3 * qo * K.HIDDEN + K.HIDDEN * qo + 2 * K.INTER * K.HIDDEN
+                       + K.HIDDEN * K.INTER)
+    per_layer += 2 * 2.0 * K.HEADS * K.HEAD_DIM * (T + 1) / 2       # scores + values
+    f += K.LAYERS * per_layer
+    L = 1
+    for _ in range(2):                                               # upsample + ConvNeXt
+        L *= 2
+        f += L * 2.0 * (K.UP_CH * K.UP_CH + K.UP_CH * 7 + 2 * K.CONVNEXT_INTER * K.UP_CH)
+    f += L * 2.0 * K.DECODER_INIT * K.PRE_CONV_OUT * 7               # decoder.0
+    for cin, cout, st in K.BLOCKS:
+        L *= st
+        f += L * 2.0 * cout * cin * 2                                # transposed conv (2 taps)
+        f += 3 * L * 2.0 * (cout * cout * 7 + cout * cout)           # residual units
+    f += L * 2.0 * 96 * 7                                            # final conv
+    return f
+
+
+def codec_main(args, c):
+    """bench.py --config codec-decode: the codec decoder (codes -> waveform)."""
+    from oracle import codec as K
+    from oracle import synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    T = c["frames"]
+    metric = "codec_decode_frames_per_s"
+    workload = {"workload": f"codec-decode: {T} frames of random codes (16 codebooks) -> "
+                            f"{T * K.SAMPLES_PER_FRAME} samples at 24 kHz per step, "
+                            "seeded synthetic fp32 speech-tokenizer weights",
+                "frames_per_step": T, "parallelism": f"replicas{max(world, args.gpus)}",
+                "l2": "no flush: weights 456 MB and per-step activations > 1 GB (> 126 MB L2)"}
+    mdir = model_dir("tiny_codec")
+    codes = np.random.default_rng(rank).integers(0, K.CODEBOOK_SIZE, (T, K.GROUPS)).astype(np.int32)
+    flops = codec_flops_per_frame(T) * T
+
+    def cpu_run(n_frames, steps, warmup):
+        import torch
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        o = K.CodecOracle(K.generate(0))
+        sample = codes[:n_frames].reshape(-1)
+        times = []
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            o.decode(sample)
+            if i >= warmup:
+                times.append(time.perf_counter() - t0)
+        return n_frames * steps / sum(times), torch.get_num_threads()
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        n = max(1, min(args.cpu_frames, T))
+        fps, cores = cpu_run(n, args.steps, args.warmup)
+        sample = f"{n} frames per step (of {T}), {args.steps} timed steps"
+        print(json.dumps({
+            "metric": metric, "value": fps, "unit": "frames/s", "impl": "reference", "n_gpus": 0,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * n / fps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload,
+            "cpu_baseline": {"value": fps, "unit": "frames/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": fps, "unit": "frames/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "reference's Rust/ROCm codec cannot run here (no cargo, no AMD GPU); timed "
+                    "arm is the repo's PyTorch-CPU fp32 restatement (oracle/codec.py)"}))
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    pkg = __graft_entry__.load_package()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    if rank == 0:
+        synth.write_model(mdir, "tiny", 0)
+        K.write_codec(mdir, 0)
+    if world > 1:
+        dist.barrier()
+    eng = pkg.HipTtsEngine.load_with_options(mdir, pkg.EngineOptions(local, 512))
+    flat = codes.reshape(-1)
+    for _ in range(args.warmup):
+        eng.decode_codes(flat)
+    dev_ms, wall, launches = 0.0, 0.0, 0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            wav = eng.decode_codes(flat)
+            wall += time.perf_counter() - t0
+            ms, n = eng.last_decode_timing()
+            dev_ms += ms
+            launches += n
+    torch.cuda.synchronize()
+    (dev_ms_max, wall_max), (frames_all, launches_all) = reduce_over_ranks(
+        [dev_ms, wall], [float(T * args.steps), float(launches)], world, torch.device("cuda", local))
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    clocks = clk.summary()
+    sm_max = clocks.get("sm_max_mhz") or 1965.0
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    peak = sms * 128 * 2 * sm_max * 1e6 / 1e12  # fp32 FMA lanes per SM x 2 FLOP x clock
+    achieved = flops * args.steps / (dev_ms / 1000.0) / 1e12
+    line = {
+        "metric": metric, "value": frames_all / (dev_ms_max / 1000.0), "unit": "frames/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random codes and fp32 codec weights)",
+        "audio_seconds_per_s": frames_all * FRAME_SECONDS / (dev_ms_max / 1000.0),
+        "config": workload,
+        "e2e": {"value": frames_all / wall_max, "unit": "frames/s",
+                "h2d_bytes_per_step": int(flat.nbytes), "d2h_bytes_per_step": int(wav.nbytes)},
+        "gpu_launches": int(launches_all),
+        "roofline": {"bound": "fp32", "kernel": "whole decode (k_codec_conv carries >99 % of "
+                                                 "the FLOPs)",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak,
+                     "peak_kind": "nominal fp32 CUDA-core: SMs x 128 lanes x 2 x max SM clock",
+                     "flops_per_step": flops, "traffic": None},
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        n = max(1, min(args.cpu_frames, T))
+        fps, cores = cpu_run(n, 2, 1)
+        line["cpu_baseline"] = {"value": fps, "unit": "frames/s", "cores": cores, "kind": "port",
+                                "sample": f"{n} frames per step, 2 timed steps"}
+    print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -225,6 +378,8 @@ def main():
     c = dict(CONFIGS[args.config])
     if args.frames:
         c["frames"] = args.frames
+    if c.get("codec"):
+        return codec_main(args, c)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

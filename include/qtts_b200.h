@@ -37,7 +37,7 @@ typedef enum {
   QTTS_ERR_CUDA = 2,          /* replaces Error::Hip / Rocblas / Hiprtc             */
   QTTS_ERR_CACHE_FULL = 3,    /* P + max_frames > max_cache_steps (generation.rs:608-617) */
   QTTS_ERR_IO = 4,            /* model directory / safetensors problems              */
-  QTTS_ERR_UNSUPPORTED = 5,   /* codec, tokenizer: outside this library              */
+  QTTS_ERR_UNSUPPORTED = 5,   /* tokenizer (outside this library); codec without its checkpoint */
   QTTS_ERR_DEVICE_STATE = 6,  /* device reported an invalid sampling state           */
 } qtts_status;
 
@@ -51,7 +51,8 @@ typedef struct {
   const char* speaker;
   const char* language;
   uint32_t max_frames;
-  int32_t decode_audio; /* must be 0: the codec is not part of this library */
+  int32_t decode_audio; /* codes-only entry points ignore it (as generate_codes does);
+                         * audio comes from qtts_decode_codes */
   int32_t do_sample;
   uint32_t top_k;
   float top_p;
@@ -110,6 +111,8 @@ typedef struct {
   /* Decode MLP of the talker [0] and the CodePredictor [1]: CTAs per cluster of
    * the fused gate|up + down kernel, 0 when it runs as two GEMVs. */
   int32_t fused_mlp_cluster[2];
+  int32_t has_codec;          /* speech_tokenizer/model.safetensors was loaded */
+  uint32_t samples_per_frame; /* waveform samples per code frame (24 kHz): 1920 */
 } qtts_engine_info;
 
 const char* qtts_last_error(void);
@@ -131,6 +134,19 @@ int32_t qtts_engine_load_with_options(const char* model_dir, int32_t device,
                                       size_t max_cache_steps, qtts_engine** out);
 void qtts_engine_destroy(qtts_engine* engine);
 int32_t qtts_engine_get_info(const qtts_engine* engine, qtts_engine_info* out);
+
+/* HipTtsEngine::decode_codes (generation.rs:619-646): codes [frames x 16]
+ * (frame-major, n_codes = frames * 16) -> mono waveform at 24 kHz, 1920
+ * samples per frame, clamped to [-1, 1], computed by the codec decoder
+ * (HipCodecInitial, src/audio/codec_hip.rs:203-1087). samples holds
+ * >= frames * 1920 floats; n_codes == 0 gives 0 samples. QTTS_ERR_UNSUPPORTED
+ * when the model directory has no speech_tokenizer/model.safetensors. */
+int32_t qtts_decode_codes(qtts_engine* engine, const int32_t* codes, size_t n_codes,
+                          float* samples, size_t samples_capacity, size_t* n_samples);
+/* Profiling seam (no reference counterpart): device time of the last
+ * qtts_decode_codes between the codes landing and the waveform being ready,
+ * and how many kernels it launched. */
+int32_t qtts_last_decode_timing(const qtts_engine* engine, float* ms, size_t* launches);
 
 /* HipTtsEngine::generate_codes (generation.rs:356-371) from content token ids
  * (the ids between the chat-template prefix and suffix, text.rs:357-362);

@@ -1,0 +1,286 @@
+// Codec decoder kernels for sm_100a (see codec.h). fp32 throughout: the
+// reference decoder (src/audio/codec_hip.rs, kernels src/gpu/kernels.rs:453-974)
+// is fp32, and the waveform is compared against an fp32 restatement.
+#include <math.h>
+
+#include "codec.h"
+
+namespace qtts {
+namespace {
+
+constexpr int kTileCo = 64, kTileT = 64, kTileK = 16, kConvThreads = 256;
+
+template <int ACT>
+__device__ __forceinline__ float codec_act(const CodecConvArgs& a, int ci, int src) {
+  const float x = __ldg(a.x + (long long)ci * a.lin + src);
+  if (ACT == CACT_SNAKE) {
+    const float s = sinf(x * __ldg(a.act_a + ci));
+    return x + (s * s) / (__ldg(a.act_b + ci) + 1.0e-9f);
+  }
+  if (ACT == CACT_SWIGLU) {
+    const float u = __ldg(a.x + (long long)(ci + a.up_off) * a.lin + src);
+    return x / (1.0f + expf(-x)) * u;
+  }
+  return x;
+}
+
+// 64 output channels x 64 input positions per CTA, K (= ci * taps) in chunks
+// of 16 through shared memory; each thread owns a 4 x 4 sub-tile (rows
+// ty + 16 i, columns tx + 16 j, so shared-memory reads are conflict-free).
+// The input tile is gathered on the fly (implicit im2col) with the input
+// transform applied once per loaded element.
+template <int ACT>
+__global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
+  __shared__ float As[kTileK][kTileCo + 4];
+  __shared__ float Bs[kTileK][kTileT + 4];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int t0 = blockIdx.x * kTileT, co0 = blockIdx.y * kTileCo, ph = blockIdx.z;
+  const float* W = a.w + (long long)ph * a.w_phase_stride;
+  const int K = a.ci * a.taps;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+  for (int k0 = 0; k0 < K; k0 += kTileK) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int idx = tid + r * kConvThreads;
+      const int row = idx >> 4, col = idx & 15;  // A: 64 rows (co) x 16 (kk)
+      const int co = co0 + row, kk = k0 + col;
+      As[col][row] = (co < a.co && kk < K) ? __ldg(W + (long long)co * K + kk) : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int idx = tid + r * kConvThreads;
+      const int row = idx >> 6, col = idx & 63;  // B: 16 (kk) x 64 (t)
+      const int kk = k0 + row, t = t0 + col;
+      float v = 0.f;
+      if (kk < K && t < a.lin) {
+        const int ci = kk / a.taps, tap = kk - ci * a.taps;
+        const int src = t + tap * a.dil - a.pad;
+        if (src >= 0 && src < a.lin) v = codec_act<ACT>(a, ci, src);
+      }
+      Bs[row][col] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kTileK; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+
+  const long long lout = (long long)a.lin * a.ostride;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int co = co0 + ty + 16 * i;
+    if (co >= a.co) continue;
+    const float b = a.bias ? __ldg(a.bias + co) : 0.f;
+    const float rs = a.rscale ? __ldg(a.rscale + co) : 1.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = t0 + tx + 16 * j;
+      if (t >= a.lin) continue;
+      float v = acc[i][j] + b;
+      if (a.epi & CEPI_GELU) v = 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
+      const long long o = (long long)co * lout + (long long)t * a.ostride + ph;
+      if (a.epi & CEPI_RESID) v = a.resid[o] + v * rs;
+      if (a.epi & CEPI_CLAMP) v = fminf(fmaxf(v, -1.0f), 1.0f);
+      a.y[o] = v;
+    }
+  }
+}
+
+__global__ void k_codec_rvq_gather(const int32_t* codes, int frames, int groups, int cb_size,
+                                   int cb_dim, const float* cb_first, const float* cb_rest,
+                                   float* first, float* rest) {
+  const int t = blockIdx.x;
+  if (t >= frames) return;
+  auto code_of = [&](int g) {
+    int c = codes[t * groups + g] % cb_size;
+    return c < 0 ? c + cb_size : c;
+  };
+  const int c0 = code_of(0);
+  for (int d = threadIdx.x; d < cb_dim; d += blockDim.x) {
+    first[(long long)t * cb_dim + d] = cb_first[(long long)c0 * cb_dim + d];
+    float r = 0.f;
+    for (int g = 1; g < groups; ++g)
+      r += cb_rest[((long long)(g - 1) * cb_size + code_of(g)) * cb_dim + d];
+    rest[(long long)t * cb_dim + d] = r;
+  }
+}
+
+__global__ void k_codec_rvq_project(const float* first, const float* rest, const float* wf,
+                                    const float* wr, int frames, int cb_dim, int out_dim,
+                                    float* y) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= frames * out_dim) return;
+  const int t = idx % frames, c = idx / frames;
+  float s = 0.f;
+  for (int d = 0; d < cb_dim; ++d) {
+    s += wf[(long long)c * cb_dim + d] * first[(long long)t * cb_dim + d];
+    s += wr[(long long)c * cb_dim + d] * rest[(long long)t * cb_dim + d];
+  }
+  y[(long long)c * frames + t] = s;
+}
+
+__global__ void k_codec_chan_norm(const float* x, int C, int T, const float* gamma,
+                                  const float* beta, float eps, float* y) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  float s = 0.f, ss = 0.f;
+  for (int c = 0; c < C; ++c) {
+    const float v = x[(long long)c * T + t];
+    s += v;
+    ss += v * v;
+  }
+  if (beta) {  // LayerNorm (codec_layernorm_f32, kernels.rs:613-660)
+    const float mean = s / (float)C;
+    const float var = fmaxf(ss / (float)C - mean * mean, 0.0f);
+    const float inv = rsqrtf(var + eps);
+    for (int c = 0; c < C; ++c)
+      y[(long long)c * T + t] = (x[(long long)c * T + t] - mean) * inv * gamma[c] + beta[c];
+  } else {  // RMSNorm (rmsnorm_f32, kernels.rs:2-37)
+    const float inv = rsqrtf(ss / (float)C + eps);
+    for (int c = 0; c < C; ++c) y[(long long)c * T + t] = x[(long long)c * T + t] * inv * gamma[c];
+  }
+}
+
+__global__ void k_codec_dwconv(const float* x, int C, int T, const float* w, const float* b,
+                               int K, float* y) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= C * T) return;
+  const int t = idx % T, c = idx / T;
+  float s = b[c];
+  for (int k = 0; k < K; ++k) {
+    const int src = t + k - (K - 1);
+    if (src >= 0) s += x[(long long)c * T + src] * w[c * K + k];
+  }
+  y[idx] = s;
+}
+
+// rope_bhsd_f32 (kernels.rs:40-77): angle = t / theta^(2i/hd), rotate-half.
+__global__ void k_codec_qkv_rope(const float* qkv, int heads, int hd, int T, float theta,
+                                 float* q, float* k, float* v) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int per = heads * T * hd;
+  if (idx >= per) return;
+  const int d = idx % hd, t = (idx / hd) % T, h = idx / (hd * T);
+  const int half = hd / 2, pair = d % half;
+  const float expo = (float)(pair * 2) / (float)hd;
+  const float ang = (float)t / powf(theta, expo);
+  const float c = cosf(ang), s = sinf(ang);
+  const int qo = heads * hd;
+  auto rot = [&](int base) {
+    const float first = qkv[(long long)(base + h * hd + pair) * T + t];
+    const float second = qkv[(long long)(base + h * hd + pair + half) * T + t];
+    return d < half ? first * c - second * s : second * c + first * s;
+  };
+  q[idx] = rot(0);
+  k[idx] = rot(qo);
+  v[idx] = qkv[(long long)(2 * qo + h * hd + d) * T + t];
+}
+
+// One warp per (head, query position): online softmax over keys 0..t; lane l
+// holds dims l and l + 32 (head_dim 64).
+__global__ void k_codec_attention(const float* q, const float* k, const float* v, int heads,
+                                  int T, float scale, float* out) {
+  constexpr int HD = 64;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= heads * T) return;
+  const int h = warp / T, t = warp % T;
+  const float* qr = q + ((long long)h * T + t) * HD;
+  const float q0 = qr[lane], q1 = qr[lane + 32];
+  float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
+  for (int j = 0; j <= t; ++j) {
+    const float* kr = k + ((long long)h * T + j) * HD;
+    float s = q0 * kr[lane] + q1 * kr[lane + 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    s *= scale;
+    const float mn = fmaxf(m, s);
+    const float corr = expf(m - mn), e = expf(s - mn);
+    const float* vr = v + ((long long)h * T + j) * HD;
+    l = l * corr + e;
+    a0 = a0 * corr + e * vr[lane];
+    a1 = a1 * corr + e * vr[lane + 32];
+    m = mn;
+  }
+  const float il = 1.0f / l;
+  out[(long long)(h * HD + lane) * T + t] = a0 * il;
+  out[(long long)(h * HD + lane + 32) * T + t] = a1 * il;
+}
+
+__global__ void k_codec_exp(const float* x, int n, float* y) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = expf(x[i]);
+}
+
+inline unsigned blocks(long long n, int per) { return (unsigned)((n + per - 1) / per); }
+
+}  // namespace
+
+cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream) {
+  if (a.ci <= 0 || a.co <= 0 || a.lin <= 0 || a.taps <= 0 || a.nphase <= 0 || a.ostride <= 0)
+    return cudaErrorInvalidValue;
+  const dim3 grid(blocks(a.lin, kTileT), blocks(a.co, kTileCo), a.nphase);
+  if (a.act == CACT_SNAKE) k_codec_conv<CACT_SNAKE><<<grid, kConvThreads, 0, stream>>>(a);
+  else if (a.act == CACT_SWIGLU) k_codec_conv<CACT_SWIGLU><<<grid, kConvThreads, 0, stream>>>(a);
+  else k_codec_conv<CACT_NONE><<<grid, kConvThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t codec_rvq(const int32_t* codes, int frames, int groups, int cb_size, int cb_dim,
+                      const float* cb_first, const float* cb_rest, const float* wf,
+                      const float* wr, int out_dim, float* first, float* rest, float* y,
+                      cudaStream_t stream) {
+  k_codec_rvq_gather<<<frames, 256, 0, stream>>>(codes, frames, groups, cb_size, cb_dim,
+                                                 cb_first, cb_rest, first, rest);
+  k_codec_rvq_project<<<blocks((long long)frames * out_dim, 256), 256, 0, stream>>>(
+      first, rest, wf, wr, frames, cb_dim, out_dim, y);
+  return cudaGetLastError();
+}
+
+cudaError_t codec_chan_norm(const float* x, int C, int T, const float* gamma, const float* beta,
+                            float eps, float* y, cudaStream_t stream) {
+  k_codec_chan_norm<<<blocks(T, 128), 128, 0, stream>>>(x, C, T, gamma, beta, eps, y);
+  return cudaGetLastError();
+}
+
+cudaError_t codec_dwconv(const float* x, int C, int T, const float* w, const float* b, int K,
+                         float* y, cudaStream_t stream) {
+  k_codec_dwconv<<<blocks((long long)C * T, 256), 256, 0, stream>>>(x, C, T, w, b, K, y);
+  return cudaGetLastError();
+}
+
+cudaError_t codec_qkv_rope(const float* qkv, int heads, int hd, int T, float theta, float* q,
+                           float* k, float* v, cudaStream_t stream) {
+  k_codec_qkv_rope<<<blocks((long long)heads * T * hd, 256), 256, 0, stream>>>(qkv, heads, hd, T,
+                                                                               theta, q, k, v);
+  return cudaGetLastError();
+}
+
+cudaError_t codec_attention(const float* q, const float* k, const float* v, int heads, int hd,
+                            int T, float scale, float* out, cudaStream_t stream) {
+  if (hd != 64) return cudaErrorInvalidValue;
+  k_codec_attention<<<blocks((long long)heads * T * 32, 256), 256, 0, stream>>>(q, k, v, heads, T,
+                                                                               scale, out);
+  return cudaGetLastError();
+}
+
+cudaError_t codec_exp(const float* x, int n, float* y, cudaStream_t stream) {
+  k_codec_exp<<<blocks(n, 256), 256, 0, stream>>>(x, n, y);
+  return cudaGetLastError();
+}
+
+}  // namespace qtts

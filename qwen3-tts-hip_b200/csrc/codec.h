@@ -1,0 +1,80 @@
+// Codec decoder kernels (codes -> 24 kHz waveform), fp32 like the reference's
+// HipCodecInitial (src/audio/codec_hip.rs). Activations are channel-major
+// [channels][time] throughout, so every linear layer of the pre-transformer
+// and the ConvNeXt blocks is a 1x1 convolution and one implicit-GEMM kernel
+// serves all of them, the causal / dilated convolutions and (phase by phase)
+// the transposed convolutions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qtts {
+
+enum CodecAct : int {
+  CACT_NONE = 0,
+  CACT_SNAKE = 1,   // x + sin(x * a[c])^2 / (b[c] + 1e-9), a = e^alpha, b = e^beta
+  CACT_SWIGLU = 2,  // silu(x[c]) * x[c + up_off]
+};
+enum CodecEpi : int {
+  CEPI_GELU = 1,   // erf GELU after the bias
+  CEPI_RESID = 2,  // y = resid + rscale[co] * v (rscale null: 1); resid may alias y
+  CEPI_CLAMP = 4,  // clamp to [-1, 1]
+};
+
+// y[co][t_out] = epi(bias[co] + sum_{ci, k} W[co][ci * taps + k] *
+//                    act(x[ci][t + k * dil - pad]))
+// for input positions t in [0, lin); t_out = t * ostride + phase with
+// phase = 0 .. nphase-1 (transposed convolutions: one packed weight set per
+// phase, w + phase * w_phase_stride). Out-of-range inputs read as 0.
+struct CodecConvArgs {
+  const float* x;
+  int ci, lin;
+  const float* w;
+  long long w_phase_stride;
+  const float* bias;
+  int co, taps, dil, pad;
+  int act;
+  const float* act_a;  // CACT_SNAKE: e^alpha per input channel
+  const float* act_b;  //             e^beta per input channel
+  int up_off;          // CACT_SWIGLU: row offset of the up half
+  float* y;
+  int ostride, nphase;
+  int epi;
+  const float* resid;
+  const float* rscale;
+};
+
+cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream);
+
+// first[t][d] = cb_first[code0][d]; rest[t][d] = sum_{g=1..15} cb_rest[g-1][code_g][d]
+// (codes taken modulo the codebook size), then
+// y[c][t] = sum_d wf[c][d] * first[t][d] + wr[c][d] * rest[t][d]
+// (codec_rvq_project_f32, kernels.rs:454-497).
+cudaError_t codec_rvq(const int32_t* codes, int frames, int groups, int cb_size, int cb_dim,
+                      const float* cb_first, const float* cb_rest, const float* wf,
+                      const float* wr, int out_dim, float* first, float* rest, float* y,
+                      cudaStream_t stream);
+
+// Per time step over the channel axis of [C][T]: RMSNorm (beta null) or
+// LayerNorm (mean / variance, beta added).
+cudaError_t codec_chan_norm(const float* x, int C, int T, const float* gamma, const float* beta,
+                            float eps, float* y, cudaStream_t stream);
+
+// y[c][t] = b[c] + sum_k w[c][k] * x[c][t + k - (K - 1)] (depthwise, causal).
+cudaError_t codec_dwconv(const float* x, int C, int T, const float* w, const float* b, int K,
+                         float* y, cudaStream_t stream);
+
+// qkv [3 * heads * hd][T] -> q, k (RoPE applied) and v as [heads][T][hd].
+cudaError_t codec_qkv_rope(const float* qkv, int heads, int hd, int T, float theta, float* q,
+                           float* k, float* v, cudaStream_t stream);
+
+// Causal softmax attention per head; out [heads * hd][T].
+cudaError_t codec_attention(const float* q, const float* k, const float* v, int heads, int hd,
+                            int T, float scale, float* out, cudaStream_t stream);
+
+// y[i] = expf(x[i]) (snake parameters, computed on the device like the
+// reference's per-element expf).
+cudaError_t codec_exp(const float* x, int n, float* y, cudaStream_t stream);
+
+}  // namespace qtts

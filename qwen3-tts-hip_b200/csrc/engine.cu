@@ -28,6 +28,7 @@
 #include <string>
 #include <vector>
 
+#include "codec.h"
 #include "frame_kernel.h"
 #include "gemm_tc.h"
 #include "json.h"
@@ -264,6 +265,333 @@ SampleCfg sub_cfg(const qtts_generate_options& o) {
                    o.subtalker_temperature};
 }
 
+
+std::vector<float> to_f32(const TensorRef& t);
+void expect_shape(const std::string& name, const TensorRef& t, std::vector<long long> shape);
+
+// Codec decoder (HipCodecInitial, src/audio/codec_hip.rs:203-1087): codes
+// [frames x 16] -> 24 kHz waveform. Loaded from speech_tokenizer/model.safetensors
+// when present; weights stay fp32 like the reference's and are packed at load
+// into the layouts the kernels of codec.cu read (channel-major activations,
+// every linear layer a 1x1 convolution, transposed convolutions split into
+// one causal convolution per output phase).
+class Codec {
+ public:
+  static constexpr int kGroups = 16, kCbSize = 2048, kCbDim = 256, kProj = 512, kPre = 1024;
+  static constexpr int kHidden = 512, kLayers = 8, kHeads = 16, kHeadDim = 64, kInter = 1024;
+  static constexpr int kUp = 1024, kCnx = 4096, kDec0 = 1536, kFinal = 96;
+  static constexpr int kBlocks[4][3] = {{1536, 768, 8}, {768, 384, 5}, {384, 192, 4}, {192, 96, 3}};
+  static constexpr int kDil[3] = {1, 3, 9};
+
+  Codec(const std::string& path, cudaStream_t stream) : stream_(stream) {
+    SafeTensors st(path);
+    auto get = [&](const std::string& n, std::vector<long long> shape) {
+      TensorRef t = st.get(n);
+      expect_shape(n, t, shape);
+      return to_f32(t);
+    };
+    auto up = [&](const std::vector<float>& v) {
+      float* d = arena_.alloc<float>(v.size());
+      QCK(cudaMemcpy(d, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+      return d;
+    };
+    auto vec = [&](const std::string& n, long long len) { return up(get(n, {len})); };
+    // snake: e^alpha, e^beta per channel, computed on the device with expf
+    auto snake = [&](const std::string& p, int C, float** a, float** b) {
+      float* ra = vec(p + ".alpha", C);
+      float* rb = vec(p + ".beta", C);
+      *a = arena_.alloc<float>(C);
+      *b = arena_.alloc<float>(C);
+      QCK(codec_exp(ra, C, *a, stream_));
+      QCK(codec_exp(rb, C, *b, stream_));
+    };
+    // normalised codebooks (codec_hip.rs:2135-2154)
+    auto book = [&](const std::string& p) {
+      std::vector<float> e = get(p + "._codebook.embedding_sum", {kCbSize, kCbDim});
+      std::vector<float> u = get(p + "._codebook.cluster_usage", {kCbSize});
+      for (int c = 0; c < kCbSize; ++c) {
+        const float sc = std::max(u[c], 1e-7f);
+        for (int d = 0; d < kCbDim; ++d) e[(size_t)c * kCbDim + d] /= sc;
+      }
+      return e;
+    };
+    const std::string q = "decoder.quantizer";
+    cb_first_ = up(book(q + ".rvq_first.vq.layers.0"));
+    {
+      std::vector<float> rest;
+      for (int g = 0; g < kGroups - 1; ++g) {
+        std::vector<float> b = book(q + ".rvq_rest.vq.layers." + std::to_string(g));
+        rest.insert(rest.end(), b.begin(), b.end());
+      }
+      cb_rest_ = up(rest);
+    }
+    wf_ = up(get(q + ".rvq_first.output_proj.weight", {kProj, kCbDim, 1}));
+    wr_ = up(get(q + ".rvq_rest.output_proj.weight", {kProj, kCbDim, 1}));
+    pre_w_ = up(get("decoder.pre_conv.conv.weight", {kPre, kProj, 3}));
+    pre_b_ = vec("decoder.pre_conv.conv.bias", kPre);
+    const std::string t = "decoder.pre_transformer";
+    in_w_ = up(get(t + ".input_proj.weight", {kHidden, kPre}));
+    in_b_ = vec(t + ".input_proj.bias", kHidden);
+    out_w_ = up(get(t + ".output_proj.weight", {kPre, kHidden}));
+    out_b_ = vec(t + ".output_proj.bias", kPre);
+    norm_ = vec(t + ".norm.weight", kHidden);
+    const int qo = kHeads * kHeadDim;
+    for (int l = 0; l < kLayers; ++l) {
+      const std::string p = t + ".layers." + std::to_string(l);
+      Layer& L = layers_[l];
+      L.in_g = vec(p + ".input_layernorm.weight", kHidden);
+      std::vector<float> qkv;
+      for (const char* nm : {"q_proj", "k_proj", "v_proj"}) {
+        std::vector<float> w = get(p + ".self_attn." + nm + ".weight", {qo, kHidden});
+        qkv.insert(qkv.end(), w.begin(), w.end());
+      }
+      L.wqkv = up(qkv);
+      L.wo = up(get(p + ".self_attn.o_proj.weight", {kHidden, qo}));
+      L.attn_scale = vec(p + ".self_attn_layer_scale.scale", kHidden);
+      L.post_g = vec(p + ".post_attention_layernorm.weight", kHidden);
+      std::vector<float> gu = get(p + ".mlp.gate_proj.weight", {kInter, kHidden});
+      std::vector<float> u = get(p + ".mlp.up_proj.weight", {kInter, kHidden});
+      gu.insert(gu.end(), u.begin(), u.end());
+      L.wgu = up(gu);
+      L.wdown = up(get(p + ".mlp.down_proj.weight", {kHidden, kInter}));
+      L.mlp_scale = vec(p + ".mlp_layer_scale.scale", kHidden);
+    }
+    for (int i = 0; i < 2; ++i) {
+      const std::string p = "decoder.upsample." + std::to_string(i);
+      Up& U = ups_[i];
+      // transposed conv, kernel = stride = 2: phase p uses tap p alone
+      U.tw = up(pack_trans(get(p + ".0.conv.weight", {kUp, kUp, 2}), kUp, kUp, 2, 2));
+      U.tb = vec(p + ".0.conv.bias", kUp);
+      U.dw = up(get(p + ".1.dwconv.conv.weight", {kUp, 1, 7}));
+      U.dwb = vec(p + ".1.dwconv.conv.bias", kUp);
+      U.ln_g = vec(p + ".1.norm.weight", kUp);
+      U.ln_b = vec(p + ".1.norm.bias", kUp);
+      U.pw1 = up(get(p + ".1.pwconv1.weight", {kCnx, kUp}));
+      U.pw1b = vec(p + ".1.pwconv1.bias", kCnx);
+      U.pw2 = up(get(p + ".1.pwconv2.weight", {kUp, kCnx}));
+      U.pw2b = vec(p + ".1.pwconv2.bias", kUp);
+      U.gamma = vec(p + ".1.gamma", kUp);
+    }
+    d0_w_ = up(get("decoder.decoder.0.conv.weight", {kDec0, kPre, 7}));
+    d0_b_ = vec("decoder.decoder.0.conv.bias", kDec0);
+    for (int b = 0; b < 4; ++b) {
+      const int cin = kBlocks[b][0], cout = kBlocks[b][1], s = kBlocks[b][2];
+      const std::string p = "decoder.decoder." + std::to_string(b + 1) + ".block";
+      Block& B = blocks_[b];
+      snake(p + ".0", cin, &B.sa, &B.sb);
+      B.tw = up(pack_trans(get(p + ".1.conv.weight", {cin, cout, 2 * s}), cin, cout, 2 * s, s));
+      B.tb = vec(p + ".1.conv.bias", cout);
+      for (int u = 0; u < 3; ++u) {
+        const std::string r = p + "." + std::to_string(u + 2);
+        Res& R = B.res[u];
+        snake(r + ".act1", cout, &R.a1, &R.b1);
+        R.c1 = up(get(r + ".conv1.conv.weight", {cout, cout, 7}));
+        R.c1b = vec(r + ".conv1.conv.bias", cout);
+        snake(r + ".act2", cout, &R.a2, &R.b2);
+        R.c2 = up(get(r + ".conv2.conv.weight", {cout, cout, 1}));
+        R.c2b = vec(r + ".conv2.conv.bias", cout);
+      }
+    }
+    snake("decoder.decoder.5", kFinal, &fa_, &fb_);
+    f_w_ = up(get("decoder.decoder.6.conv.weight", {1, kFinal, 7}));
+    f_b_ = vec("decoder.decoder.6.conv.bias", 1);
+    QCK(cudaStreamSynchronize(stream_));
+  }
+  ~Codec() { release(); }
+
+  static constexpr int samples_per_frame() { return 2 * 2 * 8 * 5 * 4 * 3; }
+  size_t device_bytes() const { return arena_.bytes() + ws_bytes_; }
+
+  // HipTtsEngine::decode_codes (generation.rs:619-646) for `frames` frames of
+  // device-resident codes; the waveform (frames * 1920 samples) is left in
+  // out() on the stream.
+  void decode(const int32_t* d_codes, int frames) {
+    ensure(frames);
+    const int T = frames;
+    launches = 0;
+    // RVQ + pre_conv
+    QCK(codec_rvq(d_codes, T, kGroups, kCbSize, kCbDim, cb_first_, cb_rest_, wf_, wr_, kProj,
+                  ws_.first, ws_.rest, ws_.a, stream_));
+    launches += 2;
+    conv(ws_.a, kProj, T, pre_w_, 0, pre_b_, kPre, 3, 1, 2, ws_.b);
+    // pre_transformer (codec_hip.rs:379-653)
+    conv(ws_.b, kPre, T, in_w_, 0, in_b_, kHidden, 1, 1, 0, ws_.h);
+    const int qo = kHeads * kHeadDim;
+    for (int l = 0; l < kLayers; ++l) {
+      const Layer& L = layers_[l];
+      QCK(codec_chan_norm(ws_.h, kHidden, T, L.in_g, nullptr, 1e-5f, ws_.n, stream_));
+      conv(ws_.n, kHidden, T, L.wqkv, 0, nullptr, 3 * qo, 1, 1, 0, ws_.qkv);
+      QCK(codec_qkv_rope(ws_.qkv, kHeads, kHeadDim, T, 10000.0f, ws_.q, ws_.k, ws_.v, stream_));
+      QCK(codec_attention(ws_.q, ws_.k, ws_.v, kHeads, kHeadDim, T, 1.0f / std::sqrt(64.0f),
+                          ws_.att, stream_));
+      launches += 3;
+      conv(ws_.att, qo, T, L.wo, 0, nullptr, kHidden, 1, 1, 0, ws_.h, CACT_NONE, nullptr,
+           nullptr, 0, CEPI_RESID, ws_.h, L.attn_scale);
+      QCK(codec_chan_norm(ws_.h, kHidden, T, L.post_g, nullptr, 1e-5f, ws_.n, stream_));
+      ++launches;
+      conv(ws_.n, kHidden, T, L.wgu, 0, nullptr, 2 * kInter, 1, 1, 0, ws_.qkv);
+      conv(ws_.qkv, kInter, T, L.wdown, 0, nullptr, kHidden, 1, 1, 0, ws_.h, CACT_SWIGLU,
+           nullptr, nullptr, kInter, CEPI_RESID, ws_.h, L.mlp_scale);
+    }
+    QCK(codec_chan_norm(ws_.h, kHidden, T, norm_, nullptr, 1e-5f, ws_.n, stream_));
+    ++launches;
+    conv(ws_.n, kHidden, T, out_w_, 0, out_b_, kPre, 1, 1, 0, ws_.a);
+    // upsample stages (codec_hip.rs:656-785)
+    float* x = ws_.a;
+    int L = T;
+    for (int i = 0; i < 2; ++i) {
+      const Up& U = ups_[i];
+      float* y = x == ws_.a ? ws_.b : ws_.a;
+      conv(x, kUp, L, U.tw, (long long)kUp * kUp, U.tb, kUp, 1, 1, 0, y, CACT_NONE, nullptr,
+           nullptr, 0, 0, nullptr, nullptr, 2, 2);
+      L *= 2;
+      QCK(codec_dwconv(y, kUp, L, U.dw, U.dwb, 7, ws_.n, stream_));
+      QCK(codec_chan_norm(ws_.n, kUp, L, U.ln_g, U.ln_b, 1e-6f, ws_.att, stream_));
+      launches += 2;
+      conv(ws_.att, kUp, L, U.pw1, 0, U.pw1b, kCnx, 1, 1, 0, ws_.qkv, CACT_NONE, nullptr, nullptr,
+           0, CEPI_GELU);
+      conv(ws_.qkv, kCnx, L, U.pw2, 0, U.pw2b, kUp, 1, 1, 0, y, CACT_NONE, nullptr, nullptr, 0,
+           CEPI_RESID, y, U.gamma);
+      x = y;
+    }
+    // decoder (codec_hip.rs:787-1041)
+    float* cur = ws_.p0;
+    conv(x, kPre, L, d0_w_, 0, d0_b_, kDec0, 7, 1, 6, cur);
+    for (int b = 0; b < 4; ++b) {
+      const int cin = kBlocks[b][0], cout = kBlocks[b][1], s = kBlocks[b][2];
+      const Block& B = blocks_[b];
+      float* nxt = cur == ws_.p0 ? ws_.p1 : ws_.p0;
+      conv(cur, cin, L, B.tw, (long long)cout * cin * 2, B.tb, cout, 2, 1, 1, nxt, CACT_SNAKE,
+           B.sa, B.sb, 0, 0, nullptr, nullptr, s, s);
+      L *= s;
+      for (int u = 0; u < 3; ++u) {
+        const Res& R = B.res[u];
+        conv(nxt, cout, L, R.c1, 0, R.c1b, cout, 7, kDil[u], 6 * kDil[u], ws_.scr, CACT_SNAKE,
+             R.a1, R.b1);
+        conv(ws_.scr, cout, L, R.c2, 0, R.c2b, cout, 1, 1, 0, nxt, CACT_SNAKE, R.a2, R.b2, 0,
+             CEPI_RESID, nxt, nullptr);
+      }
+      cur = nxt;
+    }
+    conv(cur, kFinal, L, f_w_, 0, f_b_, 1, 7, 1, 6, ws_.wav, CACT_SNAKE, fa_, fb_, 0, CEPI_CLAMP);
+  }
+  const float* out() const { return ws_.wav; }
+  size_t launches = 0;  // kernels enqueued by the last decode
+  int32_t* codes_buffer(int frames) {
+    ensure(frames);
+    return ws_.codes;
+  }
+
+ private:
+  struct Layer {
+    float *in_g, *wqkv, *wo, *attn_scale, *post_g, *wgu, *wdown, *mlp_scale;
+  } layers_[kLayers]{};
+  struct Up {
+    float *tw, *tb, *dw, *dwb, *ln_g, *ln_b, *pw1, *pw1b, *pw2, *pw2b, *gamma;
+  } ups_[2]{};
+  struct Res {
+    float *a1, *b1, *c1, *c1b, *a2, *b2, *c2, *c2b;
+  };
+  struct Block {
+    float *sa, *sb, *tw, *tb;
+    Res res[3];
+  } blocks_[4]{};
+  struct Ws {
+    int32_t* codes;
+    float *first, *rest, *a, *b, *h, *n, *qkv, *q, *k, *v, *att, *p0, *p1, *scr, *wav;
+  } ws_{};
+
+  // Transposed convolution weight [cin][cout][K] (stride s, K = s or 2 s)
+  // as one causal convolution per output phase p: [p][cout][cin * taps],
+  // taps ordered oldest input first (tap 0 reads input i - 1 through
+  // W[.][.][p + s] when K = 2 s, the last tap reads input i through W[.][.][p]).
+  static std::vector<float> pack_trans(const std::vector<float>& w, int cin, int cout, int K,
+                                       int s) {
+    const int taps = K / s;
+    std::vector<float> o((size_t)s * cout * cin * taps);
+    for (int p = 0; p < s; ++p)
+      for (int co = 0; co < cout; ++co)
+        for (int ci = 0; ci < cin; ++ci)
+          for (int j = 0; j < taps; ++j) {
+            const int k = p + (taps - 1 - j) * s;
+            o[(((size_t)p * cout + co) * cin + ci) * taps + j] =
+                w[((size_t)ci * cout + co) * K + k];
+          }
+    return o;
+  }
+
+  void conv(const float* x, int ci, int lin, const float* w, long long w_phase_stride,
+            const float* bias, int co, int taps, int dil, int pad, float* y, int act = CACT_NONE,
+            const float* act_a = nullptr, const float* act_b = nullptr, int up_off = 0,
+            int epi = 0, const float* resid = nullptr, const float* rscale = nullptr,
+            int ostride = 1, int nphase = 1) {
+    CodecConvArgs a{x,   ci,     lin,    w,      w_phase_stride, bias,  co,     taps, dil,
+                    pad, act,    act_a,  act_b,  up_off,         y,     ostride, nphase, epi,
+                    resid, rscale};
+    QCK(codec_conv(a, stream_));
+    ++launches;
+  }
+
+  void ensure(int frames) {
+    if (frames <= cap_) return;
+    release();
+    const size_t T = (size_t)frames;
+    size_t big = 0;  // largest decoder activation per frame, in floats
+    {
+      size_t L = 4;  // decoder input steps per frame (after the two upsample stages)
+      big = std::max(big, (size_t)kDec0 * L);
+      for (int b = 0; b < 4; ++b) {
+        L *= kBlocks[b][2];
+        big = std::max(big, (size_t)kBlocks[b][1] * L);
+      }
+      big = std::max(big, L);
+    }
+    auto al = [&](size_t n) {
+      void* p = nullptr;
+      QCK(cudaMalloc(&p, std::max<size_t>(n, 4) * 4));
+      ws_bytes_ += std::max<size_t>(n, 4) * 4;
+      return static_cast<float*>(p);
+    };
+    const int qo = kHeads * kHeadDim;
+    ws_.codes = reinterpret_cast<int32_t*>(al(T * kGroups));
+    ws_.first = al(T * kCbDim);
+    ws_.rest = al(T * kCbDim);
+    ws_.a = al(T * 4 * kUp);
+    ws_.b = al(T * 4 * kUp);
+    ws_.h = al(T * kHidden);
+    ws_.n = al(T * 4 * kUp);
+    ws_.qkv = al(T * std::max(3 * qo, 4 * kCnx));
+    ws_.q = al(T * qo);
+    ws_.k = al(T * qo);
+    ws_.v = al(T * qo);
+    ws_.att = al(T * 4 * kUp);
+    ws_.p0 = al(T * big);
+    ws_.p1 = al(T * big);
+    ws_.scr = al(T * big);
+    ws_.wav = al(T * samples_per_frame());
+    cap_ = frames;
+  }
+  void release() {
+    for (float* p : {reinterpret_cast<float*>(ws_.codes), ws_.first, ws_.rest, ws_.a, ws_.b, ws_.h,
+                     ws_.n, ws_.qkv, ws_.q, ws_.k, ws_.v, ws_.att, ws_.p0, ws_.p1, ws_.scr,
+                     ws_.wav})
+      if (p) cudaFree(p);
+    ws_ = Ws{};
+    ws_bytes_ = 0;
+    cap_ = 0;
+  }
+
+  cudaStream_t stream_;
+  Arena arena_;
+  float *cb_first_ = nullptr, *cb_rest_ = nullptr, *wf_ = nullptr, *wr_ = nullptr;
+  float *pre_w_ = nullptr, *pre_b_ = nullptr, *in_w_ = nullptr, *in_b_ = nullptr;
+  float *out_w_ = nullptr, *out_b_ = nullptr, *norm_ = nullptr;
+  float *d0_w_ = nullptr, *d0_b_ = nullptr, *fa_ = nullptr, *fb_ = nullptr, *f_w_ = nullptr,
+        *f_b_ = nullptr;
+  int cap_ = 0;
+  size_t ws_bytes_ = 0;
+};
+
 class Engine {
  public:
   Engine(const std::string& dir, int device, size_t max_cache_steps);
@@ -351,6 +679,10 @@ class Engine {
   bool seq_ended = false;
   size_t seq_max_frames = 0;
   qtts_generate_options seq_opts{};
+  // codec decoder (speech_tokenizer/model.safetensors); null when absent
+  std::unique_ptr<Codec> codec;
+  size_t decode_codes(const int32_t* codes, size_t n_codes, float* out, size_t cap);
+  float last_decode_ms = 0.f;  // device time of the last decode (codes resident to waveform)
   uint64_t seq_id = 0;
 
   bool has_proj() const { return cfg.cp.hidden != cfg.talker.hidden; }
@@ -860,7 +1192,36 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
       use_frame_kernel = false;
     }
   }
+  {
+    // HipCodecInitial::load (codec_hip.rs:214-336); optional here so the
+    // token loop also runs on talker-only checkpoints.
+    const std::string cpath = dir + "/speech_tokenizer/model.safetensors";
+    struct stat sb;
+    if (::stat(cpath.c_str(), &sb) == 0) codec = std::make_unique<Codec>(cpath, stream);
+  }
   QCK(cudaDeviceSynchronize());
+}
+
+// HipTtsEngine::decode_codes (generation.rs:619-646).
+size_t Engine::decode_codes(const int32_t* codes, size_t n_codes, float* out, size_t cap) {
+  if (n_codes % Codec::kGroups != 0)
+    invalid("code length " + std::to_string(n_codes) + " is not divisible by " +
+            std::to_string(Codec::kGroups));
+  if (n_codes == 0) return 0;
+  if (!codec) fail(QTTS_ERR_UNSUPPORTED, "no codec: speech_tokenizer/model.safetensors not found");
+  const size_t frames = n_codes / Codec::kGroups;
+  const size_t samples = frames * Codec::samples_per_frame();
+  if (samples > cap) invalid("sample buffer too small: need " + std::to_string(samples));
+  if (frames > (size_t)INT32_MAX / Codec::samples_per_frame()) invalid("too many frames");
+  int32_t* d = codec->codes_buffer((int)frames);
+  QCK(cudaMemcpyAsync(d, codes, n_codes * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
+  QCK(cudaEventRecord(ev0, stream));
+  codec->decode(d, (int)frames);
+  QCK(cudaEventRecord(ev1, stream));
+  QCK(cudaMemcpyAsync(out, codec->out(), samples * sizeof(float), cudaMemcpyDeviceToHost, stream));
+  QCK(cudaStreamSynchronize(stream));
+  QCK(cudaEventElapsedTime(&last_decode_ms, ev0, ev1));
+  return samples;
 }
 
 Engine::~Engine() {
@@ -1354,7 +1715,6 @@ void Engine::validate(const qtts_generate_options& o) const {
   };
   check("talker", o.top_p, o.temperature);
   check("subtalker", o.subtalker_top_p, o.subtalker_temperature);
-  if (o.decode_audio) fail(QTTS_ERR_UNSUPPORTED, "decode_audio: the codec is not part of this library");
   if (o.rng != RNG_LCG && o.rng != RNG_PHILOX) invalid("rng must be 0 (lcg) or 1 (philox)");
 }
 
@@ -2009,9 +2369,33 @@ int32_t qtts_engine_get_info(const qtts_engine* h, qtts_engine_info* out) {
     out->cp_layers = e.cfg.cp.layers;
     out->codec_eos = e.cfg.codec_eos;
     out->max_cache_steps = e.max_cache_steps;
-    out->device_bytes = e.arena.bytes();
+    out->device_bytes = e.arena.bytes() + (e.codec ? e.codec->device_bytes() : 0);
     out->fused_mlp_cluster[0] = e.mlp_cluster[0];
     out->fused_mlp_cluster[1] = e.mlp_cluster[1];
+    out->has_codec = e.codec ? 1 : 0;
+    out->samples_per_frame = qtts::Codec::samples_per_frame();
+  });
+}
+
+int32_t qtts_decode_codes(qtts_engine* h, const int32_t* codes, size_t n_codes, float* samples,
+                          size_t cap, size_t* n_samples) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(n_samples, "n_samples");
+    if (n_codes) {
+      need(codes, "codes");
+      need(samples, "samples");
+    }
+    *n_samples = e.decode_codes(codes, n_codes, samples, cap);
+  });
+}
+
+int32_t qtts_last_decode_timing(const qtts_engine* h, float* ms, size_t* launches) {
+  return guard([&] {
+    need(h, "engine");
+    const Engine& e = *h->e;
+    if (ms) *ms = e.last_decode_ms;
+    if (launches) *launches = e.codec ? e.codec->launches : 0;
   });
 }
 

@@ -5,8 +5,10 @@ Names, fields, defaults and error behaviour follow piedshag/qwen3-tts-hip's
 ``TextStreamOptions``, ``GeneratedCodes``, ``GeneratedCodesChunk``) and
 ``src/error.rs`` (``InvalidInput``).  Text arrives as content token ids
 (the caller tokenises): ``generate_codes_from_ids`` / ``push_ids`` are the
-id-based forms of ``generate_codes`` / ``push_text``.  The 24 kHz codec is not
-part of this library, so ``decode_audio`` must be False.
+id-based forms of ``generate_codes`` / ``push_text``.  The codec decoder
+(``decode_codes``, ``generate_from_ids`` with ``decode_audio``,
+``next_audio_chunk``) runs when the model directory holds
+``speech_tokenizer/model.safetensors``.
 
 All compute runs in ``libqtts_b200.so`` (sm_100a); loading fails loudly when the
 library is missing.
@@ -81,7 +83,8 @@ class _Info(C.Structure):
                 ("cp_vocab", C.c_uint32), ("num_code_groups", C.c_uint32),
                 ("talker_layers", C.c_uint32), ("cp_layers", C.c_uint32),
                 ("codec_eos", C.c_uint32), ("max_cache_steps", C.c_size_t),
-                ("device_bytes", C.c_size_t), ("fused_mlp_cluster", C.c_int32 * 2)]
+                ("device_bytes", C.c_size_t), ("fused_mlp_cluster", C.c_int32 * 2),
+                ("has_codec", C.c_int32), ("samples_per_frame", C.c_uint32)]
 
 
 # Exported symbols and their signatures (mirrors include/qtts_b200.h).
@@ -101,6 +104,8 @@ SIGNATURES = {
     "qtts_engine_load_with_options": (C.c_int32, [C.c_char_p, C.c_int32, C.c_size_t, C.POINTER(_P)]),
     "qtts_engine_destroy": (None, [_P]),
     "qtts_engine_get_info": (C.c_int32, [_P, C.POINTER(_Info)]),
+    "qtts_decode_codes": (C.c_int32, [_P, _I32, C.c_size_t, _F, C.c_size_t, _SZ]),
+    "qtts_last_decode_timing": (C.c_int32, [_P, _F, _SZ]),
     "qtts_generate_codes_from_ids": (C.c_int32, [_P, _U32, C.c_size_t, C.POINTER(_Options), _I32, C.c_size_t, _SZ, _I32]),
     "qtts_generate_codes_batch_from_ids": (C.c_int32, [_P, _U32, _SZ, C.c_size_t, C.POINTER(_Options), _I32, C.c_size_t, _SZ, _I32]),
     "qtts_generate_voice_clone_codes_from_ids": (C.c_int32, [_P, _U32, C.c_size_t, _F, C.POINTER(_Options), _I32, C.c_size_t, _SZ, _I32]),
@@ -224,6 +229,27 @@ class GeneratedCodes:
     """GeneratedCodes (generation.rs:1519-1523): codes frame-major [frames*16]."""
     codes: list
     frames: int
+    ended_by_eos: bool
+
+
+@dataclass
+class GeneratedSpeech:
+    """GeneratedSpeech (generation.rs:1494-1530) without the text field:
+    codes plus the decoded waveform (empty unless decode_audio)."""
+    codes: list
+    frames: int
+    ended_by_eos: bool
+    samples: np.ndarray
+    sample_rate: int = SAMPLE_RATE
+
+
+@dataclass
+class GeneratedAudioChunk:
+    """GeneratedAudioChunk (generation.rs:246-252)."""
+    samples: np.ndarray
+    sample_rate: int
+    frames: int
+    total_frames: int
     ended_by_eos: bool
 
 
@@ -384,11 +410,55 @@ class HipTtsEngine:
         return GeneratedCodes(out[:n].tolist(), frames.value, bool(ended.value))
 
     def generate(self, text, options=None):
-        raise Error(ERR_UNSUPPORTED, "text tokenisation and the codec are outside this library; "
-                                     "use generate_codes_from_ids")
+        raise Error(ERR_UNSUPPORTED, "text tokenisation is outside this library; "
+                                     "use generate_from_ids")
 
-    def decode_codes(self, codes):
-        raise Error(ERR_UNSUPPORTED, "the codec decoder is outside this library")
+    def generate_from_ids(self, content_ids, options: Optional[GenerateOptions] = None
+                          ) -> GeneratedSpeech:
+        """generate (generation.rs:317-334) from content ids: codes, then the
+        waveform when options.decode_audio and any frames were produced."""
+        options = options or GenerateOptions()
+        c = self.generate_codes_from_ids(content_ids, options)
+        samples = (self.decode_codes(c.codes) if options.decode_audio and c.codes
+                   else np.zeros(0, np.float32))
+        return GeneratedSpeech(c.codes, c.frames, c.ended_by_eos, samples)
+
+    @property
+    def has_codec(self) -> bool:
+        return bool(self.info.has_codec)
+
+    @property
+    def samples_per_code_frame(self) -> int:
+        """HipCodecInitial::samples_per_code_frame (codec_hip.rs:203-212)."""
+        return int(self.info.samples_per_frame)
+
+    def decode_codes(self, codes) -> np.ndarray:
+        """decode_codes (generation.rs:619-646): codes [frames*16] -> 24 kHz samples."""
+        a = np.ascontiguousarray(np.asarray(codes, dtype=np.int32).reshape(-1))
+        n = a.size // self.code_groups * self.samples_per_code_frame if a.size % self.code_groups == 0 else 0
+        out = np.zeros(max(1, n), dtype=np.float32)
+        got = C.c_size_t()
+        _check(lib().qtts_decode_codes(self._h, a.ctypes.data_as(_I32), a.size,
+                                       out.ctypes.data_as(_F), n, C.byref(got)))
+        return out[: got.value]
+
+    def last_decode_timing(self):
+        """(device ms, kernel launches) of the last decode_codes call."""
+        ms, n = C.c_float(), C.c_size_t()
+        _check(lib().qtts_last_decode_timing(self._h, C.byref(ms), C.byref(n)))
+        return float(ms.value), int(n.value)
+
+    def _audio_chunk(self, all_codes: list, chunk: "GeneratedCodesChunk", left_context: int
+                     ) -> GeneratedAudioChunk:
+        """next_audio_chunk's window (generation.rs:965-989): decode the chunk
+        with up to left_context earlier frames and drop their samples."""
+        start = chunk.total_frames - chunk.frames
+        ctx = min(left_context, start)
+        g = self.code_groups
+        decoded = self.decode_codes(all_codes[(start - ctx) * g: chunk.total_frames * g])
+        skip = min(ctx * self.samples_per_code_frame, decoded.size)
+        return GeneratedAudioChunk(decoded[skip:].copy(), SAMPLE_RATE, chunk.frames,
+                                   chunk.total_frames, chunk.ended_by_eos)
 
     def prepare_inputs_from_ids(self, content_ids, lookahead: Optional[int] = None,
                                 speaker: str = "ryan", language: str = "english") -> TtsPreparedInputs:
@@ -417,7 +487,7 @@ class HipTtsEngine:
         cso = _StreamOptions(int(so.text_lookahead_tokens), int(so.left_context_frames))
         _check(lib().qtts_stream_start_from_ids(self._h, ids.ctypes.data_as(_U32), ids.size,
                                                 C.byref(options._c()), C.byref(cso), C.byref(h)))
-        return HipTtsStream(self, h, options.max_frames)
+        return HipTtsStream(self, h, options.max_frames, int(so.left_context_frames))
 
     def start_text_stream_polling(self, options: Optional[GenerateOptions] = None,
                                   stream_options: Optional[TextStreamOptions] = None) -> "PollingTextStream":
@@ -428,7 +498,7 @@ class HipTtsEngine:
                                  int(bool(so.flush_on_punctuation)), int(so.left_context_frames))
         h = C.c_void_p()
         _check(lib().qtts_text_stream_start(self._h, C.byref(options._c()), C.byref(cso), C.byref(h)))
-        return PollingTextStream(self, h, options.max_frames)
+        return PollingTextStream(self, h, options.max_frames, int(so.left_context_frames))
 
     # ---- parity seams (talker-prefill-parity / code-predictor-parity)
     def talker_prefill(self, rows: np.ndarray):
@@ -492,11 +562,18 @@ class HipTtsEngine:
 class HipTtsStream:
     """HipTtsStream (generation.rs:145-163, 876-997)."""
 
-    def __init__(self, engine: HipTtsEngine, handle, max_frames: int):
+    def __init__(self, engine: HipTtsEngine, handle, max_frames: int,
+                 left_context_frames: int = DEFAULT_STREAM_LEFT_CONTEXT_FRAMES):
         self._e, self._h = engine, handle
         self._codes: list = []
         self._ended = False
         self._max = max_frames
+        self._ctx = left_context_frames
+
+    def next_audio_chunk(self, max_chunk_frames: int) -> Optional[GeneratedAudioChunk]:
+        """next_audio_chunk (generation.rs:965-989)."""
+        ch = self.next_codes_chunk(max_chunk_frames)
+        return None if ch is None else self._e._audio_chunk(self._codes, ch, self._ctx)
 
     def next_codes_chunk(self, max_chunk_frames: int) -> Optional[GeneratedCodesChunk]:
         out = np.zeros(max(1, int(max_chunk_frames)) * self._e.code_groups, dtype=np.int32)
@@ -528,8 +605,20 @@ class HipTtsStream:
 class PollingTextStream:
     """PollingTextStream (generation.rs:1086-1451) fed with token ids."""
 
-    def __init__(self, engine: HipTtsEngine, handle, max_frames: int):
+    def __init__(self, engine: HipTtsEngine, handle, max_frames: int,
+                 left_context_frames: int = DEFAULT_STREAM_LEFT_CONTEXT_FRAMES):
         self._e, self._h, self._max = engine, handle, max_frames
+        self._ctx = left_context_frames
+        self._codes: list = []
+
+    def next_audio_chunk(self, max_chunk_frames: int):
+        """IncrementalAudio from next_audio_chunk (generation.rs:1121-1181):
+        GeneratedAudioChunk (window decoded with left context), NeedMoreText
+        or Finished."""
+        r = self.next_codes_chunk(max_chunk_frames)
+        if not isinstance(r, GeneratedCodesChunk):
+            return r
+        return self._e._audio_chunk(self._codes, r, self._ctx)
 
     def push_ids(self, ids) -> None:
         a = _ids(ids)
@@ -550,8 +639,9 @@ class PollingTextStream:
             return NeedMoreText()
         if ch.status == FINISHED:
             return Finished(self.finish_codes())
-        return GeneratedCodesChunk(out[: ch.frames * self._e.code_groups].tolist(), ch.frames,
-                                   ch.total_frames, bool(ch.ended_by_eos))
+        codes = out[: ch.frames * self._e.code_groups].tolist()
+        self._codes.extend(codes)
+        return GeneratedCodesChunk(codes, ch.frames, ch.total_frames, bool(ch.ended_by_eos))
 
     def finish_codes(self) -> GeneratedCodes:
         n, ended = C.c_size_t(), C.c_int32()
