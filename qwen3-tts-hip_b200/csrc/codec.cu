@@ -8,7 +8,7 @@
 namespace qtts {
 namespace {
 
-constexpr int kTileCo = 64, kTileT = 64, kTileK = 16, kConvThreads = 256;
+constexpr int kTileCo = 64, kTileT = 128, kTileK = 16, kConvThreads = 256;
 
 template <int ACT>
 __device__ __forceinline__ float codec_act(const CodecConvArgs& a, int ci, int src) {
@@ -24,37 +24,45 @@ __device__ __forceinline__ float codec_act(const CodecConvArgs& a, int ci, int s
   return x;
 }
 
-// 64 output channels x 64 input positions per CTA, K (= ci * taps) in chunks
-// of 16 through shared memory; each thread owns a 4 x 4 sub-tile (rows
-// ty + 16 i, columns tx + 16 j, so shared-memory reads are conflict-free).
-// The input tile is gathered on the fly (implicit im2col) with the input
-// transform applied once per loaded element.
+__device__ __forceinline__ float snake(float x, float a, float b) {
+  const float s = sinf(x * a);
+  return x + (s * s) / (b + 1.0e-9f);
+}
+
+// 64 output channels x 128 input positions per CTA, K (= ci * taps) in
+// chunks of 16 through shared memory, the next chunk's global loads held in
+// registers while the current one is multiplied. Thread (ty, tx) owns
+// channels 4 ty .. 4 ty + 3 and positions 4 tx .. 4 tx + 3 and 64 + 4 tx ..
+// 64 + 4 tx + 3, read from shared memory as float4s. The input tile is
+// gathered on the fly (implicit im2col) with the input transform applied
+// once per loaded element.
 template <int ACT>
 __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
-  __shared__ float As[kTileK][kTileCo + 4];
-  __shared__ float Bs[kTileK][kTileT + 4];
+  __shared__ __align__(16) float As[kTileK][kTileCo + 4];  // padded: transposed stores
+  __shared__ __align__(16) float Bs[kTileK][kTileT];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int t0 = blockIdx.x * kTileT, co0 = blockIdx.y * kTileCo, ph = blockIdx.z;
   const float* W = a.w + (long long)ph * a.w_phase_stride;
   const int K = a.ci * a.taps;
-  float acc[4][4];
+  float acc[4][8];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
 
-  for (int k0 = 0; k0 < K; k0 += kTileK) {
+  float ra[4], rb[8];
+  auto load = [&](int k0) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < 4; ++r) {  // A: 64 (co) x 16 (kk)
       const int idx = tid + r * kConvThreads;
-      const int row = idx >> 4, col = idx & 15;  // A: 64 rows (co) x 16 (kk)
+      const int row = idx >> 4, col = idx & 15;
       const int co = co0 + row, kk = k0 + col;
-      As[col][row] = (co < a.co && kk < K) ? __ldg(W + (long long)co * K + kk) : 0.f;
+      ra[r] = (co < a.co && kk < K) ? __ldg(W + (long long)co * K + kk) : 0.f;
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < 8; ++r) {  // B: 16 (kk) x 128 (t)
       const int idx = tid + r * kConvThreads;
-      const int row = idx >> 6, col = idx & 63;  // B: 16 (kk) x 64 (t)
+      const int row = idx >> 7, col = idx & 127;
       const int kk = k0 + row, t = t0 + col;
       float v = 0.f;
       if (kk < K && t < a.lin) {
@@ -62,20 +70,38 @@ __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
         const int src = t + tap * a.dil - a.pad;
         if (src >= 0 && src < a.lin) v = codec_act<ACT>(a, ci, src);
       }
-      Bs[row][col] = v;
+      rb[r] = v;
     }
+  };
+  auto store = [&]() {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int idx = tid + r * kConvThreads;
+      As[idx & 15][idx >> 4] = ra[r];
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int idx = tid + r * kConvThreads;
+      Bs[idx >> 7][idx & 127] = rb[r];
+    }
+  };
+
+  load(0);
+  for (int k0 = 0; k0 < K; k0 += kTileK) {
+    store();
     __syncthreads();
+    if (k0 + kTileK < K) load(k0 + kTileK);  // in flight during the FMAs below
 #pragma unroll
     for (int kk = 0; kk < kTileK; ++kk) {
-      float av[4], bv[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty + 16 * i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx + 16 * j];
+      const float4 av = *reinterpret_cast<const float4*>(&As[kk][4 * ty]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kk][4 * tx]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kk][64 + 4 * tx]);
+      const float ar[4] = {av.x, av.y, av.z, av.w};
+      const float br[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
     }
     __syncthreads();
   }
@@ -83,20 +109,27 @@ __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
   const long long lout = (long long)a.lin * a.ostride;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int co = co0 + ty + 16 * i;
+    const int co = co0 + 4 * ty + i;
     if (co >= a.co) continue;
     const float b = a.bias ? __ldg(a.bias + co) : 0.f;
     const float rs = a.rscale ? __ldg(a.rscale + co) : 1.f;
+    const float sa = a.out_a ? __ldg(a.out_a + co) : 0.f;
+    const float sb = a.out_a ? __ldg(a.out_b + co) : 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int t = t0 + tx + 16 * j;
+    for (int j = 0; j < 8; ++j) {
+      const int t = t0 + (j < 4 ? 4 * tx + j : 64 + 4 * tx + (j - 4));
       if (t >= a.lin) continue;
       float v = acc[i][j] + b;
       if (a.epi & CEPI_GELU) v = 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
       const long long o = (long long)co * lout + (long long)t * a.ostride + ph;
       if (a.epi & CEPI_RESID) v = a.resid[o] + v * rs;
       if (a.epi & CEPI_CLAMP) v = fminf(fmaxf(v, -1.0f), 1.0f);
-      a.y[o] = v;
+      if (a.epi & CEPI_SNAKE) {
+        a.y[o] = snake(v, sa, sb);
+      } else {
+        a.y[o] = v;
+        if (a.y2) a.y2[o] = snake(v, sa, sb);
+      }
     }
   }
 }

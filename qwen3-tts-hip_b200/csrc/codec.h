@@ -20,6 +20,7 @@ enum CodecEpi : int {
   CEPI_GELU = 1,   // erf GELU after the bias
   CEPI_RESID = 2,  // y = resid + rscale[co] * v (rscale null: 1); resid may alias y
   CEPI_CLAMP = 4,  // clamp to [-1, 1]
+  CEPI_SNAKE = 8,  // store snake(v) (out_a / out_b per output channel) instead of v
 };
 
 // y[co][t_out] = epi(bias[co] + sum_{ci, k} W[co][ci * taps + k] *
@@ -43,6 +44,11 @@ struct CodecConvArgs {
   int epi;
   const float* resid;
   const float* rscale;
+  // Output snake (e^alpha, e^beta per output channel): applied to y with
+  // CEPI_SNAKE, or written to y2 (same layout) alongside y when y2 is set.
+  const float* out_a;
+  const float* out_b;
+  float* y2;
 };
 
 cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream);

@@ -454,26 +454,35 @@ class Codec {
            CEPI_RESID, y, U.gamma);
       x = y;
     }
-    // decoder (codec_hip.rs:787-1041)
-    float* cur = ws_.p0;
-    conv(x, kPre, L, d0_w_, 0, d0_b_, kDec0, 7, 1, 6, cur);
+    // decoder (codec_hip.rs:787-1041). Every snake is applied once, in the
+    // epilogue of the convolution that produces its input: decoder.0 stores
+    // snake(y) for block 0; a transposed convolution stores the residual
+    // stream x and snake(x) for its first residual unit; conv1 stores
+    // snake2(y); conv2 updates x in place and stores snake(x) for whatever
+    // reads it next (the next unit, the next block, the final convolution).
+    float* s_in = ws_.sa;
+    float* s_out = ws_.sb;
+    conv(x, kPre, L, d0_w_, 0, d0_b_, kDec0, 7, 1, 6, s_in, CACT_NONE, nullptr, nullptr, 0,
+         CEPI_SNAKE, nullptr, nullptr, 1, 1, blocks_[0].sa, blocks_[0].sb);
     for (int b = 0; b < 4; ++b) {
       const int cin = kBlocks[b][0], cout = kBlocks[b][1], s = kBlocks[b][2];
       const Block& B = blocks_[b];
-      float* nxt = cur == ws_.p0 ? ws_.p1 : ws_.p0;
-      conv(cur, cin, L, B.tw, (long long)cout * cin * 2, B.tb, cout, 2, 1, 1, nxt, CACT_SNAKE,
-           B.sa, B.sb, 0, 0, nullptr, nullptr, s, s);
+      conv(s_in, cin, L, B.tw, (long long)cout * cin * 2, B.tb, cout, 2, 1, 1, ws_.x, CACT_NONE,
+           nullptr, nullptr, 0, 0, nullptr, nullptr, s, s, B.res[0].a1, B.res[0].b1, s_out);
       L *= s;
       for (int u = 0; u < 3; ++u) {
         const Res& R = B.res[u];
-        conv(nxt, cout, L, R.c1, 0, R.c1b, cout, 7, kDil[u], 6 * kDil[u], ws_.scr, CACT_SNAKE,
-             R.a1, R.b1);
-        conv(ws_.scr, cout, L, R.c2, 0, R.c2b, cout, 1, 1, 0, nxt, CACT_SNAKE, R.a2, R.b2, 0,
-             CEPI_RESID, nxt, nullptr);
+        conv(s_out, cout, L, R.c1, 0, R.c1b, cout, 7, kDil[u], 6 * kDil[u], ws_.scr, CACT_NONE,
+             nullptr, nullptr, 0, CEPI_SNAKE, nullptr, nullptr, 1, 1, R.a2, R.b2);
+        const float* na = u < 2 ? B.res[u + 1].a1 : b < 3 ? blocks_[b + 1].sa : fa_;
+        const float* nb = u < 2 ? B.res[u + 1].b1 : b < 3 ? blocks_[b + 1].sb : fb_;
+        conv(ws_.scr, cout, L, R.c2, 0, R.c2b, cout, 1, 1, 0, ws_.x, CACT_NONE, nullptr, nullptr,
+             0, CEPI_RESID, ws_.x, nullptr, 1, 1, na, nb, s_out);
       }
-      cur = nxt;
+      std::swap(s_in, s_out);
     }
-    conv(cur, kFinal, L, f_w_, 0, f_b_, 1, 7, 1, 6, ws_.wav, CACT_SNAKE, fa_, fb_, 0, CEPI_CLAMP);
+    conv(s_in, kFinal, L, f_w_, 0, f_b_, 1, 7, 1, 6, ws_.wav, CACT_NONE, nullptr, nullptr, 0,
+         CEPI_CLAMP);
   }
   const float* out() const { return ws_.wav; }
   size_t launches = 0;  // kernels enqueued by the last decode
@@ -498,7 +507,7 @@ class Codec {
   } blocks_[4]{};
   struct Ws {
     int32_t* codes;
-    float *first, *rest, *a, *b, *h, *n, *qkv, *q, *k, *v, *att, *p0, *p1, *scr, *wav;
+    float *first, *rest, *a, *b, *h, *n, *qkv, *q, *k, *v, *att, *x, *sa, *sb, *scr, *wav;
   } ws_{};
 
   // Transposed convolution weight [cin][cout][K] (stride s, K = s or 2 s)
@@ -524,10 +533,11 @@ class Codec {
             const float* bias, int co, int taps, int dil, int pad, float* y, int act = CACT_NONE,
             const float* act_a = nullptr, const float* act_b = nullptr, int up_off = 0,
             int epi = 0, const float* resid = nullptr, const float* rscale = nullptr,
-            int ostride = 1, int nphase = 1) {
+            int ostride = 1, int nphase = 1, const float* out_a = nullptr,
+            const float* out_b = nullptr, float* y2 = nullptr) {
     CodecConvArgs a{x,   ci,     lin,    w,      w_phase_stride, bias,  co,     taps, dil,
                     pad, act,    act_a,  act_b,  up_off,         y,     ostride, nphase, epi,
-                    resid, rscale};
+                    resid, rscale, out_a, out_b, y2};
     QCK(codec_conv(a, stream_));
     ++launches;
   }
@@ -565,16 +575,17 @@ class Codec {
     ws_.k = al(T * qo);
     ws_.v = al(T * qo);
     ws_.att = al(T * 4 * kUp);
-    ws_.p0 = al(T * big);
-    ws_.p1 = al(T * big);
+    ws_.x = al(T * big);
+    ws_.sa = al(T * big);
+    ws_.sb = al(T * big);
     ws_.scr = al(T * big);
     ws_.wav = al(T * samples_per_frame());
     cap_ = frames;
   }
   void release() {
     for (float* p : {reinterpret_cast<float*>(ws_.codes), ws_.first, ws_.rest, ws_.a, ws_.b, ws_.h,
-                     ws_.n, ws_.qkv, ws_.q, ws_.k, ws_.v, ws_.att, ws_.p0, ws_.p1, ws_.scr,
-                     ws_.wav})
+                     ws_.n, ws_.qkv, ws_.q, ws_.k, ws_.v, ws_.att, ws_.x, ws_.sa, ws_.sb,
+                     ws_.scr, ws_.wav})
       if (p) cudaFree(p);
     ws_ = Ws{};
     ws_bytes_ = 0;
