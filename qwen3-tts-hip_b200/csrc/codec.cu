@@ -36,14 +36,19 @@ __device__ __forceinline__ float snake(float x, float a, float b) {
 // 64 + 4 tx + 3, read from shared memory as float4s. The input tile is
 // gathered on the fly (implicit im2col) with the input transform applied
 // once per loaded element.
-template <int ACT>
+template <int ACT, int TAPS>  // TAPS 0: taps read at run time
 __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
+  const int taps = TAPS ? TAPS : a.taps;
   __shared__ __align__(16) float As[kTileK][kTileCo + 4];  // padded: transposed stores
   __shared__ __align__(16) float Bs[kTileK][kTileT];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int t0 = blockIdx.x * kTileT, co0 = blockIdx.y * kTileCo, ph = blockIdx.z;
+  // Phase varies fastest across blockIdx.x: the nphase CTAs of one tile run
+  // together, so L2 merges their interleaved (stride-nphase) output columns
+  // into whole sectors instead of writing partial ones back to HBM.
+  const int ph = blockIdx.x % a.nphase;
+  const int t0 = (blockIdx.x / a.nphase) * kTileT, co0 = blockIdx.y * kTileCo;
   const float* W = a.w + (long long)ph * a.w_phase_stride;
-  const int K = a.ci * a.taps;
+  const int K = a.ci * taps;
   float acc[4][8];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -66,7 +71,7 @@ __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
       const int kk = k0 + row, t = t0 + col;
       float v = 0.f;
       if (kk < K && t < a.lin) {
-        const int ci = kk / a.taps, tap = kk - ci * a.taps;
+        const int ci = kk / taps, tap = kk - ci * taps;
         const int src = t + tap * a.dil - a.pad;
         if (src >= 0 && src < a.lin) v = codec_act<ACT>(a, ci, src);
       }
@@ -266,10 +271,20 @@ inline unsigned blocks(long long n, int per) { return (unsigned)((n + per - 1) /
 cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream) {
   if (a.ci <= 0 || a.co <= 0 || a.lin <= 0 || a.taps <= 0 || a.nphase <= 0 || a.ostride <= 0)
     return cudaErrorInvalidValue;
-  const dim3 grid(blocks(a.lin, kTileT), blocks(a.co, kTileCo), a.nphase);
-  if (a.act == CACT_SNAKE) k_codec_conv<CACT_SNAKE><<<grid, kConvThreads, 0, stream>>>(a);
-  else if (a.act == CACT_SWIGLU) k_codec_conv<CACT_SWIGLU><<<grid, kConvThreads, 0, stream>>>(a);
-  else k_codec_conv<CACT_NONE><<<grid, kConvThreads, 0, stream>>>(a);
+  const dim3 grid(blocks(a.lin, kTileT) * a.nphase, blocks(a.co, kTileCo), 1);
+  if (a.act == CACT_SNAKE) {
+    k_codec_conv<CACT_SNAKE, 0><<<grid, kConvThreads, 0, stream>>>(a);
+  } else if (a.act == CACT_SWIGLU) {
+    k_codec_conv<CACT_SWIGLU, 0><<<grid, kConvThreads, 0, stream>>>(a);
+  } else {
+    switch (a.taps) {  // constant taps: the im2col index split is a multiply, not a divide
+      case 1: k_codec_conv<CACT_NONE, 1><<<grid, kConvThreads, 0, stream>>>(a); break;
+      case 2: k_codec_conv<CACT_NONE, 2><<<grid, kConvThreads, 0, stream>>>(a); break;
+      case 3: k_codec_conv<CACT_NONE, 3><<<grid, kConvThreads, 0, stream>>>(a); break;
+      case 7: k_codec_conv<CACT_NONE, 7><<<grid, kConvThreads, 0, stream>>>(a); break;
+      default: k_codec_conv<CACT_NONE, 0><<<grid, kConvThreads, 0, stream>>>(a); break;
+    }
+  }
   return cudaGetLastError();
 }
 
