@@ -100,7 +100,6 @@ class SafeTensors {
     if (map_ && map_ != MAP_FAILED) munmap(map_, size_);
     if (fd_ >= 0) ::close(fd_);
   }
-  bool has(const std::string& name) const { return header_.has(name); }
   TensorRef get(const std::string& name) const {
     if (!header_.has(name)) invalid("failed to load " + name + ": tensor not found");
     const Json& m = header_.at(name);
