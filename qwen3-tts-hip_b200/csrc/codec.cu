@@ -29,36 +29,37 @@ __device__ __forceinline__ float snake(float x, float a, float b) {
   return x + (s * s) / (b + 1.0e-9f);
 }
 
-// 64 output channels x 128 input positions per CTA, K (= ci * taps) in
-// chunks of 16 through shared memory, the next chunk's global loads held in
-// registers while the current one is multiplied. Thread (ty, tx) owns
-// channels 4 ty .. 4 ty + 3 and positions 4 tx .. 4 tx + 3 and 64 + 4 tx ..
-// 64 + 4 tx + 3, read from shared memory as float4s. The input tile is
-// gathered on the fly (implicit im2col) with the input transform applied
-// once per loaded element.
-template <int ACT, int TAPS>  // TAPS 0: taps read at run time
+// BM output channels (64 or 128) x 128 input positions per CTA, K (= ci *
+// taps) in chunks of 16 through shared memory, the next chunk's global loads
+// held in registers while the current one is multiplied. Thread (ty, tx)
+// owns channels MR ty .. MR ty + MR - 1 (MR = BM / 16) and positions
+// 4 tx .. 4 tx + 3 and 64 + 4 tx .. 64 + 4 tx + 3, all read from shared
+// memory as float4s. The input tile is gathered on the fly (implicit
+// im2col) with the input transform applied once per loaded element.
+template <int ACT, int TAPS, int BM>  // TAPS 0: taps read at run time
 __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
+  constexpr int MR = BM / 16, AL = BM * kTileK / kConvThreads;
   const int taps = TAPS ? TAPS : a.taps;
-  __shared__ __align__(16) float As[kTileK][kTileCo + 4];  // padded: transposed stores
+  __shared__ __align__(16) float As[kTileK][BM + 4];  // padded: transposed stores
   __shared__ __align__(16) float Bs[kTileK][kTileT];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   // Phase varies fastest across blockIdx.x: the nphase CTAs of one tile run
   // together, so L2 merges their interleaved (stride-nphase) output columns
   // into whole sectors instead of writing partial ones back to HBM.
   const int ph = blockIdx.x % a.nphase;
-  const int t0 = (blockIdx.x / a.nphase) * kTileT, co0 = blockIdx.y * kTileCo;
+  const int t0 = (blockIdx.x / a.nphase) * kTileT, co0 = blockIdx.y * BM;
   const float* W = a.w + (long long)ph * a.w_phase_stride;
   const int K = a.ci * taps;
-  float acc[4][8];
+  float acc[MR][8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < MR; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
 
-  float ra[4], rb[8];
+  float ra[AL], rb[8];
   auto load = [&](int k0) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {  // A: 64 (co) x 16 (kk)
+    for (int r = 0; r < AL; ++r) {  // A: BM (co) x 16 (kk)
       const int idx = tid + r * kConvThreads;
       const int row = idx >> 4, col = idx & 15;
       const int co = co0 + row, kk = k0 + col;
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
   };
   auto store = [&]() {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < AL; ++r) {
       const int idx = tid + r * kConvThreads;
       As[idx & 15][idx >> 4] = ra[r];
     }
@@ -98,13 +99,17 @@ __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
     if (k0 + kTileK < K) load(k0 + kTileK);  // in flight during the FMAs below
 #pragma unroll
     for (int kk = 0; kk < kTileK; ++kk) {
-      const float4 av = *reinterpret_cast<const float4*>(&As[kk][4 * ty]);
+      float ar[MR];
+#pragma unroll
+      for (int q = 0; q < MR / 4; ++q) {
+        const float4 av = *reinterpret_cast<const float4*>(&As[kk][MR * ty + 4 * q]);
+        ar[4 * q] = av.x; ar[4 * q + 1] = av.y; ar[4 * q + 2] = av.z; ar[4 * q + 3] = av.w;
+      }
       const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kk][4 * tx]);
       const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kk][64 + 4 * tx]);
-      const float ar[4] = {av.x, av.y, av.z, av.w};
       const float br[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < MR; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
     }
@@ -113,8 +118,8 @@ __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
 
   const long long lout = (long long)a.lin * a.ostride;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int co = co0 + 4 * ty + i;
+  for (int i = 0; i < MR; ++i) {
+    const int co = co0 + MR * ty + i;
     if (co >= a.co) continue;
     const float b = a.bias ? __ldg(a.bias + co) : 0.f;
     const float rs = a.rscale ? __ldg(a.rscale + co) : 1.f;
@@ -268,24 +273,31 @@ inline unsigned blocks(long long n, int per) { return (unsigned)((n + per - 1) /
 
 }  // namespace
 
-cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream) {
-  if (a.ci <= 0 || a.co <= 0 || a.lin <= 0 || a.taps <= 0 || a.nphase <= 0 || a.ostride <= 0)
-    return cudaErrorInvalidValue;
-  const dim3 grid(blocks(a.lin, kTileT) * a.nphase, blocks(a.co, kTileCo), 1);
+template <int BM>
+static cudaError_t codec_conv_bm(const CodecConvArgs& a, cudaStream_t stream) {
+  const dim3 grid(blocks(a.lin, kTileT) * a.nphase, blocks(a.co, BM), 1);
   if (a.act == CACT_SNAKE) {
-    k_codec_conv<CACT_SNAKE, 0><<<grid, kConvThreads, 0, stream>>>(a);
+    k_codec_conv<CACT_SNAKE, 0, BM><<<grid, kConvThreads, 0, stream>>>(a);
   } else if (a.act == CACT_SWIGLU) {
-    k_codec_conv<CACT_SWIGLU, 0><<<grid, kConvThreads, 0, stream>>>(a);
+    k_codec_conv<CACT_SWIGLU, 0, BM><<<grid, kConvThreads, 0, stream>>>(a);
   } else {
     switch (a.taps) {  // constant taps: the im2col index split is a multiply, not a divide
-      case 1: k_codec_conv<CACT_NONE, 1><<<grid, kConvThreads, 0, stream>>>(a); break;
-      case 2: k_codec_conv<CACT_NONE, 2><<<grid, kConvThreads, 0, stream>>>(a); break;
-      case 3: k_codec_conv<CACT_NONE, 3><<<grid, kConvThreads, 0, stream>>>(a); break;
-      case 7: k_codec_conv<CACT_NONE, 7><<<grid, kConvThreads, 0, stream>>>(a); break;
-      default: k_codec_conv<CACT_NONE, 0><<<grid, kConvThreads, 0, stream>>>(a); break;
+      case 1: k_codec_conv<CACT_NONE, 1, BM><<<grid, kConvThreads, 0, stream>>>(a); break;
+      case 2: k_codec_conv<CACT_NONE, 2, BM><<<grid, kConvThreads, 0, stream>>>(a); break;
+      case 3: k_codec_conv<CACT_NONE, 3, BM><<<grid, kConvThreads, 0, stream>>>(a); break;
+      case 7: k_codec_conv<CACT_NONE, 7, BM><<<grid, kConvThreads, 0, stream>>>(a); break;
+      default: k_codec_conv<CACT_NONE, 0, BM><<<grid, kConvThreads, 0, stream>>>(a); break;
     }
   }
   return cudaGetLastError();
+}
+
+cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream) {
+  if (a.ci <= 0 || a.co <= 0 || a.lin <= 0 || a.taps <= 0 || a.nphase <= 0 || a.ostride <= 0)
+    return cudaErrorInvalidValue;
+  // 64-channel tiles throughout: 128-channel tiles (8 x 8 per thread, ~168
+  // registers, one CTA per SM) measured slower on every layer mix tried.
+  return codec_conv_bm<64>(a, stream);
 }
 
 cudaError_t codec_rvq(const int32_t* codes, int frames, int groups, int cb_size, int cb_dim,
