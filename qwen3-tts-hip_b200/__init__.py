@@ -1,4 +1,5 @@
-"""B200-native Qwen3-TTS token loop (talker decode step + CodePredictor pass).
+"""B200-native Qwen3-TTS token loop (talker decode step + CodePredictor pass) and
+codec decoder (codes to 24 kHz audio).
 
 Import name ``qwen3_tts_hip_b200`` (the directory is ``qwen3-tts-hip_b200/``;
 ``__graft_entry__.load_package()`` registers it). Compute lives in
@@ -6,8 +7,8 @@ Import name ``qwen3_tts_hip_b200`` (the directory is ``qwen3-tts-hip_b200/``;
 host-side mirror of the reference's ``HipTtsEngine`` API over its C ABI.
 """
 from .engine import (  # noqa: F401
-    SAMPLE_RATE, EngineOptions, Error, Finished, GenerateOptions, GeneratedCodes,
-    GeneratedCodesChunk, HipTextStream, HipTtsEngine, HipTtsStream, InvalidInput,
+    SAMPLE_RATE, EngineOptions, Error, Finished, GenerateOptions, GeneratedAudioChunk,
+    GeneratedCodes, GeneratedCodesChunk, GeneratedSpeech, HipTextStream, HipTtsEngine, HipTtsStream, InvalidInput,
     NeedMoreText, PollingTextStream, StreamOptions, TextStreamInput, TextStreamOptions,
     TtsPreparedInputs, lib, library_path, start_text_stream, SIGNATURES,
 )

@@ -4,6 +4,7 @@ import ctypes
 import re
 from pathlib import Path
 
+import numpy as np
 import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
@@ -65,3 +66,33 @@ def test_text_stream_input_semantics(pkg):
     assert sink == [("ids", [1, 2]), ("finish", None)]
     with pytest.raises(pkg.InvalidInput):
         inp.push_ids([3])
+
+
+def test_audio_chunk_window(pkg):
+    """next_audio_chunk's window (generation.rs:965-989) on the host: the chunk's
+    frames plus min(left_context, start) earlier frames are decoded and the
+    context's samples dropped. A stub decoder stands in for the codec."""
+    spf = 4
+
+    class Stub:
+        code_groups = 2
+        samples_per_code_frame = spf
+        calls = []
+
+        def decode_codes(self, codes):
+            self.calls.append(list(codes))
+            frames = len(codes) // self.code_groups
+            # sample k of frame f encodes (first code of the frame, k)
+            return np.array([codes[f * 2] * 10 + k for f in range(frames) for k in range(spf)],
+                            dtype=np.float32)
+
+    stub = Stub()
+    all_codes = [f for f in range(7) for _ in range(2)]  # frame f's codes are (f, f)
+    for start, n, ctx in [(0, 3, 2), (3, 2, 2), (5, 2, 25), (1, 1, 0)]:
+        chunk = pkg.GeneratedCodesChunk(all_codes[start * 2:(start + n) * 2], n, start + n, False)
+        out = pkg.HipTtsEngine._audio_chunk(stub, all_codes, chunk, ctx)
+        used = min(ctx, start)
+        assert stub.calls[-1] == all_codes[(start - used) * 2:(start + n) * 2]
+        want = [f * 10 + k for f in range(start, start + n) for k in range(spf)]
+        assert out.samples.tolist() == want
+        assert (out.frames, out.total_frames, out.sample_rate) == (n, start + n, 24000)
