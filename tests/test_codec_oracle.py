@@ -109,3 +109,26 @@ def test_decode_shapes_and_range(codec_weights):
     assert wav.shape == (3 * K.SAMPLES_PER_FRAME,)
     assert np.all(np.abs(wav) <= 1.0) and wav.std() > 0.05
     assert o.decode([]).size == 0
+
+
+def test_golden_fixture_reproduces(codec_weights):
+    """tests/golden/codec_seed0.json (made by tests/golden/make_codec_golden.py)
+    pins the codec oracle's stage sums and waveform across changes."""
+    import importlib.util
+    import json
+    from pathlib import Path
+
+    gdir = Path(__file__).parent / "golden"
+    spec = importlib.util.spec_from_file_location("make_codec_golden",
+                                                  gdir / "make_codec_golden.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    want = json.loads((gdir / "codec_seed0.json").read_text())
+    got = mod.compute(codec_weights)
+    assert got["codes"] == want["codes"]
+    for stage in ("rvq", "pre_conv", "pre_transformer", "upsample", "waveform"):
+        assert got[stage]["shape"] == want[stage]["shape"]
+        tol = 1e-5 * want[stage]["abs_sum"]
+        assert abs(got[stage]["sum"] - want[stage]["sum"]) <= tol, stage
+        assert abs(got[stage]["abs_sum"] - want[stage]["abs_sum"]) <= tol, stage
+    np.testing.assert_allclose(got["waveform_samples"], want["waveform_samples"], atol=1e-5)
