@@ -39,6 +39,7 @@ __device__ __forceinline__ float snake(float x, float a, float b) {
 template <int ACT, int TAPS, int BM>  // TAPS 0: taps read at run time
 __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
   constexpr int MR = BM / 16, AL = BM * kTileK / kConvThreads;
+  static_assert(AL >= 1 && MR >= 1, "row tile must give every thread an A element");
   const int taps = TAPS ? TAPS : a.taps;
   __shared__ __align__(16) float As[kTileK][BM + 4];  // padded: transposed stores
   __shared__ __align__(16) float Bs[kTileK][kTileT];
@@ -100,10 +101,15 @@ __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
 #pragma unroll
     for (int kk = 0; kk < kTileK; ++kk) {
       float ar[MR];
+      if constexpr (MR % 4 == 0) {
 #pragma unroll
-      for (int q = 0; q < MR / 4; ++q) {
-        const float4 av = *reinterpret_cast<const float4*>(&As[kk][MR * ty + 4 * q]);
-        ar[4 * q] = av.x; ar[4 * q + 1] = av.y; ar[4 * q + 2] = av.z; ar[4 * q + 3] = av.w;
+        for (int q = 0; q < MR / 4; ++q) {
+          const float4 av = *reinterpret_cast<const float4*>(&As[kk][MR * ty + 4 * q]);
+          ar[4 * q] = av.x; ar[4 * q + 1] = av.y; ar[4 * q + 2] = av.z; ar[4 * q + 3] = av.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < MR; ++i) ar[i] = As[kk][MR * ty + i];
       }
       const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kk][4 * tx]);
       const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kk][64 + 4 * tx]);
@@ -295,9 +301,11 @@ static cudaError_t codec_conv_bm(const CodecConvArgs& a, cudaStream_t stream) {
 cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream) {
   if (a.ci <= 0 || a.co <= 0 || a.lin <= 0 || a.taps <= 0 || a.nphase <= 0 || a.ostride <= 0)
     return cudaErrorInvalidValue;
-  // 64-channel tiles throughout: 128-channel tiles (8 x 8 per thread, ~168
-  // registers, one CTA per SM) measured slower on every layer mix tried.
-  return codec_conv_bm<64>(a, stream);
+  // 64-channel tiles, except a 16-channel tile for the final 96 -> 1
+  // convolution (a 64-row tile would spend 63/64 of its FMAs on padding).
+  // 128-channel tiles (8 x 8 per thread, ~168 registers, one CTA per SM)
+  // measured slower.
+  return a.co <= 16 ? codec_conv_bm<16>(a, stream) : codec_conv_bm<64>(a, stream);
 }
 
 cudaError_t codec_rvq(const int32_t* codes, int frames, int groups, int cb_size, int cb_dim,
