@@ -302,10 +302,14 @@ cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream) {
   if (a.ci <= 0 || a.co <= 0 || a.lin <= 0 || a.taps <= 0 || a.nphase <= 0 || a.ostride <= 0)
     return cudaErrorInvalidValue;
   // 64-channel tiles, except a 16-channel tile for the final 96 -> 1
-  // convolution (a 64-row tile would spend 63/64 of its FMAs on padding).
+  // convolution (a 64-row tile would spend 63/64 of its FMAs on padding) and
+  // 32-channel tiles for the 96-channel block (three exact tiles, not two
+  // 64-row tiles of which a quarter is padding).
   // 128-channel tiles (8 x 8 per thread, ~168 registers, one CTA per SM)
   // measured slower.
-  return a.co <= 16 ? codec_conv_bm<16>(a, stream) : codec_conv_bm<64>(a, stream);
+  if (a.co <= 16) return codec_conv_bm<16>(a, stream);
+  if (a.co % 64 != 0 && a.co % 32 == 0) return codec_conv_bm<32>(a, stream);  // 96 channels
+  return codec_conv_bm<64>(a, stream);
 }
 
 cudaError_t codec_rvq(const int32_t* codes, int frames, int groups, int cb_size, int cb_dim,
