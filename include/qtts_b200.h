@@ -242,7 +242,9 @@ int32_t qtts_talker_decode_step(qtts_engine* engine, const float* input, size_t 
  * talkers whose step activations exceed it are rejected with
  * QTTS_ERR_INVALID_INPUT.
  * The first call on a device looks up the array's address (make it before
- * any stream capture). Calls share the array: calls that overlap on the GPU
+ * any stream capture) and keeps it for the life of the process, which
+ * assumes the device's primary context is never reset meanwhile
+ * (cudaDeviceReset). Calls share the array: calls that overlap on the GPU
  * race. No counterpart in the reference. */
 int32_t qtts_talker_decode_step_static(qtts_engine* engine, const float* input, size_t offset,
                                        float* hidden_out, float* logits_out,

@@ -111,7 +111,24 @@ def argmax_device(logits: np.ndarray) -> int:
     return best_i
 
 
-def sample_topk_device(logits: np.ndarray, top_k: int, temperature: float, u: np.float32) -> int:
+def _cdf_margin(probs, j: int, target0) -> float:
+    """Distance of the inverse-CDF target from the edges of the bucket it fell
+    in, as a fraction of the total mass: how far the draw was from picking a
+    neighbour. Summation in fp32 in candidate order, as the walk does."""
+    before = np.float32(0.0)
+    for i in range(j):
+        before = np.float32(before + probs[i])
+    after = np.float32(before + probs[j])
+    total = np.float32(0.0)
+    for p in probs:
+        total = np.float32(total + p)
+    if not total > 0:
+        return float("inf")
+    return float(min(float(target0) - float(before), float(after) - float(target0)) / float(total))
+
+
+def sample_topk_device(logits: np.ndarray, top_k: int, temperature: float, u: np.float32,
+                       with_margin: bool = False):
     """sample_topk_f32 (kernels.rs:265-336): non-finite -> -FLT_MAX, sort descending,
     softmax over the first min(top_k, vocab) entries in fp32, inverse CDF on u*sum.
     Ties are ordered by lowest index (the reference's bitonic order for exact ties
@@ -129,16 +146,19 @@ def sample_topk_device(logits: np.ndarray, top_k: int, temperature: float, u: np
         probs[i] = p
         s = np.float32(s + p)
     if not np.isfinite(s) or s <= 0:
-        return int(order[0])
+        return (int(order[0]), float("inf")) if with_margin else int(order[0])
     target = np.float32(np.float32(u) * s)
+    target0, pick = target, kept - 1
     for i in range(kept):
         if target <= probs[i]:
-            return int(order[i])
+            pick = i
+            break
         target = np.float32(target - probs[i])
-    return int(order[kept - 1])
+    tok = int(order[pick])
+    return (tok, _cdf_margin(probs, pick, target0)) if with_margin else tok
 
 
-def sample_cpu(logits: np.ndarray, cfg: SamplingConfig, rng) -> int:
+def sample_cpu(logits: np.ndarray, cfg: SamplingConfig, rng, with_margin: bool = False):
     """sampling.rs:53-118: finite candidates, stable descending sort, top-k,
     softmax((l-max)/T), optional top-p renormalisation, inverse CDF on u.
     No draw when the probability sum is not finite/positive (sampling.rs:79-81)."""
@@ -158,7 +178,7 @@ def sample_cpu(logits: np.ndarray, cfg: SamplingConfig, rng) -> int:
     for p in probs:
         s = np.float32(s + p)
     if not np.isfinite(s) or s <= 0:
-        return int(idx[0])
+        return (int(idx[0]), float("inf")) if with_margin else int(idx[0])
     probs = (probs / s).astype(np.float32)
     if cfg.top_p < 1.0:
         cum, keep = np.float32(0), 0
@@ -175,22 +195,34 @@ def sample_cpu(logits: np.ndarray, cfg: SamplingConfig, rng) -> int:
         if ks > 0:
             probs = (probs / ks).astype(np.float32)
     target = rng.next_f32()
-    for tok, p in zip(idx, probs):
+    target0, pick = target, len(idx) - 1
+    for i, p in enumerate(probs):
         if target <= p:
-            return int(tok)
+            pick = i
+            break
         target = np.float32(target - p)
-    return int(idx[-1])
+    tok = int(idx[pick])
+    return (tok, _cdf_margin(probs, pick, target0)) if with_margin else tok
 
 
 def select(logits: np.ndarray, cfg: SamplingConfig, rng) -> int:
     """Token selection as the reference engine routes it: greedy -> device argmax;
     device-eligible -> one draw + device top-k; else CPU sampler."""
+    return select_margin(logits, cfg, rng)[0]
+
+
+def select_margin(logits: np.ndarray, cfg: SamplingConfig, rng):
+    """select() plus how robust its choice is against small logit errors:
+    greedy -> the top-2 logit gap (logit units); sampled -> the distance of the
+    inverse-CDF target from its bucket's edges (fraction of probability mass).
+    A GPU run whose logits differ from these by bf16 rounding can pick a
+    different token only where this margin is small."""
     if not cfg.do_sample:
-        return argmax_device(logits)
+        return argmax_device(logits), top2_gap(logits)
     if cfg.supports_device_sampling():
         u = rng.next_f32()
-        return sample_topk_device(logits, cfg.top_k, cfg.temperature, u)
-    return sample_cpu(logits, cfg, rng)
+        return sample_topk_device(logits, cfg.top_k, cfg.temperature, u, with_margin=True)
+    return sample_cpu(logits, cfg, rng, with_margin=True)
 
 
 def top2_gap(logits: np.ndarray) -> float:
@@ -317,6 +349,10 @@ class FrameRecord:
     talker_gap: float
     acoustic: list
     cp_gaps: list
+    # select_margin() of each token: the semantic token, then the 15 acoustic
+    # tokens (equal to the gaps for greedy selection)
+    talker_margin: float = float("inf")
+    cp_margins: list = field(default_factory=list)
 
 
 class OracleModel:
@@ -456,7 +492,7 @@ class OracleModel:
         self.cp.reset()
         prefix = torch.stack([talker_hidden, semantic_embed])
         out = self.cp.forward(self.project(prefix), 0)
-        tokens, gaps, all_logits = [], [], []
+        tokens, gaps, all_logits, margins = [], [], [], []
         h = out[1]
         emb_sum = None
         for g in range(self.groups - 1):
@@ -465,12 +501,14 @@ class OracleModel:
             lg = self.cp_logits(h, g)
             all_logits.append(lg)
             gaps.append(top2_gap(lg))
-            tok = select(lg, cfg, rng)
+            tok, margin = select_margin(lg, cfg, rng)
+            margins.append(margin)
             if forced is not None:
                 tok = int(forced[g])
             tokens.append(tok)
             cur = self.cp_embs[g][tok]
             emb_sum = cur.clone() if emb_sum is None else emb_sum + cur
+        self.last_cp_margins = margins
         return tokens, emb_sum, gaps, all_logits
 
     # ---- rollout (generation.rs:657-749) ----------------------------------
@@ -484,8 +522,9 @@ class OracleModel:
         P = prefill.shape[0]
         _, hidden, logits = self.talker_prefill(prefill)
         logits = self.penalise_and_suppress(logits, None, 1.0)
-        semantic = select(logits, talker_cfg, rng)
+        semantic, margin = select_margin(logits, talker_cfg, rng)
         gaps = [top2_gap(logits)]
+        margins = [margin]
         if forced_codes is not None and len(forced_codes) >= 16:
             semantic = int(forced_codes[0])
         codes, history, records = [], [], []
@@ -502,15 +541,17 @@ class OracleModel:
             codes.append(semantic)
             codes.extend(toks)
             history.append(semantic)
-            records.append(FrameRecord(semantic, gaps[-1], toks, cp_gaps))
+            records.append(FrameRecord(semantic, gaps[-1], toks, cp_gaps, margins[-1],
+                                       list(self.last_cp_margins)))
             if frame + 1 < max_frames:
                 tr = trailing[frame] if frame < trailing.shape[0] else tts_pad
                 step = sem_emb + emb_sum + tr
                 _, hidden, logits = self.talker_step(step, P + frame)
                 use_hist = penalty != 1.0 or talker_cfg.do_sample
                 logits = self.penalise_and_suppress(logits, history if use_hist else None, penalty)
-                semantic = select(logits, talker_cfg, rng)
+                semantic, margin = select_margin(logits, talker_cfg, rng)
                 gaps.append(top2_gap(logits))
+                margins.append(margin)
                 if forced_codes is not None and len(forced_codes) >= 16 * (frame + 2):
                     semantic = int(forced_codes[16 * (frame + 1)])
         return codes, ended, records

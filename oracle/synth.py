@@ -105,6 +105,14 @@ SHAPES = {
                        cp_vocab=2048, num_code_groups=16, text_vocab=4096, text_hidden=2048,
                        text_proj_intermediate=512, im_start=4000, assistant=4001, tts_pad=4002,
                        tts_bos=4003, tts_eos=4004),
+    # One talker layer whose decode-step activations (input row, QKV, attention
+    # output, post-attention row and 66,560-wide MLP row) exceed 264 KiB: the
+    # allocation-free step must refuse it.
+    "tiny_wide": Shape("tiny_wide", hidden=256, intermediate=66560, layers=1, q_heads=4,
+                       kv_heads=2, head_dim=128, vocab=3072, cp_hidden=256, cp_intermediate=512,
+                       cp_layers=1, cp_vocab=2048, num_code_groups=16, text_vocab=4096,
+                       text_hidden=256, text_proj_intermediate=256, im_start=4000,
+                       assistant=4001, tts_pad=4002, tts_bos=4003, tts_eos=4004),
 }
 
 

@@ -629,6 +629,19 @@ class Engine {
   unsigned* tickets = nullptr;
   SeqState* st = nullptr;
   SeqState* st_host = nullptr;  // pinned
+  // Host-to-device uploads go through this pinned staging area as
+  // cudaMemcpyAsync on `stream`, so the kernels that read the data are
+  // ordered after the copy by the stream itself (a synchronous cudaMemcpy from
+  // pageable memory may return before its DMA lands, and the non-blocking
+  // engine stream does not wait for the legacy stream). Sized at load; never
+  // grows, so uploads allocate nothing.
+  char* stage = nullptr;
+  size_t stage_cap = 0, stage_off = 0;
+  void h2d(void* dst, const void* src, size_t bytes);
+  void stream_sync() {
+    QCK(cudaStreamSynchronize(stream));
+    stage_off = 0;
+  }
   int *codes = nullptr, *history = nullptr, *token = nullptr;
   float *trailing = nullptr, *tts_pad = nullptr, *cp_prefix = nullptr, *cp_next = nullptr,
         *emb_sum = nullptr, *xvec = nullptr;
@@ -1102,6 +1115,9 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   tickets = arena.alloc<unsigned>(64);
   st = arena.alloc<SeqState>(1);
   QCK(cudaMallocHost(&st_host, sizeof(SeqState)));
+  // prefill rows + trailing rows + tts_pad row, plus small id / index arrays
+  stage_cap = ((2 * mcs + 4) * (size_t)T.hidden + 4 * ((size_t)mcs + 64)) * sizeof(float);
+  QCK(cudaMallocHost(&stage, stage_cap));
   codes = arena.alloc<int>(mcs * C.groups);
   history = arena.alloc<int>(mcs);
   token = arena.alloc<int>(4);
@@ -1224,7 +1240,7 @@ size_t Engine::decode_codes(const int32_t* codes, size_t n_codes, float* out, si
   if (samples > cap) invalid("sample buffer too small: need " + std::to_string(samples));
   if (frames > (size_t)INT32_MAX / Codec::samples_per_frame()) invalid("too many frames");
   int32_t* d = codec->codes_buffer((int)frames);
-  QCK(cudaMemcpyAsync(d, codes, n_codes * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
+  h2d(d, codes, n_codes * sizeof(int32_t));
   QCK(cudaEventRecord(ev0, stream));
   codec->decode(d, (int)frames);
   QCK(cudaEventRecord(ev1, stream));
@@ -1234,12 +1250,29 @@ size_t Engine::decode_codes(const int32_t* codes, size_t n_codes, float* out, si
   return samples;
 }
 
+// Stream-ordered upload of `bytes` host bytes: through the pinned staging
+// area when they fit (the area is reused once the stream has drained), else
+// straight from the caller's memory (still ordered on the stream).
+void Engine::h2d(void* dst, const void* src, size_t bytes) {
+  if (bytes == 0) return;
+  const size_t aligned = (bytes + 255) & ~(size_t)255;
+  if (aligned > stage_cap) {
+    QCK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream));
+    return;
+  }
+  if (stage_off + aligned > stage_cap) stream_sync();
+  std::memcpy(stage + stage_off, src, bytes);
+  QCK(cudaMemcpyAsync(dst, stage + stage_off, bytes, cudaMemcpyHostToDevice, stream));
+  stage_off += aligned;
+}
+
 Engine::~Engine() {
   cudaSetDevice(device);
   if (stream) cudaStreamSynchronize(stream);
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
   for (auto& kv : batch_graphs) cudaGraphExecDestroy(kv.second);
   if (st_host) cudaFreeHost(st_host);
+  if (stage) cudaFreeHost(stage);
   if (bt.st_host) cudaFreeHost(bt.st_host);
   for (auto& ev : bt.ev)
     if (ev) cudaEventDestroy(ev);
@@ -1651,14 +1684,13 @@ void Engine::project_text(const std::vector<int>& ids, float* out) {
   const int n = (int)ids.size();
   if (n == 0) return;
   if (n > tp_rows) invalid("too many text rows");
-  QCK(cudaMemcpyAsync(tp_ids, ids.data(), n * 4, cudaMemcpyHostToDevice, stream));
+  h2d(tp_ids, ids.data(), (size_t)n * 4);
   QCK(launch_gather_rows(text_emb, tp_ids, n, text_hidden, tp_a, stream));
   TcScope tcs(tc_scope, true);
   linear(fc1, tp_a, text_hidden, nullptr, 0.f, tp_b, text_inter, nullptr, 0, fc1_b, n,
          text_inter, text_hidden, EPI_BIAS_SILU, nullptr);
   linear(fc2, tp_b, text_inter, nullptr, 0.f, out, cfg.talker.hidden, nullptr, 0, fc2_b, n,
          cfg.talker.hidden, text_inter, EPI_BIAS, nullptr);
-  QCK(cudaStreamSynchronize(stream));  // ids buffer is pageable host memory
 }
 
 // prepare_custom_voice_with_lookahead / prepare_voice_clone_xvector_with_lookahead
@@ -1700,9 +1732,9 @@ int Engine::prepare(const uint32_t* ids, size_t n, size_t lookahead, const char*
     pidx[9 + i] = 9 + (int)i;
     cids[9 + i] = codec_list[i + 1 == la ? 6 : 5];
   }
-  if (xvec_host) QCK(cudaMemcpy(xvec, xvec_host, cfg.talker.hidden * 4, cudaMemcpyHostToDevice));
-  QCK(cudaMemcpy(tp_pidx, pidx.data(), P * 4, cudaMemcpyHostToDevice));
-  QCK(cudaMemcpy(tp_cids, cids.data(), P * 4, cudaMemcpyHostToDevice));
+  if (xvec_host) h2d(xvec, xvec_host, (size_t)cfg.talker.hidden * 4);
+  h2d(tp_pidx, pidx.data(), (size_t)P * 4);
+  h2d(tp_cids, cids.data(), (size_t)P * 4);
   const int H = cfg.talker.hidden;
   QCK(launch_assemble_rows(tp_c, tp_pidx, codec_emb, tp_cids, xvec, P, H, tb.x, stream));
   QCK(cudaMemcpyAsync(trailing, tp_c + (size_t)P * H, (size_t)ntr * H * 4,
@@ -1769,7 +1801,7 @@ void Engine::begin(int P, int n_trailing, const qtts_generate_options& o) {
 
 void Engine::sync_state() {
   QCK(cudaMemcpyAsync(st_host, st, sizeof(SeqState), cudaMemcpyDeviceToHost, stream));
-  QCK(cudaStreamSynchronize(stream));
+  stream_sync();
   if (st_host->error)
     fail(QTTS_ERR_DEVICE_STATE, "cannot sample from logits with no finite values");
   if (mlp_err) {
@@ -1881,7 +1913,7 @@ void Engine::ensure_batch() {
     std::vector<int> pt((size_t)bt.pages * cap);
     for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
     int* d = arena.alloc<int>(pt.size());
-    QCK(cudaMemcpy(d, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice));
+    h2d(d, pt.data(), pt.size() * 4);
     bt.tkv.page_table = d;
   }
   // CodePredictor KV: one page (all its positions) per sequence
@@ -1891,7 +1923,7 @@ void Engine::ensure_batch() {
     std::vector<int> pt(cap);
     for (int i = 0; i < cap; ++i) pt[i] = i;
     int* d = arena.alloc<int>(cap);
-    QCK(cudaMemcpy(d, pt.data(), cap * 4, cudaMemcpyHostToDevice));
+    h2d(d, pt.data(), (size_t)cap * 4);
     bt.ckv.page_table = d;
   }
   // 16-row token tiles with a split-K workspace
@@ -2482,9 +2514,9 @@ int32_t qtts_generate_codes_from_rows(qtts_engine* h, const float* prefill, size
     if (P > e.max_cache_steps) qtts::invalid("prefill longer than max_cache_steps");
     const size_t H = e.cfg.talker.hidden;
     const size_t Tn = std::min(T, e.max_cache_steps + 1);
-    QCK(cudaMemcpy(e.tb.x, prefill, P * H * 4, cudaMemcpyHostToDevice));
-    if (Tn) QCK(cudaMemcpy(e.trailing, trailing, Tn * H * 4, cudaMemcpyHostToDevice));
-    QCK(cudaMemcpy(e.tts_pad, pad, H * 4, cudaMemcpyHostToDevice));
+    e.h2d(e.tb.x, prefill, P * H * 4);
+    if (Tn) e.h2d(e.trailing, trailing, Tn * H * 4);
+    e.h2d(e.tts_pad, pad, H * 4);
     e.begin((int)P, (int)Tn, *o);
     finish_generation(e, codes_out, cap, frames_out, ended);
   });
@@ -2670,7 +2702,7 @@ int32_t qtts_text_stream_next_codes_chunk(qtts_text_stream* h, size_t max_chunk,
     const size_t H = e.cfg.talker.hidden;
     if (!tr_ids.empty()) e.project_text(tr_ids, e.trailing + (size_t)e.seq_frames * H);
     const int ntr = e.seq_frames + (int)tr_ids.size();
-    QCK(cudaMemcpyAsync(&e.st->n_trailing, &ntr, 4, cudaMemcpyHostToDevice, e.stream));
+    e.h2d(&e.st->n_trailing, &ntr, 4);
     QCK(cudaStreamSynchronize(e.stream));
     const size_t before = e.seq_frames;
     const size_t produced = e.run_frames(n);
@@ -2719,7 +2751,7 @@ int32_t qtts_talker_prefill(qtts_engine* h, const float* rows, size_t steps, flo
     if (steps == 0) qtts::invalid("prefill steps must be non-zero");
     if (steps > e.max_cache_steps) qtts::invalid("prefill steps outside cache");
     const size_t H = e.cfg.talker.hidden;
-    QCK(cudaMemcpy(e.tb.x, rows, steps * H * 4, cudaMemcpyHostToDevice));
+    e.h2d(e.tb.x, rows, steps * H * 4);
     qtts_generate_options o;
     qtts_generate_options_default(&o);
     o.do_sample = 0;
@@ -2739,11 +2771,11 @@ int32_t qtts_talker_decode_step(qtts_engine* h, const float* input, size_t offse
     need(input, "input");
     if (offset >= e.max_cache_steps) qtts::invalid("offset outside cache length");
     const size_t H = e.cfg.talker.hidden;
-    QCK(cudaMemcpy(e.tb.x, input, H * 4, cudaMemcpyHostToDevice));
+    e.h2d(e.tb.x, input, H * 4);
     e.st_host->talker_pos = (int)offset;
     e.st_host->halt = 0;
     e.st_host->frames = 0;
-    QCK(cudaMemcpy(e.st, e.st_host, sizeof(qtts::SeqState), cudaMemcpyHostToDevice));
+    e.h2d(e.st, e.st_host, sizeof(qtts::SeqState));
     qtts::SampleCfg greedy{0, 0, 1.f, 1.f};
     e.stack_step(e.talker, e.tb, e.tkv, &e.st->talker_pos, 0, nullptr);
     e.talker_head(qtts::ROLE_TALKER_STEP, e.tb.x, greedy, 1.0f, nullptr, e.cp_prefix_target());
@@ -2825,36 +2857,14 @@ int32_t qtts_talker_decode_step_static(qtts_engine* h, const float* input, size_
     B.attn = B.qkv + nqkv;
     B.h1 = B.attn + nattn;
     B.act = B.h1 + nh1;
-    QCK(cudaMemcpy(B.x, input, H * 4, cudaMemcpyHostToDevice));
+    e.h2d(B.x, input, H * 4);
     e.st_host->talker_pos = (int)offset;
     e.st_host->halt = 0;
     e.st_host->frames = 0;
-    QCK(cudaMemcpy(e.st, e.st_host, sizeof(qtts::SeqState), cudaMemcpyHostToDevice));
-    const float scale = 1.0f / std::sqrt((float)c.head_dim);
-    for (int l = 0; l < c.layers; ++l) {
-      e.linear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr, 1,
-               S.qkv_w, c.hidden, qtts::EPI_STORE, nullptr);
-      qtts::AttnDecodeArgs da{};
-      da.qkv = B.qkv;
-      da.q_gamma = S.q_g[l];
-      da.k_gamma = S.k_g[l];
-      da.eps = c.eps;
-      da.rope_cos = S.rope_cos;
-      da.rope_sin = S.rope_sin;
-      da.kv = e.tkv;
-      da.layer = l;
-      da.pos_ptr = &e.st->talker_pos;
-      da.q_heads = c.q_heads;
-      da.scale = scale;
-      da.out = B.attn;
-        QCK(qtts::launch_attn_decode(da, e.stream));
-      e.linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, 1,
-               c.hidden, S.q_out, qtts::EPI_RESID, nullptr);
-      e.linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
-               nullptr, 1, c.intermediate, c.hidden, qtts::EPI_SWIGLU, nullptr);
-      e.linear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.x, c.hidden, B.h1, c.hidden,
-               nullptr, 1, c.hidden, c.intermediate, qtts::EPI_RESID, nullptr);
-    }
+    e.h2d(e.st, e.st_host, sizeof(qtts::SeqState));
+    // The same layer sequence as qtts_talker_decode_step, over the static
+    // array (the engine's other workspaces were allocated at load).
+    e.stack_step(S, B, e.tkv, &e.st->talker_pos, 0, nullptr);
     qtts::SampleCfg greedy{0, 0, 1.f, 1.f};
     e.talker_head(qtts::ROLE_TALKER_STEP, B.x, greedy, 1.0f, nullptr, e.cp_prefix_target());
     e.sync_state();
@@ -2879,8 +2889,8 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
     e.validate(opt);
     const size_t H = e.cfg.talker.hidden;
     const auto& C = e.cfg.cp;
-    QCK(cudaMemcpy(e.cp_prefix_target(), talker_hidden, H * 4, cudaMemcpyHostToDevice));
-    QCK(cudaMemcpy(e.cp_prefix_target() + H, semantic_embed, H * 4, cudaMemcpyHostToDevice));
+    e.h2d(e.cp_prefix_target(), talker_hidden, H * 4);
+    e.h2d(e.cp_prefix_target() + H, semantic_embed, H * 4);
     qtts::SeqState s{};
     s.semantic = 0;
     s.rng_kind = opt.rng;
@@ -2888,7 +2898,7 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
     s.rng_seed = opt.seed;
     s.n_trailing = 0;
     *e.st_host = s;
-    QCK(cudaMemcpy(e.st, e.st_host, sizeof(s), cudaMemcpyHostToDevice));
+    e.h2d(e.st, e.st_host, sizeof(s));
     const qtts::SampleCfg sc = qtts::sub_cfg(opt);
     // Eager CodePredictor pass with per-group logits kept for parity checks.
     if (e.has_proj())

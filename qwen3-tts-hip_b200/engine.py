@@ -520,8 +520,11 @@ class HipTtsEngine:
         return hidden, logits, tok.value
 
     def talker_decode_step_static(self, step_input: np.ndarray, offset: int):
-        """talker_decode_step without any device allocation by the call: the
-        attention scratch lives in the library's static device array."""
+        """talker_decode_step for hosts that may not allocate device memory
+        while running: the call allocates nothing. All of its per-call
+        activations (input row, QKV, attention output, post-attention row and
+        MLP row of every layer) live in the library's 264 KiB static device
+        array, which every call shares; overlapping calls race."""
         x = np.ascontiguousarray(step_input, dtype=np.float32)
         hidden = np.zeros(self.hidden, np.float32)
         logits = np.zeros(self.info.vocab, np.float32)

@@ -32,3 +32,20 @@ def oracles(model_dirs):
     from oracle import qtts_oracle as O
 
     return {s: O.OracleModel(d, 128) for s, d in model_dirs.items()}
+
+
+@pytest.fixture(scope="session")
+def full_model_dir(tmp_path_factory):
+    """Lazily written full-size synthetic checkpoints ("0.6b", "1.7b"), shared
+    by every test of the session."""
+    from oracle import synth
+
+    base = Path(os.environ.get("QTTS_TEST_MODELS", str(tmp_path_factory.mktemp("full"))))
+    made = {}
+
+    def get(shape):
+        if shape not in made:
+            made[shape] = synth.write_model(base / shape, shape, 0)
+        return made[shape]
+
+    return get

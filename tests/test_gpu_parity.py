@@ -15,6 +15,7 @@ import pytest
 import torch
 
 from oracle import qtts_oracle as O, synth
+from parity import check_codes
 
 pytestmark = pytest.mark.gpu
 
@@ -121,8 +122,7 @@ def test_sampled_rollout(engines, oracles, pkg, shape, rng):
     pre, tr, pad = m.prepare(list(ids))
     codes, _, recs = m.rollout(pre, tr, pad, 16, SAMPLED, SAMPLED, penalty=1.05, seed=11,
                                rng_kind=rng, forced_codes=out.codes)
-    agree = np.mean(np.asarray(out.codes) == np.asarray(codes[: len(out.codes)]))
-    assert agree >= 0.98, agree
+    check_codes(out.codes, codes, recs, f"sampled {shape} {rng}", sampled=True)
 
 
 def test_cpu_sampler_path(engines, oracles, pkg):
@@ -135,9 +135,9 @@ def test_cpu_sampler_path(engines, oracles, pkg):
     t = O.SamplingConfig(True, 300, 0.8, 0.9)
     s = O.SamplingConfig(True, 0, 0.9, 0.9)
     pre, tr, pad = m.prepare(list(ids))
-    codes, _, _ = m.rollout(pre, tr, pad, 6, t, s, penalty=1.05, seed=3, forced_codes=out.codes)
-    agree = np.mean(np.asarray(out.codes) == np.asarray(codes[: len(out.codes)]))
-    assert agree >= 0.95, agree
+    codes, _, recs = m.rollout(pre, tr, pad, 6, t, s, penalty=1.05, seed=3,
+                               forced_codes=out.codes)
+    check_codes(out.codes, codes, recs, "cpu sampler path", sampled=True)
 
 
 def test_graph_equals_eager(engines, oracles, pkg):
@@ -419,9 +419,10 @@ for shape, d in [('tiny', {str(model_dirs['tiny'])!r}), ('tiny_proj', {str(model
     out2 = e.generate_codes_from_ids(ids, s)
     assert list(e.generate_codes_from_ids(ids, s).codes) == list(out2.codes), shape  # repeatable
     sc = O.SamplingConfig(True, 50, 1.0, 0.9)
-    codes2, _, _ = m.rollout(pre, tr, pad, 12, sc, sc, penalty=1.05, seed=4, forced_codes=out2.codes)
-    agree = np.mean(np.asarray(out2.codes) == np.asarray(codes2[: len(out2.codes)]))
-    assert agree >= 0.98, (shape, agree)
+    codes2, _, recs2 = m.rollout(pre, tr, pad, 12, sc, sc, penalty=1.05, seed=4, forced_codes=out2.codes)
+    ms = [x for r in recs2 for x in [r.talker_margin] + r.cp_margins]
+    bad2 = [i for i, (a, b) in enumerate(zip(out2.codes, codes2)) if a != b and ms[i] > 1e-2]
+    assert not bad2, (shape, bad2)
 print("frame kernel ok")
 """
     env = dict(os.environ, **{env_var: value})

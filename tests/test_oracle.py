@@ -122,3 +122,36 @@ def test_prefill_layout(oracles):
     cfg = m.cfg["talker_config"]
     torch.testing.assert_close(pre[-1], t[-1] + m.codec_emb[cfg["codec_bos_id"]])
     torch.testing.assert_close(pre[-2], t[-2] + m.codec_emb[cfg["codec_pad_id"]])
+
+
+def test_reference_kernel_extraction():
+    """oracle/build_ref.py finds every reference kernel that oracle/ref_launch.cu
+    launches (needs the reference tree, present where the library is built)."""
+    import re
+    from pathlib import Path
+
+    from oracle import build_ref
+
+    if not (build_ref.DEFAULT_REFERENCE / "src" / "gpu" / "kernels.rs").exists():
+        pytest.skip("reference tree not on this machine")
+    names = set(build_ref.kernel_names(build_ref.extract(build_ref.DEFAULT_REFERENCE)))
+    launched = set(re.findall(r"(\w+_f32)<<<", (Path(build_ref.HERE) / "ref_launch.cu").read_text()))
+    assert launched and launched <= names, launched - names
+
+
+def test_reference_kernel_library_exports():
+    """The built checker library exports one wrapper per launched kernel."""
+    import ctypes
+
+    from oracle import ref_kernels
+
+    if not ref_kernels.available():
+        pytest.skip("oracle/_ref/libqtts_ref.so not built")
+    try:
+        lib = ctypes.CDLL(str(ref_kernels.LIB))
+    except OSError as e:  # no CUDA driver on this machine
+        pytest.skip(str(e))
+    for fn in ("ref_rmsnorm", "ref_rope", "ref_write_kv", "ref_attention_scores_cache",
+               "ref_softmax", "ref_apply_value_cache", "ref_residual_add", "ref_swiglu",
+               "ref_argmax", "ref_suppress", "ref_penalty", "ref_sample_topk"):
+        assert hasattr(lib, fn), fn
