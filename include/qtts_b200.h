@@ -108,9 +108,10 @@ typedef struct {
   uint32_t codec_eos;
   size_t max_cache_steps;
   size_t device_bytes; /* weights + KV + workspaces held on the device */
-  /* Decode MLP of the talker [0] and the CodePredictor [1]: CTAs per cluster of
-   * the fused gate|up + down kernel, 0 when it runs as two GEMVs. */
-  int32_t fused_mlp_cluster[2];
+  /* CTAs of the persistent CodePredictor pass (one per SM), 0 when the
+   * CodePredictor runs as one kernel per op. */
+  int32_t cp_pass_grid;
+  int32_t reserved;
   int32_t has_codec;          /* speech_tokenizer/model.safetensors was loaded */
   uint32_t samples_per_frame; /* waveform samples per code frame (24 kHz): 1920 */
 } qtts_engine_info;
@@ -256,6 +257,20 @@ int32_t qtts_talker_decode_step_static(qtts_engine* engine, const float* input, 
 int32_t qtts_code_predictor(qtts_engine* engine, const float* talker_hidden,
                             const float* semantic_embed, const qtts_generate_options* options,
                             int32_t* tokens_out, float* embedding_sum_out, float* logits_out);
+
+/* Measurement hook (no reference counterpart): device time (CUDA events on
+ * the engine stream, inside the frame graph) of the persistent CodePredictor
+ * pass of the last frame the last generation call ran, and the weight bytes
+ * one pass streams. QTTS_ERR_UNSUPPORTED when the pass is off. */
+int32_t qtts_last_cp_pass_timing(const qtts_engine* engine, float* ms, double* weight_bytes);
+
+/* Self-test of the library's bounded device waits (no reference
+ * counterpart): one kernel waits for a device counter that nothing
+ * increments, bounded by limit_us microseconds (at most 5 s), the same way the
+ * persistent CodePredictor pass waits for the other CTAs. Returns
+ * QTTS_ERR_DEVICE_STATE ("a bounded device wait ran out") once the bound
+ * expires; the engine stays usable afterwards. */
+int32_t qtts_selftest_device_wait(qtts_engine* engine, uint32_t limit_us);
 
 /* Device time of the last generation's frame loop (CUDA events), in ms. */
 int32_t qtts_last_timings(const qtts_engine* engine, float* prefill_ms, float* frames_ms,

@@ -111,20 +111,23 @@ def argmax_device(logits: np.ndarray) -> int:
     return best_i
 
 
-def _cdf_margin(probs, j: int, target0) -> float:
-    """Distance of the inverse-CDF target from the edges of the bucket it fell
-    in, as a fraction of the total mass: how far the draw was from picking a
-    neighbour. Summation in fp32 in candidate order, as the walk does."""
+def _cdf_margin(probs, j: int, target0, temperature: float) -> float:
+    """How robust an inverse-CDF draw is, in logit units: the smallest logit
+    error that could move an edge of the drawn bucket j past the target.
+    With every logit off by at most d, each probability (and so the mass C_e
+    below an edge e, and the target u * sum) moves by a factor of at most
+    exp(d / T), so the edge crosses the target only once
+    d / T >= |target - C_e| / (target + C_e). Sums in fp32, candidate order."""
     before = np.float32(0.0)
     for i in range(j):
         before = np.float32(before + probs[i])
     after = np.float32(before + probs[j])
-    total = np.float32(0.0)
-    for p in probs:
-        total = np.float32(total + p)
-    if not total > 0:
-        return float("inf")
-    return float(min(float(target0) - float(before), float(after) - float(target0)) / float(total))
+    t = float(target0)
+    best = float("inf")
+    for edge in (float(before), float(after)):
+        if t + edge > 0:
+            best = min(best, abs(t - edge) / (t + edge) * float(temperature))
+    return best
 
 
 def sample_topk_device(logits: np.ndarray, top_k: int, temperature: float, u: np.float32,
@@ -155,7 +158,7 @@ def sample_topk_device(logits: np.ndarray, top_k: int, temperature: float, u: np
             break
         target = np.float32(target - probs[i])
     tok = int(order[pick])
-    return (tok, _cdf_margin(probs, pick, target0)) if with_margin else tok
+    return (tok, _cdf_margin(probs, pick, target0, temperature)) if with_margin else tok
 
 
 def sample_cpu(logits: np.ndarray, cfg: SamplingConfig, rng, with_margin: bool = False):
@@ -202,7 +205,7 @@ def sample_cpu(logits: np.ndarray, cfg: SamplingConfig, rng, with_margin: bool =
             break
         target = np.float32(target - p)
     tok = int(idx[pick])
-    return (tok, _cdf_margin(probs, pick, target0)) if with_margin else tok
+    return (tok, _cdf_margin(probs, pick, target0, cfg.temperature)) if with_margin else tok
 
 
 def select(logits: np.ndarray, cfg: SamplingConfig, rng) -> int:
@@ -213,8 +216,9 @@ def select(logits: np.ndarray, cfg: SamplingConfig, rng) -> int:
 
 def select_margin(logits: np.ndarray, cfg: SamplingConfig, rng):
     """select() plus how robust its choice is against small logit errors:
-    greedy -> the top-2 logit gap (logit units); sampled -> the distance of the
-    inverse-CDF target from its bucket's edges (fraction of probability mass).
+    greedy -> the top-2 logit gap; sampled -> the smallest logit error that
+    could move an edge of the drawn bucket past the inverse-CDF target (both
+    in logit units).
     A GPU run whose logits differ from these by bf16 rounding can pick a
     different token only where this margin is small."""
     if not cfg.do_sample:
@@ -488,11 +492,13 @@ class OracleModel:
         """generate_inner[_sampled] (code_predictor.rs:366-471): 2-row prefill at
         positions 0,1, head 0, then groups g=1..14 decoded at offset g+1.
         ``forced`` (15 ids) replays given tokens (teacher forcing) while still
-        consuming the same RNG draws, so logits can be compared along a path."""
+        consuming the same RNG draws, so logits can be compared along a path.
+        Returns the path's tokens; the oracle's own choice at every step (what
+        it would have selected on that path) is kept in ``last_cp_choices``."""
         self.cp.reset()
         prefix = torch.stack([talker_hidden, semantic_embed])
         out = self.cp.forward(self.project(prefix), 0)
-        tokens, gaps, all_logits, margins = [], [], [], []
+        tokens, gaps, all_logits, margins, choices = [], [], [], [], []
         h = out[1]
         emb_sum = None
         for g in range(self.groups - 1):
@@ -503,12 +509,14 @@ class OracleModel:
             gaps.append(top2_gap(lg))
             tok, margin = select_margin(lg, cfg, rng)
             margins.append(margin)
+            choices.append(tok)
             if forced is not None:
                 tok = int(forced[g])
             tokens.append(tok)
             cur = self.cp_embs[g][tok]
             emb_sum = cur.clone() if emb_sum is None else emb_sum + cur
         self.last_cp_margins = margins
+        self.last_cp_choices = choices
         return tokens, emb_sum, gaps, all_logits
 
     # ---- rollout (generation.rs:657-749) ----------------------------------
@@ -517,29 +525,39 @@ class OracleModel:
                 forced_codes=None):
         """Frame loop: EOS check, CP prefix, CP pass, append 16 codes, step input,
         talker decode at P+frame. ``forced_codes`` ([frames*16]) teacher-forces
-        the path so per-frame logits/gaps can be checked against another run."""
+        the path so per-frame choices can be checked against another run: the
+        returned codes are then the ORACLE'S OWN choices at every step of the
+        forced path (not the forced codes), frame count and EOS follow the
+        path, and ``final_choice`` / ``final_margin`` hold the oracle's choice
+        (and its margin) for the semantic token that ended the path (None when
+        max_frames ended it)."""
         rng = Lcg(seed) if rng_kind == "lcg" else PhiloxStream(seed)
         P = prefill.shape[0]
         _, hidden, logits = self.talker_prefill(prefill)
         logits = self.penalise_and_suppress(logits, None, 1.0)
         semantic, margin = select_margin(logits, talker_cfg, rng)
+        choice = semantic
         gaps = [top2_gap(logits)]
         margins = [margin]
         if forced_codes is not None and len(forced_codes) >= 16:
             semantic = int(forced_codes[0])
+        elif forced_codes is not None:
+            semantic = self.codec_eos  # the forced path produced no frame: it ended here
         codes, history, records = [], [], []
         ended = False
+        self.final_choice, self.final_margin = None, None
         for frame in range(max_frames):
             if semantic == self.codec_eos:
                 ended = True
+                self.final_choice, self.final_margin = choice, margins[-1]
                 break
             sem_emb = self.codec_emb[semantic]
             forced = None
             if forced_codes is not None and len(forced_codes) >= 16 * (frame + 1):
                 forced = forced_codes[16 * frame + 1: 16 * frame + 16]
             toks, emb_sum, cp_gaps, _ = self.code_predictor(hidden, sem_emb, sub_cfg, rng, forced)
-            codes.append(semantic)
-            codes.extend(toks)
+            codes.append(choice)
+            codes.extend(self.last_cp_choices)
             history.append(semantic)
             records.append(FrameRecord(semantic, gaps[-1], toks, cp_gaps, margins[-1],
                                        list(self.last_cp_margins)))
@@ -550,10 +568,13 @@ class OracleModel:
                 use_hist = penalty != 1.0 or talker_cfg.do_sample
                 logits = self.penalise_and_suppress(logits, history if use_hist else None, penalty)
                 semantic, margin = select_margin(logits, talker_cfg, rng)
+                choice = semantic
                 gaps.append(top2_gap(logits))
                 margins.append(margin)
                 if forced_codes is not None and len(forced_codes) >= 16 * (frame + 2):
                     semantic = int(forced_codes[16 * (frame + 1)])
+                elif forced_codes is not None:
+                    semantic = self.codec_eos  # the forced path ended after this frame
         return codes, ended, records
 
 

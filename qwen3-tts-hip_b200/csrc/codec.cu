@@ -8,7 +8,7 @@
 namespace qtts {
 namespace {
 
-constexpr int kTileCo = 64, kTileT = 128, kTileK = 16, kConvThreads = 256;
+constexpr int kTileT = 128, kTileK = 16, kConvThreads = 256;
 
 template <int ACT>
 __device__ __forceinline__ float codec_act(const CodecConvArgs& a, int ci, int src) {

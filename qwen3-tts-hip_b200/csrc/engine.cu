@@ -29,7 +29,7 @@
 #include <vector>
 
 #include "codec.h"
-#include "frame_kernel.h"
+#include "cp_pass.h"
 #include "gemm_tc.h"
 #include "json.h"
 #include "kernels.h"
@@ -57,7 +57,6 @@ struct QttsError : std::runtime_error {
 constexpr uint64_t kSeedXor = 0x9e3779b97f4a7c15ull;  // generation.rs:667
 constexpr int kNewline = 198;                          // text.rs:15
 constexpr int kTalkerPageShift = 5;                    // 32 positions per KV page
-constexpr int kFrameTalkerSplits = 4;                  // frame kernel talker attention splits
 
 // ---------------------------------------------------------------------------
 // safetensors (8-byte LE header length, JSON header, raw little-endian data)
@@ -224,6 +223,10 @@ class Arena {
     const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
     QCK(cudaMalloc(&p, bytes));
     QCK(cudaMemset(p, 0, bytes));
+    // The zeroing runs on the legacy stream, which the engine's non-blocking
+    // stream does not wait for: finish it before anything is uploaded into
+    // the new buffer on that stream.
+    QCK(cudaStreamSynchronize(0));
     ptrs_.push_back(p);
     bytes_ += bytes;
     return static_cast<T*>(p);
@@ -239,7 +242,6 @@ struct DevStack {
   StackCfg c;
   int q_out, kv_out, qkv_w;
   std::vector<__nv_bfloat16*> wqkv, wo, wgu, wdown;
-  std::vector<__nv_bfloat16*> wdownT;  // [I, H] copies for the fused decode MLP (empty: unused)
   std::vector<float*> in_g, post_g, q_g, k_g;
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
@@ -651,10 +653,24 @@ class Engine {
   std::vector<int> pinned_ids_storage;
 
   std::map<SampleKey, cudaGraphExec_t> graphs;
-  // persistent frame kernel
-  std::map<SampleKey, std::pair<FrameOp*, int>> frame_ops;  // device op lists
-  int frame_grid = 0;
-  bool use_frame_kernel = true;
+  // Persistent CodePredictor pass (one cooperative launch per frame; the
+  // per-op kernels when QTTS_CP_PASS=0 or the shape is unsupported).
+  bool use_cp_pass = false;
+  int cp_grid = 0;
+  CpOp* cp_ops = nullptr;
+  CpLoad* cp_loads = nullptr;
+  int cp_n_ops = 0;
+  unsigned long long* cp_counter = nullptr;
+  int* cp_err = nullptr;
+  unsigned long long* cp_trace = nullptr;  // with QTTS_STEP_TRACE: [ops][4] stamps of CTA 0
+  std::vector<std::string> cp_op_names;
+  cudaEvent_t cp_ev[2] = {nullptr, nullptr};  // around the pass inside the frame graph
+  float last_cp_ms = 0.f;        // the pass of the last frame of the last burst
+  double cp_weight_bytes = 0.0;  // weight bytes one pass streams
+  unsigned long long* selftest_ctr = nullptr;  // qtts_selftest_device_wait
+  int* selftest_status = nullptr;
+  void build_cp_pass();
+  void launch_cp(const SampleKey& k, float* dbg_logits = nullptr, float* emb_sum_out = nullptr);
   // tcgen05 projections for M >= tc_min_rows rows (QTTS_TC=0 disables)
   // Which projections use it is fixed per call site, not per row count, so a
   // row gets identical arithmetic however the rows are batched (one-shot vs
@@ -672,22 +688,6 @@ class Engine {
   };
   // CodePredictor attention inside the O projection (QTTS_FUSE_ATTN_O=0: separate kernels)
   bool fuse_attn_o = true;
-  // Fused decode MLP (QTTS_FUSE_MLP=1; default: gate|up and down as two
-  // GEMVs); used for a stack when its shape fits and all its clusters can be
-  // resident at once.
-  float* mlp_ws = nullptr;
-  unsigned* mlp_tickets = nullptr;
-  int* mlp_err = nullptr;
-  int mlp_cluster[2] = {0, 0};  // talker, CodePredictor: cluster size, 0 = not fused
-  unsigned* frame_seq = nullptr;
-  int* frame_error = nullptr;
-  unsigned* frame_counters = nullptr;
-  long long* frame_trace = nullptr;  // QTTS_FRAME_TRACE=<file>: per-op clock64 trace
-  std::string frame_trace_path;
-  struct TagBufs {
-    TV *x, *qkv, *attn, *h1, *act;
-  } ct{}, tt{};
-  TV *logits_t = nullptr, *cp_cache_t = nullptr, *cp_dummy_t = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
   float last_prefill_ms = 0.f, last_frames_ms = 0.f;
   size_t last_frames = 0;
@@ -724,8 +724,6 @@ class Engine {
     }
     static const char* kEpi[] = {"gemv", "gemv+resid", "gemv+swiglu", "gemv+bias", "gemv+bias+silu"};
     a.trace_id = trace_tag(kEpi[epi], N, K);
-    a.trigger = trigger_mode;
-    plan_prefetch(a, (size_t)(epi == EPI_SWIGLU ? 2 : 1) * N * K * sizeof(__nv_bfloat16));
     QCK(launch_linear(a, epi, stream));
     ++launches;
   }
@@ -733,28 +731,12 @@ class Engine {
   // Post-attention half of a decode layer for one row: B.x = B.h1 + MLP(B.h1).
   void mlp(const DevStack& S, int l, StackBufs& B, const int* halt) {
     const StackCfg& c = S.c;
-    if (!S.wdownT.empty()) {
-      MlpArgs m{S.wgu[l], S.wdownT[l], B.h1, S.post_g[l], c.eps, B.x, mlp_ws, mlp_tickets,
-                c.hidden, c.intermediate, halt, mlp_err};
-      m.trace_id = trace_tag("mlp", c.intermediate, c.hidden);
-      m.cluster = &S == &talker ? mlp_cluster[0] : mlp_cluster[1];
-      m.trigger = trigger_mode;
-      QCK(launch_mlp_fused(m, stream));
-      ++launches;
-      return;
-    }
     linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
            nullptr, 1, c.intermediate, c.hidden, EPI_SWIGLU, halt);
     linear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.x, c.hidden, B.h1, c.hidden,
            nullptr, 1, c.hidden, c.intermediate, EPI_RESID, halt);
   }
 
-  // ---- L2 prefetch plan ----
-  // A frame graph is captured twice: the first capture records every weight
-  // matrix in launch order (a cyclic byte stream, since frames repeat); the
-  // second gives each op the stream range pf_ahead bytes past its own
-  // weights, of the same length, to prefetch into L2 before its dependency
-  // wait. HBM then streams weights ahead of the chain of dependent launches.
   // ---- step trace (QTTS_STEP_TRACE=<file>) ----
   // Frame `trace_frame` of each run records, per launch, the first CTA entry,
   // the first CTA past its dependency wait and the last CTA exit.
@@ -765,46 +747,13 @@ class Engine {
   std::vector<std::string> trace_names;
   size_t trace_frame = 6;
   int trace_tag(const char* kind, int N, int K) {
-    if (!trace_capture || pf_mode == 1 || (int)trace_names.size() + 1 >= kTraceCap) return 0;
+    if (!trace_capture || (int)trace_names.size() + 1 >= kTraceCap) return 0;
     trace_names.push_back(std::string(kind) + " N=" + std::to_string(N) + " K=" + std::to_string(K));
     return (int)trace_names.size();
   }
   void dump_step_trace();
 
-  // Decode GEMVs launch their dependents after the dependency wait (1):
-  // measured faster than at entry (0), which floods the memory queues with
-  // weight loads of several launches at once. QTTS_TRIGGER overrides.
-  int trigger_mode = 1;
   unsigned* crumbs_host = nullptr;  // QTTS_CRUMBS=1: last kernel ids entered / left
-  size_t pf_ahead = 0;                          // QTTS_L2_PREFETCH=<MB> enables
-  int pf_mode = 0;                              // 0 off, 1 record, 2 apply
-  std::vector<std::pair<const char*, size_t>> pf_ops;
-  size_t pf_next = 0;
-  void plan_prefetch(LinearArgs& a, size_t bytes) {
-    if (pf_mode == 1) {
-      pf_ops.push_back({reinterpret_cast<const char*>(a.W), bytes});
-    } else if (pf_mode == 2 && pf_next < pf_ops.size()) {
-      size_t total = 0, own = 0;
-      for (size_t i = 0; i < pf_ops.size(); ++i) {
-        if (i == pf_next) own = total;
-        total += pf_ops[i].second;
-      }
-      size_t want = pf_ops[pf_next].second;
-      size_t at = (own + std::min(pf_ahead, total - want)) % total;
-      int piece = 0;
-      while (want > 0 && piece < 3) {
-        size_t base = 0, i = 0;
-        while (base + pf_ops[i].second <= at) base += pf_ops[i++].second;
-        const size_t take = std::min(want, base + pf_ops[i].second - at);
-        a.pf_ptr[piece] = pf_ops[i].first + (at - base);
-        a.pf_bytes[piece] = (unsigned)take;
-        ++piece;
-        want -= take;
-        at = (at + take) % total;
-      }
-      ++pf_next;
-    }
-  }
   void stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int pos0, const int* halt);
   void stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* pos_ptr, int pos_const,
                   const int* halt);
@@ -849,11 +798,6 @@ class Engine {
   void generate_batch(const std::vector<std::vector<uint32_t>>& ids,
                       const std::vector<qtts_generate_options>& opts, int32_t* codes_out,
                       size_t cap_per_request, size_t* frames_out, int32_t* ended_out);
-  void enqueue_frame_kernel(const SampleKey& k);
-  std::vector<FrameOp> build_frame_ops(const SampleKey& k);
-  bool frame_ops_fit(const std::vector<FrameOp>& ops) const;
-  void check_frame_error();
-  void dump_frame_trace(const SampleKey& k);
   cudaGraphExec_t frame_graph(const SampleKey& k);
 
   // ---- text prep ----
@@ -997,7 +941,7 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   if (dev < 0 || dev >= ndev) invalid("device " + std::to_string(dev) + " not present");
   QCK(cudaSetDevice(dev));
   QCK(configure_kernels());
-  QCK(configure_frame_kernel());
+  QCK(configure_cp_pass());
   QCK(configure_tc_kernels());
   QCK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   QCK(cudaEventCreate(&ev0));
@@ -1135,10 +1079,6 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   tp_b = arena.alloc<float>((size_t)tp_rows * text_inter);
   tp_c = arena.alloc<float>((size_t)tp_rows * T.hidden);
   {
-    // The persistent frame kernel is opt-in (QTTS_FRAME_KERNEL=1) until it
-    // beats the per-op graph; both paths are parity-tested.
-    const char* env = std::getenv("QTTS_FRAME_KERNEL");
-    use_frame_kernel = env && env[0] == '1';
     if (const char* tp = std::getenv("QTTS_STEP_TRACE")) {
       step_trace_path = tp;
       step_trace = arena.alloc<unsigned long long>(8 * (size_t)kTraceCap);
@@ -1150,73 +1090,15 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
       QCK(set_crumbs_kernels(d));
       QCK(set_crumbs_gemm(d));
     }
-    if (const char* tg = std::getenv("QTTS_TRIGGER")) trigger_mode = std::atoi(tg);
-    if (const char* pa = std::getenv("QTTS_L2_PREFETCH"))
-      pf_ahead = (size_t)std::max(0, std::atoi(pa)) << 20;
     const char* fz = std::getenv("QTTS_FUSE_ATTN_O");
     fuse_attn_o = !(fz && fz[0] == '0');
-    // Opt-in: measured slower than the two GEMVs on B200 (its cross-CTA
-    // reduction adds more L2 round trips than the launch it removes).
-    const char* fm = std::getenv("QTTS_FUSE_MLP");
-    if (fm && fm[0] == '1') {
-      for (DevStack* S : {&talker, &cp}) {
-        const int H = S->c.hidden, I = S->c.intermediate;
-        if (!mlp_fused_supported(H, I)) continue;
-        // Largest cluster size whose clusters all fit on the GPU at once.
-        int& cl = &*S == &talker ? mlp_cluster[0] : mlp_cluster[1];
-        for (int c : {8, 4, 2}) {
-          int resident = 0;
-          QCK(configure_mlp_fused(H, I, c, &resident));
-          if (resident >= kMlpCtas / c) { cl = c; break; }
-        }
-        if (!cl) continue;
-        for (int l = 0; l < S->c.layers; ++l) {
-          __nv_bfloat16* t = arena.alloc<__nv_bfloat16>((size_t)I * H);
-          QCK(launch_transpose_bf16(S->wdown[l], H, I, t, stream));
-          S->wdownT.push_back(t);
-        }
-        if (!mlp_ws) {
-          mlp_ws = arena.alloc<float>((size_t)(kMlpCtas / 2) * std::max(T.hidden, C.hidden));
-          mlp_tickets = arena.alloc<unsigned>(kMlpMaxCluster);
-          mlp_err = arena.alloc<int>(1);
-          QCK(cudaMemsetAsync(mlp_tickets, 0, kMlpMaxCluster * sizeof(unsigned), stream));
-          QCK(cudaMemsetAsync(mlp_err, 0, sizeof(int), stream));
-        }
-      }
-      QCK(cudaStreamSynchronize(stream));
-    }
-    frame_grid = frame_grid_size(dev);
-    if (const char* g = std::getenv("QTTS_FRAME_GRID"))  // profiling aid: fewer CTAs
-      frame_grid = std::min(frame_grid, std::atoi(g));
-    if (use_frame_kernel && frame_grid > 0) {
-      auto bufs = [&](const DevStack& S, int rows, int nsplit) {
-        TagBufs b;
-        const size_t Hh = S.c.hidden, I = S.c.intermediate;
-        b.x = arena.alloc<TV>(rows * Hh);
-        b.qkv = arena.alloc<TV>((size_t)rows * S.qkv_w);
-        b.attn = arena.alloc<TV>(nsplit > 1 ? (size_t)S.c.q_heads * nsplit * (2 + kHeadDim)
-                                            : (size_t)rows * S.q_out);
-        b.h1 = arena.alloc<TV>(rows * Hh);
-        b.act = arena.alloc<TV>(rows * I);
-        return b;
-      };
-      ct = bufs(cp, 2, 1);
-      tt = bufs(talker, 1, kFrameTalkerSplits);
-      logits_t = arena.alloc<TV>(std::max(T.vocab, C.vocab));
-      cp_cache_t = arena.alloc<TV>((size_t)C.layers * 2 * C.kv_heads * kFrameCpPositions * kHeadDim);
-      cp_dummy_t = arena.alloc<TV>(T.hidden);
-      frame_seq = arena.alloc<unsigned>(4);
-      const unsigned one = 1;
-      QCK(cudaMemcpy(frame_seq, &one, 4, cudaMemcpyHostToDevice));
-      frame_error = arena.alloc<int>(4);
-      frame_counters = arena.alloc<unsigned>(8 * 8192);
-      if (const char* tp = std::getenv("QTTS_FRAME_TRACE")) {
-        frame_trace_path = tp;
-        frame_trace = arena.alloc<long long>(8 * 8192);
-      }
-    } else {
-      use_frame_kernel = false;
-    }
+    const char* cz = std::getenv("QTTS_CP_PASS");
+    cp_grid = cp_pass_grid(dev);
+    use_cp_pass = !(cz && cz[0] == '0') && cp_grid > 0 &&
+                  cp_pass_supported(C.hidden, C.intermediate, C.q_heads, C.kv_heads, T.hidden,
+                                    C.vocab, cp_grid) &&
+                  C.groups <= kCpPositions;
+    if (use_cp_pass) build_cp_pass();
   }
   {
     // HipCodecInitial::load (codec_hip.rs:214-336); optional here so the
@@ -1276,6 +1158,8 @@ Engine::~Engine() {
   if (bt.st_host) cudaFreeHost(bt.st_host);
   for (auto& ev : bt.ev)
     if (ev) cudaEventDestroy(ev);
+  for (auto& ev : cp_ev)
+    if (ev) cudaEventDestroy(ev);
   if (ev0) cudaEventDestroy(ev0);
   if (ev1) cudaEventDestroy(ev1);
   if (ev2) cudaEventDestroy(ev2);
@@ -1322,8 +1206,6 @@ void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* 
     if (fuse_attn_o && attn_o_fusable(da, o)) {
       if (&S == &cp) da.page0 = 0;  // the CodePredictor cache is one page (page 0)
       o.trace_id = trace_tag("attn+o+resid", c.hidden, S.q_out);
-      o.trigger = trigger_mode;
-      plan_prefetch(o, (size_t)c.hidden * S.q_out * sizeof(__nv_bfloat16));
       QCK(launch_attn_o(da, o, stream));  // attention inside the O projection's staging
       ++launches;
     } else {
@@ -1366,8 +1248,6 @@ void Engine::talker_head(int role, const float* x, const SampleCfg& c, float pen
   a.cp_prefix = cp_prefix_dst;
   a.token_out = token;
   a.lin.trace_id = trace_tag("talker head+select", T.vocab, T.hidden);
-  a.lin.trigger = trigger_mode;
-  plan_prefetch(a.lin, (size_t)T.vocab * T.hidden * sizeof(__nv_bfloat16));
   QCK(launch_head(a, stream));
   ++launches;
 }
@@ -1387,8 +1267,6 @@ void Engine::cp_head(int group, const float* x, const SampleCfg& c, const int* h
   a.trailing = trailing;
   a.tts_pad = tts_pad;
   a.lin.trace_id = trace_tag("cp head+select", C.vocab, C.hidden);
-  a.lin.trigger = trigger_mode;
-  plan_prefetch(a.lin, (size_t)C.vocab * C.hidden * sizeof(__nv_bfloat16));
   QCK(launch_head(a, stream));
   ++launches;
 }
@@ -1399,6 +1277,14 @@ void Engine::enqueue_frame(const SampleKey& k) {
   const int* halt = &st->halt;
   const StackCfg& C = cfg.cp;
   const int H = cfg.talker.hidden;
+  if (use_cp_pass) {
+    launch_cp(k);
+    if (!k.last) {
+      stack_step(talker, tb, tkv, &st->talker_pos, 0, halt);
+      talker_head(ROLE_TALKER_STEP, tb.x, k.t, k.penalty, halt, cp_prefix_target());
+    }
+    return;
+  }
   if (has_proj())
     linear(proj_w, cp_prefix, H, nullptr, 0.f, cb.x, C.hidden, nullptr, 0, proj_b, 2, C.hidden,
            H, EPI_BIAS, halt);
@@ -1417,207 +1303,173 @@ void Engine::enqueue_frame(const SampleKey& k) {
   }
 }
 
-// Static op list of one frame for the persistent frame kernel (same order and
-// semantics as enqueue_frame). Each reader records which op last wrote its
-// input so it can wait for that op's tag.
-std::vector<FrameOp> Engine::build_frame_ops(const SampleKey& k) {
-  std::vector<FrameOp> ops;
+// Op list of the persistent CodePredictor pass (the same sequence as the
+// CodePredictor part of enqueue_frame): built once per engine; the sampling
+// configuration travels in the launch parameters.
+void Engine::build_cp_pass() {
   const StackCfg& C = cfg.cp;
-  const StackCfg& T = cfg.talker;
-  const int H = T.hidden;
-  struct Src {
-    int src;
-    const float* ext;
-    const TV* tag;
-    int op;
-  };
-  auto gemv = [&](const __nv_bfloat16* W, Src x, int ldx, const float* gamma, float eps, TV* y,
-                  int ldy, Src r, int ldr, const float* bias, int M, int N, int K, int epi) {
-    FrameOp o{};
-    o.kind = FOP_GEMV;
-    o.epi = epi;
-    o.M = M; o.N = N; o.K = K;
-    o.x_src = x.src; o.x_ext = x.ext; o.x_tag = x.tag; o.x_op = x.op; o.ldx = ldx;
-    o.r_src = r.src; o.r_ext = r.ext; o.r_tag = r.tag; o.r_op = r.op; o.ldr = ldr;
-    o.W = W; o.gamma = gamma; o.eps = eps; o.bias = bias; o.y = y; o.ldy = ldy;
-    ops.push_back(o);
-    return (int)ops.size() - 1;
-  };
-  auto attn = [&](DevStack& S, const TagBufs& B, int qkv_op, int l, int kind, int pos, int nsplit) {
-    FrameOp o{};
-    o.kind = kind;
-    o.x_src = FSRC_TAG; o.x_tag = B.qkv; o.x_op = qkv_op;
-    o.y = B.attn;
-    o.q_gamma = S.q_g[l]; o.k_gamma = S.k_g[l]; o.eps = S.c.eps;
-    o.rope_cos = S.rope_cos; o.rope_sin = S.rope_sin;
-    o.kv = tkv; o.cp_cache = cp_cache_t; o.layer = l;
-    o.q_heads = S.c.q_heads; o.kv_heads = S.c.kv_heads;
-    o.pos_const = pos; o.nsplit = nsplit;
-    o.scale = 1.0f / std::sqrt((float)S.c.head_dim);
-    ops.push_back(o);
-    return (int)ops.size() - 1;
-  };
-  const Src none{FSRC_NONE, nullptr, nullptr, 0};
-  // one decoder layer; returns the index of the op that wrote B.x
-  auto layer = [&](DevStack& S, const TagBufs& B, int l, int M, Src x_in, Src r_in, int akind,
-                   int pos, int nsplit) {
-    const StackCfg& c = S.c;
-    const int q = gemv(S.wqkv[l], x_in, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, none, 0,
-                       nullptr, M, S.qkv_w, c.hidden, EPI_STORE);
-    const int a = attn(S, B, q, l, akind, pos, nsplit);
-    Src ain{nsplit > 1 ? FSRC_PARTIALS : FSRC_TAG, nullptr, B.attn, a};
-    const int o = gemv(S.wo[l], ain, S.q_out, nullptr, 0.f, B.h1, c.hidden, r_in, c.hidden,
-                       nullptr, M, c.hidden, S.q_out, EPI_RESID);
-    if (nsplit > 1) { ops[o].q_heads = c.q_heads; ops[o].nsplit = nsplit; }
-    const int g = gemv(S.wgu[l], Src{FSRC_TAG, nullptr, B.h1, o}, c.hidden, S.post_g[l], c.eps,
-                       B.act, c.intermediate, none, 0, nullptr, M, c.intermediate, c.hidden,
-                       EPI_SWIGLU);
-    return gemv(S.wdown[l], Src{FSRC_TAG, nullptr, B.act, g}, c.intermediate, nullptr, 0.f, B.x,
-                c.hidden, Src{FSRC_TAG, nullptr, B.h1, o}, c.hidden, nullptr, M, c.hidden,
-                c.intermediate, EPI_RESID);
-  };
-  auto add_head = [&](const __nv_bfloat16* W, Src x, const float* gamma, float eps, int V, int K,
-                      int role, const SampleCfg& sc, float penalty, int suppress, int group,
-                      const __nv_bfloat16* emb, TV* next_x) {
-    const int i = gemv(W, x, K, gamma, eps, logits_t, V, none, 0, nullptr, 1, V, K, EPI_STORE);
-    FrameOp& o = ops[i];
-    o.kind = FOP_HEAD;
-    o.role = role; o.cfg = sc; o.penalty = penalty; o.suppress = suppress;
-    o.group = group; o.last_group = C.groups - 2; o.emb = emb; o.next_x = next_x;
-    return i;
-  };
+  const int H = cfg.talker.hidden;
   const bool proj = has_proj();
-  const int Hc = C.hidden;
-  // CodePredictor 2-row prefill (positions 0, 1)
-  Src first{FSRC_EXT, cb.x, nullptr, 0}, first_r = first;
-  int wx = -1;
-  if (proj) {
-    wx = gemv(proj_w, Src{FSRC_EXT, cp_prefix, nullptr, 0}, H, nullptr, 0.f, ct.x, Hc, none, 0,
-              proj_b, 2, Hc, H, EPI_BIAS);
-    first = first_r = Src{FSRC_TAG, nullptr, ct.x, wx};
-  }
+  DevStack& S = cp;
+  StackBufs& B = cb;
+  std::vector<CpOp> ops;
+  auto name = [&](const std::string& n) { cp_op_names.push_back(n); };
+  auto gemv = [&](const __nv_bfloat16* W, int N, int K, int M, int epi, const float* gamma,
+                  int x_src, const float* x, int ldx, float* y, int ldy, int wait) {
+    CpOp o{};
+    o.kind = CPOP_GEMV;
+    o.epi = epi;
+    o.M = M;
+    o.N = N;
+    o.K = K;
+    o.W = W;
+    o.gamma = gamma;
+    o.eps = C.eps;
+    o.x_src = x_src;
+    o.x = x;
+    o.ldx = ldx;
+    o.y = y;
+    o.ldy = ldy;
+    o.wait = wait;
+    return o;
+  };
+  // One decoder layer on M rows at positions pos0.. whose input (and residual)
+  // is `in_src` / `in`.
+  auto layer = [&](int l, int M, int pos0, int in_src, const float* in, int ld_in, int wait_qkv,
+                   const std::string& tag) {
+    ops.push_back(gemv(S.wqkv[l], S.qkv_w, C.hidden, M, EPI_STORE, S.in_g[l], in_src, in, ld_in,
+                       B.qkv, S.qkv_w, wait_qkv));
+    name(tag + " qkv");
+    CpOp o = gemv(S.wo[l], C.hidden, S.q_out, M, EPI_RESID, nullptr, CPSRC_GLOBAL, nullptr, 0,
+                  B.h1, C.hidden, 1);
+    o.kind = CPOP_ATTN_O;
+    o.r_src = in_src;
+    o.resid = in;
+    o.ldr = ld_in;
+    o.qkv = B.qkv;
+    o.ld_qkv = S.qkv_w;
+    o.q_gamma = S.q_g[l];
+    o.k_gamma = S.k_g[l];
+    o.layer = l;
+    o.pos0 = pos0;
+    ops.push_back(o);
+    name(tag + " attn+o");
+    ops.push_back(gemv(S.wgu[l], C.intermediate, C.hidden, M, EPI_SWIGLU, S.post_g[l],
+                       CPSRC_GLOBAL, B.h1, C.hidden, B.act, C.intermediate, 1));
+    name(tag + " gate|up");
+    CpOp d = gemv(S.wdown[l], C.hidden, C.intermediate, M, EPI_RESID, nullptr, CPSRC_GLOBAL,
+                  B.act, C.intermediate, B.x, C.hidden, 1);
+    d.r_src = CPSRC_GLOBAL;
+    d.resid = B.h1;
+    d.ldr = C.hidden;
+    ops.push_back(d);
+    name(tag + " down");
+  };
+  auto head = [&](int g, const float* x) {
+    CpOp o = gemv(cp_heads + (size_t)g * C.vocab * C.hidden, C.vocab, C.hidden, 1, EPI_STORE,
+                  cp_norm_g, CPSRC_GLOBAL, x, C.hidden, logits, C.vocab, 1);
+    o.kind = CPOP_HEAD;
+    o.group = g;
+    ops.push_back(o);
+    name("head " + std::to_string(g));
+  };
+  auto projection = [&](int M, int x_src, const float* x) {
+    CpOp o = gemv(proj_w, C.hidden, H, M, EPI_BIAS, nullptr, x_src, x, H, B.x, C.hidden, 0);
+    o.bias = proj_b;
+    ops.push_back(o);
+    name("projection");
+  };
+  // 2-row prefill at positions 0, 1 (code_predictor.rs:366-392)
+  // The talker head leaves the two prefix rows in cp_prefix_target(): the
+  // projection's input for 1.7B, else the CodePredictor's input rows B.x.
+  if (proj) projection(2, CPSRC_GLOBAL, cp_prefix);
   for (int l = 0; l < C.layers; ++l) {
-    const Src xin = l == 0 ? first : Src{FSRC_TAG, nullptr, ct.x, wx};
-    const Src rin = l == 0 ? first_r : Src{FSRC_TAG, nullptr, ct.x, wx};
-    wx = layer(cp, ct, l, 2, xin, rin, FOP_ATTN_PAIR, 0, 1);
+    const bool first = l == 0 && !proj;  // rows written before the launch: no wait
+    layer(l, 2, 0, CPSRC_GLOBAL, B.x, C.hidden, first ? 0 : 1, "prefill L" + std::to_string(l));
   }
-  TV* cp_next = proj ? cp_dummy_t : ct.x;
-  int wh = add_head(cp_heads, Src{FSRC_TAG, nullptr, ct.x + Hc, wx}, cp_norm_g, C.eps, C.vocab,
-                    Hc, ROLE_CP_GROUP, k.s, 1.0f, 0, 0, cp_embs,
-                    C.groups - 2 == 0 ? tt.x : cp_next);
+  head(0, B.x + C.hidden);
+  // groups 1..14 at position g + 1 (code_predictor.rs:393-471)
   for (int g = 1; g < C.groups - 1; ++g) {
-    if (proj) {
-      wx = gemv(proj_w, Src{FSRC_LOCAL, nullptr, nullptr, 0}, H, nullptr, 0.f, ct.x, Hc, none, 0,
-                proj_b, 1, Hc, H, EPI_BIAS);
-      first = first_r = Src{FSRC_TAG, nullptr, ct.x, wx};
-    } else {
-      first = Src{FSRC_LOCAL, nullptr, nullptr, 0};
-      first_r = Src{FSRC_TAG, nullptr, ct.x, wh};
-    }
+    if (proj) projection(1, CPSRC_LOCAL, nullptr);
     for (int l = 0; l < C.layers; ++l) {
-      const Src xin = l == 0 ? first : Src{FSRC_TAG, nullptr, ct.x, wx};
-      const Src rin = l == 0 ? first_r : Src{FSRC_TAG, nullptr, ct.x, wx};
-      wx = layer(cp, ct, l, 1, xin, rin, FOP_ATTN_DECODE, g + 1, 1);
+      const bool local = l == 0 && !proj;
+      layer(l, 1, g + 1, local ? CPSRC_LOCAL : CPSRC_GLOBAL, local ? nullptr : B.x, C.hidden,
+            local ? 0 : 1, "g" + std::to_string(g) + " L" + std::to_string(l));
     }
-    wh = add_head(cp_heads + (size_t)g * C.vocab * Hc, Src{FSRC_TAG, nullptr, ct.x, wx},
-                  cp_norm_g, C.eps, C.vocab, Hc, ROLE_CP_GROUP, k.s, 1.0f, 0, g,
-                  cp_embs + (size_t)g * C.vocab * H, g == C.groups - 2 ? tt.x : cp_next);
+    head(g, B.x);
   }
-  if (!k.last) {
-    int wt = wh;  // the last CodePredictor head wrote the talker input slices
-    for (int l = 0; l < T.layers; ++l) {
-      const Src xin = l == 0 ? Src{FSRC_LOCAL, nullptr, nullptr, 0} : Src{FSRC_TAG, nullptr, tt.x, wt};
-      wt = layer(talker, tt, l, 1, xin, Src{FSRC_TAG, nullptr, tt.x, wt}, FOP_ATTN_DECODE, -1,
-                 kFrameTalkerSplits);
-    }
-    add_head(head, Src{FSRC_TAG, nullptr, tt.x, wt}, norm_g, T.eps, T.vocab, T.hidden,
-             ROLE_TALKER_STEP, k.t, k.penalty, 1, 0, codec_emb, nullptr);
+  // The ring is refilled between ops, so every op's rows must fit in it at
+  // once; the op list must fit the shared-memory weight table.
+  bool fits = ops.size() <= (size_t)kCpMaxOps;
+  for (const CpOp& o : ops) {
+    const int rows = (o.N + cp_grid - 1) / cp_grid;
+    const int rps = kCpStageBytes / (2 * o.K);
+    const int pieces = (o.epi == EPI_SWIGLU ? 2 : 1) * ((rows + rps - 1) / rps);
+    if (rps < 1 || pieces > kCpStages) fits = false;
   }
-  for (FrameOp& o : ops)
-    o.writers = (o.kind == FOP_GEMV || o.kind == FOP_HEAD) ? frame_grid : o.q_heads * o.nsplit;
-  return ops;
+  if (!fits) {
+    use_cp_pass = false;
+    cp_op_names.clear();
+    return;
+  }
+  std::vector<CpLoad> loads(ops.size());
+  for (size_t i = 0; i < ops.size(); ++i)
+    loads[i] = CpLoad{ops[i].W, ops[i].N, (short)ops[i].K,
+                      (short)(ops[i].epi == EPI_SWIGLU ? 2 : 1)};
+  cp_loads = arena.alloc<CpLoad>(loads.size());
+  QCK(cudaMemcpy(cp_loads, loads.data(), loads.size() * sizeof(CpLoad), cudaMemcpyHostToDevice));
+  cp_n_ops = (int)ops.size();
+  cp_weight_bytes = 0.0;
+  for (const CpOp& o : ops)
+    cp_weight_bytes += 2.0 * o.K * (double)o.N * (o.epi == EPI_SWIGLU ? 2 : 1);
+  for (auto& ev : cp_ev) QCK(cudaEventCreate(&ev));
+  cp_ops = arena.alloc<CpOp>(ops.size());
+  QCK(cudaMemcpy(cp_ops, ops.data(), ops.size() * sizeof(CpOp), cudaMemcpyHostToDevice));
+  cp_counter = arena.alloc<unsigned long long>(1);
+  cp_err = arena.alloc<int>(2);
+  QCK(cudaMemset(cp_counter, 0, sizeof(unsigned long long)));
+  QCK(cudaMemset(cp_err, 0, 2 * sizeof(int)));
+  if (step_trace) cp_trace = arena.alloc<unsigned long long>(kCpTraceSlots * ops.size());
 }
 
-// Per-CTA limits of the frame kernel (rows per CTA, shared-memory scratch).
-bool Engine::frame_ops_fit(const std::vector<FrameOp>& ops) const {
-  const int G = frame_grid;
-  if (G <= 0) return false;
-  for (const FrameOp& o : ops) {
-    if (o.kind == FOP_GEMV || o.kind == FOP_HEAD) {
-      const int rows = (o.N + G - 1) / G;
-      if (o.N < G || rows * o.M > 256 || o.K > 6144 || o.K % 256 != 0 || o.M > 2) return false;
-      const size_t floats = (size_t)o.M * o.K + (size_t)rows * (o.epi == EPI_SWIGLU ? 2 : 1) * 16;
-      if (floats * 4 > (size_t)kFrameScratchBytes) return false;
-      if (o.kind == FOP_HEAD && o.N > max_sample_vocab()) return false;
-      if (o.x_src == FSRC_PARTIALS && (o.nsplit > 4 || o.q_heads * o.nsplit > 128)) return false;
-    } else if (o.q_heads * o.nsplit > G) {
-      return false;
-    }
-  }
-  if (ops.size() > 8192) return false;
-  return cfg.talker.hidden <= kFrameMaxH && cfg.cp.groups <= kFrameCpPositions;
-}
-
-void Engine::enqueue_frame_kernel(const SampleKey& k) {
-  const auto& ol = frame_ops.at(k);
-  FrameParams p{};
-  p.ops = ol.first;
-  p.n_ops = ol.second;
+void Engine::launch_cp(const SampleKey& k, float* dbg_logits, float* emb_sum_out) {
+  const StackCfg& C = cfg.cp;
+  CpPassParams p{};
+  p.ops = cp_ops;
+  p.loads = cp_loads;
+  p.n_ops = cp_n_ops;
+  p.counter = cp_counter;
+  p.error = cp_err;
   p.st = st;
-  p.seq = frame_seq;
-  p.error = frame_error;
-  p.counters = frame_counters;
-  {
-    const char* env = std::getenv("QTTS_FRAME_COUNTERS");
-    p.use_counters = env ? std::atoi(env) : 1;
-  }
-  p.talker_codec_emb = codec_emb;
+  p.q_heads = C.q_heads;
+  p.kv_heads = C.kv_heads;
+  p.scale = 1.0f / std::sqrt((float)C.head_dim);
+  p.rope_cos = cp.rope_cos;
+  p.rope_sin = cp.rope_sin;
+  p.cache = ckv.pool;  // page 0: [layer][K|V][kv_head][16][128]
   p.H = cfg.talker.hidden;
-  p.groups = cfg.cp.groups;
-  p.eos_token = cfg.codec_eos;
+  p.groups = C.groups;
+  p.vocab = C.vocab;
+  p.cp_embs = cp_embs;
+  p.cfg = k.s;
   p.codes = codes;
   p.history = history;
+  p.talker_codec_emb = codec_emb;
   p.trailing = trailing;
   p.tts_pad = tts_pad;
-  p.cp_prefix = cp_prefix_target();
-  p.trace = frame_trace;
-  p.trace_cta = 0;
-  p.trace_frame = 5;
-  QCK(launch_frame(p, frame_grid, stream));
-  launches += 1;
-}
-
-void Engine::check_frame_error() {
-  if (!use_frame_kernel) return;
-  int err[2] = {0, 0};
-  QCK(cudaMemcpy(err, frame_error, sizeof err, cudaMemcpyDeviceToHost));
-  if (err[0])
-    fail(QTTS_ERR_DEVICE_STATE, "frame kernel wait timed out (code " + std::to_string(err[0]) +
-                                    ", op " + std::to_string(err[1]) + ")");
-}
-
-void Engine::dump_frame_trace(const SampleKey& k) {
-  if (!frame_trace || !frame_ops.count(k)) return;
-  const auto& ol = frame_ops.at(k);
-  std::vector<long long> tr(8 * (size_t)ol.second + 128);
-  std::vector<FrameOp> ops(ol.second);
-  QCK(cudaMemcpy(tr.data(), frame_trace, tr.size() * 8, cudaMemcpyDeviceToHost));
-  QCK(cudaMemcpy(ops.data(), ol.first, ops.size() * sizeof(FrameOp), cudaMemcpyDeviceToHost));
-  if (FILE* f = std::fopen(frame_trace_path.c_str(), "w")) {
-    for (size_t i = 0; i < ops.size(); ++i)
-      std::fprintf(f, "%d %d %d %d %d %lld %lld %lld %lld %lld\n", ops[i].kind, ops[i].epi,
-                   ops[i].M, ops[i].N, ops[i].K, tr[8 * i], tr[8 * i + 1], tr[8 * i + 2],
-                   tr[8 * i + 3], tr[8 * i + 4] + 0 * tr[8 * i + 5]);
-    for (size_t i = 0; i < ops.size(); ++i)
-      std::fprintf(f, "#w %zu %lld %lld %lld\n", i, tr[8 * i + 5], tr[8 * i + 6], tr[8 * i + 7]);
-    for (int h = 0; h < 32; ++h) {
-      const long long* t = tr.data() + 8 * ops.size() + 4 * h;
-      if (t[0] && t[3] > t[0])
-        std::fprintf(f, "# head %d gemv->logits %lld select %lld actions %lld\n", h, t[1] - t[0],
-                     t[2] - t[1], t[3] - t[2]);
-    }
-    std::fclose(f);
-  }
+  p.step_in = tb.x;
+  p.trace = trace_capture ? cp_trace : nullptr;
+  p.dbg_logits = dbg_logits;
+  p.emb_sum_out = emb_sum_out;
+  // inside a captured frame graph the events must be external record nodes
+  // (a plain record under capture only orders work and keeps no time)
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  QCK(cudaStreamIsCapturing(stream, &cs));
+  const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
+  QCK(cudaEventRecordWithFlags(cp_ev[0], stream, flags));
+  QCK(launch_cp_pass(p, cp_grid, stream));
+  QCK(cudaEventRecordWithFlags(cp_ev[1], stream, flags));
+  ++launches;
 }
 
 cudaGraphExec_t Engine::frame_graph(const SampleKey& k) {
@@ -1625,42 +1477,19 @@ cudaGraphExec_t Engine::frame_graph(const SampleKey& k) {
   if (it != graphs.end()) return it->second;
   cudaGraph_t g = nullptr;
   const size_t before = launches;
-  bool fk = use_frame_kernel;
-  if (fk && !frame_ops.count(k)) {
-    std::vector<FrameOp> ops = build_frame_ops(k);
-    if (frame_ops_fit(ops)) {
-      FrameOp* d = arena.alloc<FrameOp>(ops.size());
-      QCK(cudaMemcpy(d, ops.data(), ops.size() * sizeof(FrameOp), cudaMemcpyHostToDevice));
-      frame_ops[k] = {d, (int)ops.size()};
-    } else {
-      fk = use_frame_kernel = false;
-    }
-  }
-  const bool pf = !fk && pf_ahead > 0;
-  trace_capture = step_trace != nullptr && !fk && !k.last;
+  trace_capture = step_trace != nullptr && !k.last;
   if (trace_capture) trace_names.clear();
-  for (int pass = pf ? 1 : 2; pass <= 2; ++pass) {
-    pf_mode = pf ? pass : 0;
-    if (pass == 1) pf_ops.clear();
-    pf_next = 0;
+  QCK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    enqueue_frame(k);
+  } catch (...) {
+    cudaStreamEndCapture(stream, &g);
+    if (g) cudaGraphDestroy(g);
     launches = before;
-    QCK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
-    try {
-      if (fk) enqueue_frame_kernel(k); else enqueue_frame(k);
-    } catch (...) {
-      cudaStreamEndCapture(stream, &g);
-      if (g) cudaGraphDestroy(g);
-      launches = before;
-      pf_mode = 0;
-      throw;
-    }
-    QCK(cudaStreamEndCapture(stream, &g));
-    if (pass == 1) {
-      cudaGraphDestroy(g);
-      g = nullptr;
-    }
+    trace_capture = false;
+    throw;
   }
-  pf_mode = 0;
+  QCK(cudaStreamEndCapture(stream, &g));
   trace_capture = false;
   graph_nodes[k] = launches - before;
   launches = before;
@@ -1779,6 +1608,10 @@ void Engine::begin(int P, int n_trailing, const qtts_generate_options& o) {
   s.rng_seed = o.seed;
   *st_host = s;
   QCK(cudaMemcpyAsync(st, st_host, sizeof(SeqState), cudaMemcpyHostToDevice, stream));
+  if (cp_counter) {
+    QCK(cudaMemsetAsync(cp_counter, 0, sizeof(unsigned long long), stream));
+    QCK(cudaMemsetAsync(cp_err, 0, 2 * sizeof(int), stream));
+  }
   QCK(cudaEventRecord(ev0, stream));
   const size_t l0 = launches;
   stack_rows(talker, tb, tkv, P, 0, nullptr);
@@ -1804,10 +1637,13 @@ void Engine::sync_state() {
   stream_sync();
   if (st_host->error)
     fail(QTTS_ERR_DEVICE_STATE, "cannot sample from logits with no finite values");
-  if (mlp_err) {
-    int e = 0;
-    QCK(cudaMemcpy(&e, mlp_err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (e) fail(QTTS_ERR_DEVICE_STATE, "fused MLP weight copies timed out");
+  if (cp_err) {
+    int e[2] = {0, 0};
+    QCK(cudaMemcpy(e, cp_err, sizeof e, cudaMemcpyDeviceToHost));
+    if (e[0])
+      fail(QTTS_ERR_DEVICE_STATE, "CodePredictor pass stopped: a bounded device wait ran out "
+                                  "(code " + std::to_string(e[0]) + ", op " +
+                                  std::to_string(e[1]) + ")");
   }
   if (tc_err) {
     int e = 0;
@@ -1849,8 +1685,7 @@ size_t Engine::run_frames(size_t n) {
   }
   QCK(cudaEventRecord(ev2, stream));
   sync_state();
-  check_frame_error();
-  if (gf) dump_frame_trace(full);
+  if (use_cp_pass) QCK(cudaEventElapsedTime(&last_cp_ms, cp_ev[0], cp_ev[1]));
   if (traced) dump_step_trace();
   float ms = 0.f;
   QCK(cudaEventElapsedTime(&ms, ev1, ev2));
@@ -1882,6 +1717,25 @@ void Engine::dump_step_trace() {
                  t[7 * kTraceCap + i], trace_names[i - 1].c_str());
   }
   std::fclose(f);
+  if (!cp_trace) return;
+  // the persistent CodePredictor pass: per op, CTA 0's stamps (kCpTraceSlots)
+  std::vector<unsigned long long> c((size_t)kCpTraceSlots * cp_n_ops);
+  QCK(cudaMemcpy(c.data(), cp_trace, c.size() * sizeof(unsigned long long),
+                 cudaMemcpyDeviceToHost));
+  FILE* g = std::fopen((step_trace_path + ".cp").c_str(), "w");
+  if (!g) return;
+  std::fprintf(g, "# op wait staged first_stage rows stored arrived sel0 sel1 (ns after op 0's "
+                  "wait; sel only for heads) name\n");
+  const unsigned long long c0 = c[0];
+  for (int i = 0; i < cp_n_ops; ++i) {
+    std::fprintf(g, "%d", i);
+    for (int k = 0; k < kCpTraceSlots; ++k) {
+      const unsigned long long v = c[(size_t)kCpTraceSlots * i + k];
+      std::fprintf(g, " %lld", v >= c0 && v - c0 < (1ull << 40) ? (long long)(v - c0) : -1LL);
+    }
+    std::fprintf(g, " %s\n", cp_op_names[i].c_str());
+  }
+  std::fclose(g);
 }
 
 // ---- batched serving -------------------------------------------------------
@@ -2412,8 +2266,8 @@ int32_t qtts_engine_get_info(const qtts_engine* h, qtts_engine_info* out) {
     out->codec_eos = e.cfg.codec_eos;
     out->max_cache_steps = e.max_cache_steps;
     out->device_bytes = e.arena.bytes() + (e.codec ? e.codec->device_bytes() : 0);
-    out->fused_mlp_cluster[0] = e.mlp_cluster[0];
-    out->fused_mlp_cluster[1] = e.mlp_cluster[1];
+    out->cp_pass_grid = e.use_cp_pass ? e.cp_grid : 0;
+    out->reserved = 0;
     out->has_codec = e.codec ? 1 : 0;
     out->samples_per_frame = qtts::Codec::samples_per_frame();
   });
@@ -2900,6 +2754,26 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
     *e.st_host = s;
     e.h2d(e.st, e.st_host, sizeof(s));
     const qtts::SampleCfg sc = qtts::sub_cfg(opt);
+    const int na = C.groups - 1;
+    if (e.use_cp_pass) {
+      // the persistent pass the frame graph runs, with every head's logits
+      // and the embedding sum copied out for parity checks
+      QCK(cudaMemsetAsync(e.cp_counter, 0, sizeof(unsigned long long), e.stream));
+      QCK(cudaMemsetAsync(e.cp_err, 0, 2 * sizeof(int), e.stream));
+      const qtts::SampleKey k{qtts::talker_cfg(opt), sc, 1.0f, 1};
+      e.launch_cp(k, e.dbg_logits, e.emb_sum);
+      e.sync_state();
+      std::vector<int32_t> row(C.groups);
+      e.read_codes(0, 1, row.data());
+      if (tokens_out) std::memcpy(tokens_out, row.data() + 1, na * 4);
+      if (emb_sum_out) QCK(cudaMemcpy(emb_sum_out, e.emb_sum, H * 4, cudaMemcpyDeviceToHost));
+      if (logits_out)
+        QCK(cudaMemcpy(logits_out, e.dbg_logits, (size_t)na * C.vocab * 4,
+                       cudaMemcpyDeviceToHost));
+      e.seq_ended = true;
+      ++e.seq_id;
+      return;
+    }
     // Eager CodePredictor pass with per-group logits kept for parity checks.
     if (e.has_proj())
       e.linear(e.proj_w, e.cp_prefix, H, nullptr, 0.f, e.cb.x, C.hidden, nullptr, 0, e.proj_b, 2,
@@ -2917,7 +2791,6 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
                                 cudaMemcpyDeviceToDevice, e.stream));
     }
     e.sync_state();
-    const int na = C.groups - 1;
     std::vector<int32_t> row(C.groups);
     e.read_codes(0, 1, row.data());
     if (tokens_out) std::memcpy(tokens_out, row.data() + 1, na * 4);
@@ -2926,6 +2799,41 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
       QCK(cudaMemcpy(logits_out, e.dbg_logits, (size_t)na * C.vocab * 4, cudaMemcpyDeviceToHost));
     e.seq_ended = true;  // the talker state was not advanced: no stream may continue
     ++e.seq_id;
+  });
+}
+
+int32_t qtts_last_cp_pass_timing(const qtts_engine* h, float* ms, double* weight_bytes) {
+  return guard([&] {
+    need(h, "engine");
+    const Engine& e = *h->e;
+    if (!e.use_cp_pass) qtts::fail(QTTS_ERR_UNSUPPORTED, "the persistent CodePredictor pass is off");
+    if (ms) *ms = e.last_cp_ms;
+    if (weight_bytes) *weight_bytes = e.cp_weight_bytes;
+  });
+}
+
+int32_t qtts_selftest_device_wait(qtts_engine* h, uint32_t limit_us) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    if (limit_us == 0 || limit_us > 5000000u) qtts::invalid("limit_us must be in (0, 5e6]");
+    // a private counter nobody increments, and the wait's status word
+    if (!e.selftest_ctr) {
+      e.selftest_ctr = e.arena.alloc<unsigned long long>(1);
+      e.selftest_status = e.arena.alloc<int>(1);
+    }
+    unsigned long long* ctr = e.selftest_ctr;
+    int* status = e.selftest_status;
+    QCK(cudaMemsetAsync(ctr, 0, sizeof(unsigned long long), e.stream));
+    QCK(cudaMemsetAsync(status, 0xff, sizeof(int), e.stream));
+    QCK(qtts::launch_wait_selftest(ctr, 1ull, (unsigned long long)limit_us * 1000ull, status,
+                                   e.stream));
+    int st = -1;
+    QCK(cudaMemcpyAsync(&st, status, sizeof(int), cudaMemcpyDeviceToHost, e.stream));
+    e.stream_sync();
+    if (st == 1)
+      qtts::fail(QTTS_ERR_DEVICE_STATE, "a bounded device wait ran out after " +
+                                            std::to_string(limit_us) + " us");
+    if (st != 0) qtts::fail(QTTS_ERR_CUDA, "wait self-test did not report");
   });
 }
 

@@ -70,31 +70,6 @@ __device__ __forceinline__ void trace_dur(int id, int slot, unsigned long long t
   atomicMax(t.buf + slot * t.cap + id, trace_clock(id) - t0);
 }
 
-// This CTA's share of the op's L2 prefetch ranges (warp 0, 4 KB per bulk
-// prefetch; fire-and-forget, so it never delays the kernel).
-__device__ __forceinline__ void l2_prefetch_share(const LinearArgs& a, int cta, int ncta) {
-  const unsigned tot = a.pf_bytes[0] + a.pf_bytes[1] + a.pf_bytes[2];
-  if (tot == 0u || threadIdx.x >= 32) return;
-  const unsigned chunk = ((tot + ncta - 1) / ncta + 15u) & ~15u;
-  const unsigned b = (unsigned)cta * chunk;
-  const unsigned e = min(tot, b + chunk);
-  for (unsigned o = b + threadIdx.x * 4096u; o < e; o += 32u * 4096u) {
-    unsigned n = min(4096u, e - o), at = o, base = 0;
-#pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      const unsigned len = a.pf_bytes[i];
-      if (n && at < base + len) {
-        const unsigned take = min(n, base + len - at);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
-                     :: "l"(a.pf_ptr[i] + (at - base)), "r"(take) : "memory");
-        at += take;
-        n -= take;
-      }
-      base += len;
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Projection body: for the block's M-tile and RPW output columns per warp,
 //   acc = W[row] . (gamma * x[m])   then  y = epilogue(inv_rms[m] * acc)
@@ -110,7 +85,6 @@ __device__ __forceinline__ bool linear_body(const LinearArgs& a, float* sx, floa
   const int m0 = blockIdx.y * MT;
   const int K = a.K;
   trace_mark(a.trace_id, 0);
-  if (blockIdx.y == 0) l2_prefetch_share(a, blockIdx.x, gridDim.x);
 
   const __nv_bfloat16* wr[NR];
   bool valid[RPW];
@@ -268,12 +242,14 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
 #pragma unroll
     for (int j = 0; j < KCH; ++j) w[r][j] = ldg_stream(src + j * 256, pol);
   }
-  l2_prefetch_share(a, blockIdx.x, gridDim.x);
-  if (a.trigger == 0) pdl_trigger();
   pdl_wait();
   trace_mark(a.trace_id, 1);
   const unsigned long long tw = trace_clock(a.trace_id);
-  if (a.trigger == 1) pdl_trigger();
+  // Dependents launch once this kernel is past its wait: their weight loads
+  // then overlap this kernel's staging and compute (measured faster than
+  // launching them at entry, which floods the memory queues with several
+  // kernels' weights at once, or after staging).
+  pdl_trigger();
   // The halt flag is loaded alongside the input (not before it) and only
   // checked before the first write.
   const int halted = a.halt ? __ldcg(a.halt) : 0;
@@ -313,7 +289,6 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
   }
   if (halted) return false;
   if (inv_out && threadIdx.x == 0) *inv_out = sc[0];
-  if (a.trigger == 2) pdl_trigger();
   trace_mark(a.trace_id, 4);
   float acc[MR][NR];
 #pragma unroll
@@ -1233,4 +1208,3 @@ cudaError_t launch_assemble_rows(const float* proj, const int* proj_index,
 
 }  // namespace qtts
 
-#include "mlp.cuh"

@@ -33,15 +33,7 @@ struct LinearArgs {
   const float* bias;       // EPI_BIAS* [N]
   int M, N, K;
   const int* halt;         // optional: kernel is a no-op while *halt != 0
-  // Optional L2 prefetch of up to three byte ranges (16-byte aligned, sizes
-  // multiples of 16), shared out over the grid before the dependency wait:
-  // the weights of ops further down the frame, so HBM streams ahead of the
-  // dependency chain.
-  const char* pf_ptr[3];
-  unsigned pf_bytes[3];
   int trace_id;            // > 0: record entry / dependency-wait / exit times (step trace)
-  int trigger;             // decode GEMV: 0 = launch dependents at entry, 1 = after the
-                           // wait, 2 = after staging the input, 3 = at exit
 };
 
 // Sampling parameters of one token kind (talker or subtalker).
@@ -172,40 +164,7 @@ struct AttnPrefillArgs {
   const int* halt;
 };
 
-// Fused decode MLP (gate|up GEMV, SwiGLU, down GEMV + residual in one
-// kernel): kMlpCtas CTAs in clusters of 8, 4 or 2, CTA j owning intermediate
-// channels [j*I/kMlpCtas, (j+1)*I/kMlpCtas).
-constexpr int kMlpCtas = 128;
-constexpr int kMlpMaxCluster = 8;
-constexpr size_t kMlpMaxSmem = 200 * 1024;
-
-struct MlpArgs {
-  const __nv_bfloat16* Wgu;  // [2I, H]: gate rows then up rows
-  const __nv_bfloat16* WdT;  // [I, H]: down_proj.weight transposed
-  const float* x;            // [H] residual input r (normalised inside)
-  const float* gamma;        // [H] post-attention RMSNorm gamma
-  float eps;
-  float* y;                  // [H] r + down(silu(gate) * up); must not alias x
-  float* ws;                 // [kMlpCtas / cluster, H] cluster partial sums
-  unsigned* tickets;         // [cluster] zero-initialised, reset by the kernel
-  int H, I;
-  const int* halt;
-  int* err;                  // set to 7 if the weight copies never land
-  int trace_id;
-  int trigger;
-  int cluster;               // CTAs per cluster: 8, 4 or 2
-};
-
 cudaError_t launch_linear(const LinearArgs& a, Epilogue epi, cudaStream_t stream);
-bool mlp_fused_supported(int H, int I);
-size_t mlp_fused_smem(int H, int I);
-// Sets the shared-memory limit of the kernel for this shape and cluster size;
-// reports how many such clusters can be resident at once.
-cudaError_t configure_mlp_fused(int H, int I, int cluster, int* active_clusters);
-cudaError_t launch_mlp_fused(const MlpArgs& a, cudaStream_t stream);
-// dst[c, r] = src[r, c] of a [rows x cols] bf16 matrix.
-cudaError_t launch_transpose_bf16(const __nv_bfloat16* src, int rows, int cols,
-                                  __nv_bfloat16* dst, cudaStream_t stream);
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t stream);
 // CodePredictor decode attention fused into the O projection (o.x unused,
 // o.resid = residual); only for a fixed position below 16 and two q heads per

@@ -125,6 +125,172 @@ struct Selector {
     Sync::sync();
   }
 
+  // Device-path sampling for 0 < K <= kFastK: the same selection as the
+  // general path below, with fewer block barriers. The K-th largest key is
+  // found by an MSB-first radix select over 4-bit digits: each thread counts
+  // its keys per digit in packed 8-bit fields of two registers (no shared
+  // atomics), warps reduce them with __reduce_add_sync, and one barrier per
+  // digit publishes the eight warp counts, from which every warp derives the
+  // same bucket. Once at most kFastCand keys lie at or above the bucket they
+  // are compacted with ballots, ranked exactly (value descending, index
+  // ascending), and thread 0 sums their probabilities and walks the inverse
+  // CDF in rank order. Returns -1 (uniformly) when more than kFastCand keys
+  // tie at the threshold; the caller then runs the general path.
+  static constexpr int kFastK = 64;
+  static constexpr int kFastCand = 128;
+  __device__ __forceinline__ int select_fast(int V, const SampleCfg& cfg, float u) {
+    __shared__ unsigned s_wc[2][kSelThreads / 32][16];
+    __shared__ int s_wn[kSelThreads / 32];
+    __shared__ __align__(16) unsigned long long s_cand[kFastCand];
+    __shared__ float s_val[kFastK];
+    __shared__ int s_idx[kFastK];
+    __shared__ __align__(16) float s_prob[kFastK];
+    __shared__ int s_res, s_cnt;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int kPer = kSelMaxVocab / kSelThreads;
+    const int K = min(cfg.top_k, V);
+    unsigned key[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int v = j * kSelThreads + tid;
+      unsigned k = 0u;  // 0: no entry (no float maps to 0)
+      if (v < V) {
+        float x = val[v];
+        if (!isfinite(x)) {  // the device path ranks non-finite logits as -FLT_MAX
+          x = -FLT_MAX;
+          val[v] = x;
+        }
+        k = order_key(x);
+      }
+      key[j] = k;
+    }
+    unsigned prefix = 0u, mask = 0u, lower = 0u;
+    int above = 0, rem = K, buf = 0;
+    bool done = false;
+    for (int shift = 28; shift >= 0; shift -= 4) {
+      unsigned long long c_lo = 0ull, c_hi = 0ull;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const unsigned k = key[j];
+        if (k != 0u && (k & mask) == prefix) {
+          const unsigned d = (k >> shift) & 15u;
+          if (d < 8u) c_lo += 1ull << (8u * d);
+          else c_hi += 1ull << (8u * (d - 8u));
+        }
+      }
+      unsigned mine = 0u;
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        const unsigned c = (unsigned)((d < 8 ? c_lo >> (8 * d) : c_hi >> (8 * (d - 8))) & 255ull);
+        const unsigned w = __reduce_add_sync(0xffffffffu, c);
+        if (lane == d) mine = w;
+      }
+      if (lane < 16) s_wc[buf][warp][lane] = mine;
+      Sync::sync();
+      // every warp derives the bucket: lane d < 16 holds digit d's total
+      unsigned tot = 0u;
+      if (lane < 16)
+#pragma unroll
+        for (int w = 0; w < kSelThreads / 32; ++w) tot += s_wc[buf][w][lane];
+      unsigned incl = tot;  // keys in digits >= lane
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) {
+        const unsigned n = __shfl_down_sync(0xffffffffu, incl, o);
+        if (lane + o < 16) incl += n;
+      }
+      const unsigned excl = incl - tot;  // keys in digits > lane
+      const bool hit = lane < 16 && (int)excl < rem && (int)incl >= rem;
+      const int digit = __ffs(__ballot_sync(0xffffffffu, hit)) - 1;
+      const int ex = (int)__shfl_sync(0xffffffffu, excl, digit);
+      const int in_bucket = (int)__shfl_sync(0xffffffffu, tot, digit);
+      prefix |= (unsigned)digit << shift;
+      mask |= 15u << shift;
+      above += ex;
+      rem -= ex;
+      buf ^= 1;
+      if (above + in_bucket <= kFastCand) {
+        lower = prefix;
+        done = true;
+        break;
+      }
+    }
+    if (!done) return -1;  // more than kFastCand keys equal the threshold (uniform)
+    // compaction: keys at or above `lower`, per-warp ballots, warp order
+    auto take = [&](unsigned k) { return k != 0u && k >= lower; };
+    int wc = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) wc += __popc(__ballot_sync(0xffffffffu, take(key[j])));
+    if (lane == 0) s_wn[warp] = wc;
+    Sync::sync();
+    int base = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < kSelThreads / 32; ++w) {
+      const int c = s_wn[w];
+      base += w < warp ? c : 0;
+      total += c;
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const bool t = take(key[j]);
+      const unsigned bal = __ballot_sync(0xffffffffu, t);
+      if (t)
+        s_cand[base + __popc(bal & ((1u << lane) - 1u))] =
+            ((unsigned long long)key[j] << 32) |
+            (unsigned)(0xffffffffu - (unsigned)(j * kSelThreads + tid));
+      base += __popc(bal);
+    }
+    Sync::sync();
+    // exact rank of each candidate: larger key first, then lower index
+    if (tid < total) {
+      const unsigned long long me = s_cand[tid];
+      int rank = 0;
+      for (int i = 0; i < total; i += 2) {
+        const ulonglong2 q = *reinterpret_cast<const ulonglong2*>(s_cand + i);
+        rank += (q.x > me) + (i + 1 < total && q.y > me);
+      }
+      if (rank < K) {
+        const int idx = (int)(0xffffffffu - (unsigned)me);
+        s_val[rank] = val[idx];
+        s_idx[rank] = idx;
+      }
+    }
+    Sync::sync();
+    if (tid < K) s_prob[tid] = expf((s_val[tid] - s_val[0]) / cfg.temperature);
+    Sync::sync();
+    if (tid == 0) {
+      // sum and inverse-CDF walk in rank order (sample_topk_f32's sequence)
+      float p[kFastK];
+#pragma unroll
+      for (int i = 0; i < kFastK; i += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(s_prob + i);
+        p[i] = q.x; p[i + 1] = q.y; p[i + 2] = q.z; p[i + 3] = q.w;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < kFastK; ++i)
+        if (i < K) sum += p[i];
+      int pick = 0;
+      if (isfinite(sum) && sum > 0.f) {
+        float target = u * sum;
+        pick = K - 1;
+#pragma unroll
+        for (int i = 0; i < kFastK; ++i) {
+          if (i < K) {
+            if (target <= p[i]) {
+              pick = i;
+              break;
+            }
+            target -= p[i];
+          }
+        }
+      }
+      s_res = s_idx[pick];
+      s_cnt = total;
+    }
+    Sync::sync();
+    return s_res;
+  }
+
   // Returns the token to every thread; *error set when no finite logits.
   // Only thread 0 draws from `rng`.
   __device__ __forceinline__ int select(int V, const SampleCfg& cfg, Rng& rng, int* error) {
@@ -172,6 +338,10 @@ struct Selector {
     // reference), so the draw can run here, off the serial tail.
     float u_dev = 0.f;
     if (device_path && tid == 0) u_dev = rng.next();
+    if (device_path && min(cfg.top_k, V) <= kFastK) {
+      const int r = select_fast(V, cfg, u_dev);
+      if (r >= 0) return r;
+    }
     stamp(0);
     // Keys of this thread's entries (v = j * 256 + tid) stay in registers;
     // 0 marks an ineligible entry (no finite float maps to 0). The device

@@ -108,7 +108,8 @@ pub mod ffi {
         pub codec_eos: u32,
         pub max_cache_steps: usize,
         pub device_bytes: usize,
-        pub fused_mlp_cluster: [i32; 2],
+        pub cp_pass_grid: i32,
+        pub reserved: i32,
         pub has_codec: i32,
         pub samples_per_frame: u32,
     }
@@ -202,6 +203,9 @@ pub mod ffi {
                                    semantic_embed: *const f32,
                                    options: *const qtts_generate_options, tokens_out: *mut i32,
                                    embedding_sum_out: *mut f32, logits_out: *mut f32) -> i32;
+        pub fn qtts_last_cp_pass_timing(engine: *const qtts_engine, ms: *mut f32,
+                                        weight_bytes: *mut f64) -> i32;
+        pub fn qtts_selftest_device_wait(engine: *mut qtts_engine, limit_us: u32) -> i32;
         pub fn qtts_last_timings(engine: *const qtts_engine, prefill_ms: *mut f32,
                                  frames_ms: *mut f32, frames: *mut usize) -> i32;
         pub fn qtts_last_launch_count(engine: *const qtts_engine, kernels: *mut usize) -> i32;

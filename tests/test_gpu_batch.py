@@ -92,3 +92,24 @@ def test_batch_errors(engines, pkg):
             [[1, 2], [3, 4]],
             [pkg.GenerateOptions(decode_audio=False, top_k=50),
              pkg.GenerateOptions(decode_audio=False, top_k=40)])
+
+
+@pytest.mark.parametrize("shape", ["0.6b", "1.7b"])
+def test_batch_of_one_matches_single_full_size(pkg, full_model_dir, shape):
+    """A one-request batch against the same request generated alone, greedy, at
+    the full shapes: both must agree with the oracle's choices (gap-gated)."""
+    from parity import check_codes
+
+    d = full_model_dir(shape)
+    e = pkg.HipTtsEngine.load_with_options(d, pkg.EngineOptions(0, 128))
+    m = O.OracleModel(d, 128)
+    ids = np.random.default_rng(31).integers(0, 150000, 20)
+    opts = pkg.GenerateOptions(decode_audio=False, do_sample=False, subtalker_dosample=False,
+                               repetition_penalty=1.0, max_frames=3)
+    single = e.generate_codes_from_ids(ids, opts)
+    (batch,) = e.generate_codes_batch_from_ids([ids], [opts])
+    pre, tr, pad = m.prepare(list(ids))
+    for label, out in (("single", single), ("batch of 1", batch)):
+        codes, _, recs = m.rollout(pre, tr, pad, 3, GREEDY, GREEDY, forced_codes=out.codes)
+        check_codes(out.codes, codes, recs, f"{shape} {label}")
+    e.close()

@@ -104,3 +104,39 @@ def test_decode_errors(pkg, codec_engine, model_dirs):
         assert out.frames == 2 and out.samples.size == 0
     finally:
         tiny.close()
+
+
+def test_server_shell_streams_the_engine(pkg, codec_engine):
+    """The HTTP shell over the real engine: /api/stream sends one s16le chunk
+    per audio chunk, equal to the Python stream's chunks for the same request;
+    /api/generate's WAV holds decode_codes of the generated codes."""
+    import threading
+
+    from qwen3_tts_hip_b200 import server as S
+    from test_server import _raw_chunks, _post
+
+    srv = S.TtsServer(codec_engine, "127.0.0.1:0", max_cache_frames=64, log=lambda *_: None)
+    t = threading.Thread(target=srv.serve_forever, daemon=True)
+    t.start()
+    try:
+        ids = np.random.default_rng(8).integers(0, 4000, 10)
+        form = ("ids=" + ",".join(str(i) for i in ids) +
+                "&max_frames=7&stream_chunk_frames=3&left_context_frames=2&seed=3&"
+                "text_lookahead_tokens=4")
+        _, chunks = _raw_chunks(srv, form)
+        opts = pkg.GenerateOptions(decode_audio=False, max_frames=7, seed=3)
+        st = codec_engine.start_stream_from_ids(
+            ids, opts, pkg.StreamOptions(text_lookahead_tokens=4, left_context_frames=2))
+        want = []
+        while (ch := st.next_audio_chunk(3)) is not None:
+            want.append(S.pcm16(ch.samples, 1.0))
+        st.close()
+        assert chunks == want and len(chunks) >= 1
+        wav = _post(srv, "/api/generate", "ids=" + ",".join(str(i) for i in ids) +
+                    "&max_frames=5&seed=3").read()
+        gen = codec_engine.generate_codes_from_ids(
+            ids, pkg.GenerateOptions(decode_audio=False, max_frames=5, seed=3))
+        assert wav[44:] == S.pcm16(codec_engine.decode_codes(gen.codes), 1.0)
+    finally:
+        srv.shutdown()
+        srv.server_close()

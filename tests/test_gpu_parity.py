@@ -15,7 +15,7 @@ import pytest
 import torch
 
 from oracle import qtts_oracle as O, synth
-from parity import check_codes
+from parity import check_codes, check_end
 
 pytestmark = pytest.mark.gpu
 
@@ -43,13 +43,14 @@ def gaps_per_code(records):
     return [g for r in records for g in [r.talker_gap] + r.cp_gaps]
 
 
-def assert_tokens_match(gpu_codes, ref_codes, gaps, min_agree=1.0):
+def assert_tokens_match(gpu_codes, ref_codes, gaps):
+    """Greedy codes against the oracle's own choices along the same path:
+    identical wherever the oracle's top-2 gap exceeds GAP."""
     gpu, ref = np.asarray(gpu_codes), np.asarray(ref_codes[: len(gpu_codes)])
     assert len(gpu) == len(ref)
     mism = np.flatnonzero(gpu != ref)
     hard = [int(i) for i in mism if gaps[i] > GAP]
     assert not hard, f"token mismatch above the gap threshold at {hard[:10]}"
-    assert 1.0 - len(mism) / max(1, len(gpu)) >= min_agree
 
 
 @pytest.mark.parametrize("shape", SHAPES)
@@ -79,6 +80,7 @@ def test_talker_prefill_and_step(engines, oracles, shape):
     for off in (pre.shape[0], pre.shape[0] + 1):
         h2, l2, t2 = e.talker_decode_step(x, off)
         _, rh2, rl2 = m.talker_step(torch.from_numpy(x), off)
+        print(f"[logits] {shape} talker step at {off}: max abs error {np.abs(l2 - rl2).max():.2e}")
         assert np.abs(l2 - rl2).max() <= LOGIT_TOL
         assert np.abs(h2 - rh2.numpy()).max() <= LOGIT_TOL
 
@@ -92,6 +94,8 @@ def test_code_predictor_reference_inputs(engines, oracles, shape):
     toks, esum, logits = e.code_predictor(th, se)
     rt, resum, gaps, rlg = m.code_predictor(torch.from_numpy(th), torch.from_numpy(se), GREEDY,
                                             O.Lcg(0), forced=toks)
+    print(f"[logits] {shape} CodePredictor heads: max abs error "
+          f"{max(float(np.abs(logits[g] - rlg[g]).max()) for g in range(len(toks))):.2e}")
     for g in range(len(toks)):
         assert np.abs(logits[g] - rlg[g]).max() <= LOGIT_TOL
         if gaps[g] > GAP:
@@ -153,7 +157,12 @@ def test_graph_equals_eager(engines, oracles, pkg):
                                repetition_penalty=1.0, max_frames=2)
     out = e.generate_codes_from_ids(ids, opts)
     assert out.codes[0] == tok
-    assert out.codes[1:16] == toks
+    # the frame graph runs the persistent CodePredictor pass, the eager seam
+    # the per-op kernels: same arithmetic in a different summation order
+    _, _, gaps, _ = m.code_predictor(torch.from_numpy(hidden), torch.from_numpy(sem), GREEDY,
+                                     O.Lcg(0), forced=toks)
+    bad = [g for g in range(15) if out.codes[1 + g] != toks[g] and gaps[g] > GAP]
+    assert not bad, bad
 
 
 def test_stream_chunks(engines, oracles, pkg):
@@ -263,6 +272,23 @@ def test_errors(engines, pkg):
     assert out.frames == 2
 
 
+def test_bounded_device_wait_reports_expiry(engines, pkg):
+    """A device wait on a counter nothing increments runs out after its bound
+    (0.2 s here) and the host gets the device-state error; the engine keeps
+    working afterwards."""
+    import time
+
+    e = engines["tiny"]
+    t0 = time.perf_counter()
+    with pytest.raises(pkg.CudaError, match="bounded device wait ran out") as info:
+        e.selftest_device_wait(200_000)
+    assert info.value.code == pkg.engine.ERR_DEVICE_STATE
+    assert 0.15 < time.perf_counter() - t0 < 5.0
+    out = e.generate_codes_from_ids(ids_for(15, 5), pkg.GenerateOptions(decode_audio=False,
+                                                                       max_frames=2))
+    assert out.frames == 2
+
+
 def _scale_codec_head_row(src, dst, row, scale):
     """Copies a synthetic checkpoint with one codec_head row scaled."""
     shutil.copytree(src, dst)
@@ -309,6 +335,7 @@ def test_eos_stops_generation(pkg, model_dirs, oracles, tmp_path):
     print("eos test: frames", out.frames, "ended", out.ended_by_eos)
     codes, ended, recs = m.rollout(pre, tr, pad, 20, GREEDY, GREEDY, forced_codes=out.codes)
     assert out.ended_by_eos == ended
+    check_end(m, out.ended_by_eos, "eos test")
     assert out.frames == len(codes) // 16
     assert_tokens_match(out.codes, codes, gaps_per_code(recs))
     if out.ended_by_eos:
@@ -325,6 +352,7 @@ def test_eos_stops_generation(pkg, model_dirs, oracles, tmp_path):
         p2, t2, q2 = m.prepare(list(r))
         c2, ended2, rec2 = m.rollout(p2, t2, q2, 20, GREEDY, GREEDY, forced_codes=o.codes)
         assert o.ended_by_eos == ended2
+        check_end(m, o.ended_by_eos, "eos batch")
         assert o.frames == len(c2) // 16
         assert_tokens_match(o.codes, c2, gaps_per_code(rec2))
     e.close()
@@ -379,17 +407,19 @@ def test_full_size_1p7b(pkg, tmp_path_factory):
     e.close()
 
 
-@pytest.mark.parametrize("env_var,value", [("QTTS_FRAME_KERNEL", "1"), ("QTTS_FUSE_ATTN_O", "0"),
-                                           ("QTTS_FUSE_MLP", "1"), ("QTTS_TC_CP", "1"),
-                                           ("QTTS_TC", "0")])
-def test_alternate_path_parity(model_dirs, tmp_path, env_var, value):
-    """The alternate paths against the oracle: the opt-in persistent frame
-    kernel (QTTS_FRAME_KERNEL=1), the unfused CodePredictor attention
-    (QTTS_FUSE_ATTN_O=0), the fused decode MLP (QTTS_FUSE_MLP=1: gate|up,
-    SwiGLU and down in one kernel, a cluster reduction), the tcgen05 projection also for the CodePredictor's
-    2-row prefill (QTTS_TC_CP=1) and the CUDA-core projections only
-    (QTTS_TC=0). Run in a child process so the engine reads
-    the setting at load."""
+@pytest.mark.parametrize("env", [{"QTTS_CP_PASS": "0"},
+                                 {"QTTS_CP_PASS": "0", "QTTS_FUSE_ATTN_O": "0"},
+                                 {"QTTS_CP_PASS": "0", "QTTS_TC_CP": "1"},
+                                 {"QTTS_TC": "0"}],
+                         ids=["per-op-cp", "per-op-cp-unfused-attn", "per-op-cp-tc-prefill",
+                              "cuda-core-prefill"])
+def test_alternate_path_parity(model_dirs, tmp_path, env):
+    """The alternate paths against the oracle: the CodePredictor as one kernel
+    per op instead of the persistent pass (QTTS_CP_PASS=0), with its attention
+    as a separate kernel (QTTS_FUSE_ATTN_O=0) or its 2-row prefill on the
+    tcgen05 GEMM (QTTS_TC_CP=1), and the talker prefill on CUDA cores only
+    (QTTS_TC=0). Run in a child process so the engine reads the setting at
+    load."""
     import os
     import subprocess
     import sys
@@ -421,11 +451,11 @@ for shape, d in [('tiny', {str(model_dirs['tiny'])!r}), ('tiny_proj', {str(model
     sc = O.SamplingConfig(True, 50, 1.0, 0.9)
     codes2, _, recs2 = m.rollout(pre, tr, pad, 12, sc, sc, penalty=1.05, seed=4, forced_codes=out2.codes)
     ms = [x for r in recs2 for x in [r.talker_margin] + r.cp_margins]
-    bad2 = [i for i, (a, b) in enumerate(zip(out2.codes, codes2)) if a != b and ms[i] > 1e-2]
+    bad2 = [i for i, (a, b) in enumerate(zip(out2.codes, codes2)) if a != b and ms[i] > 2e-3]
     assert not bad2, (shape, bad2)
-print("frame kernel ok")
+print("alternate path ok")
 """
-    env = dict(os.environ, **{env_var: value})
+    env = dict(os.environ, **env)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
                        timeout=600)
-    assert r.returncode == 0 and "frame kernel ok" in r.stdout, r.stdout + r.stderr
+    assert r.returncode == 0 and "alternate path ok" in r.stdout, r.stdout + r.stderr
