@@ -44,6 +44,7 @@ typedef enum {
 typedef struct qtts_engine qtts_engine;
 typedef struct qtts_stream qtts_stream;
 typedef struct qtts_text_stream qtts_text_stream;
+typedef struct qtts_codec_stream qtts_codec_stream;
 
 /* GenerateOptions (src/generation.rs:40-77). speaker/language are config keys
  * ("ryan", "english"); NULL means the reference defaults. */
@@ -148,6 +149,21 @@ int32_t qtts_decode_codes(qtts_engine* engine, const int32_t* codes, size_t n_co
  * qtts_decode_codes between the codes landing and the waveform being ready,
  * and how many kernels it launched. */
 int32_t qtts_last_decode_timing(const qtts_engine* engine, float* ms, size_t* launches);
+
+/* Streaming codec decode with carried state (in place of next_audio_chunk's
+ * re-decode of left-context frames, generation.rs:965-989): each causal
+ * convolution keeps its last input columns and the pre-transformer keeps the
+ * keys / values of every decoded frame, so a chunk decodes only its own
+ * frames and its samples equal those of one qtts_decode_codes call over the
+ * whole stream. open: up to max_frames frames in total (the key / value
+ * cache is sized for them: 64 KiB per frame). decode: the next frames'
+ * codes (frame-major, n_codes = frames * 16) -> frames * 1920 samples;
+ * QTTS_ERR_INVALID_INPUT past max_frames. One stream decodes on the
+ * engine's stream; destroy every codec stream before its engine. */
+int32_t qtts_codec_stream_open(qtts_engine* engine, size_t max_frames, qtts_codec_stream** out);
+int32_t qtts_codec_stream_decode(qtts_codec_stream* stream, const int32_t* codes, size_t n_codes,
+                                 float* samples, size_t samples_capacity, size_t* n_samples);
+void qtts_codec_stream_destroy(qtts_codec_stream* stream);
 
 /* HipTtsEngine::generate_codes (generation.rs:356-371) from content token ids
  * (the ids between the chat-template prefix and suffix, text.rs:357-362);

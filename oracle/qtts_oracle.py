@@ -114,10 +114,11 @@ def argmax_device(logits: np.ndarray) -> int:
 def _cdf_margin(probs, j: int, target0, temperature: float) -> float:
     """How robust an inverse-CDF draw is, in logit units: the smallest logit
     error that could move an edge of the drawn bucket j past the target.
-    With every logit off by at most d, each probability (and so the mass C_e
-    below an edge e, and the target u * sum) moves by a factor of at most
-    exp(d / T), so the edge crosses the target only once
-    d / T >= |target - C_e| / (target + C_e). Sums in fp32, candidate order."""
+    With every logit off by at most d, each probability exp((l - max) / T)
+    moves by a factor of at most exp(2 d / T) (l and the max both move), and
+    so do the mass C_e below an edge e and the target u * sum; the edge
+    crosses the target only once 2 d / T >= |target - C_e| / (target + C_e).
+    Sums in fp32, candidate order."""
     before = np.float32(0.0)
     for i in range(j):
         before = np.float32(before + probs[i])
@@ -126,7 +127,7 @@ def _cdf_margin(probs, j: int, target0, temperature: float) -> float:
     best = float("inf")
     for edge in (float(before), float(after)):
         if t + edge > 0:
-            best = min(best, abs(t - edge) / (t + edge) * float(temperature))
+            best = min(best, abs(t - edge) / (t + edge) * float(temperature) / 2.0)
     return best
 
 

@@ -9,7 +9,8 @@ host-side mirror of the reference's ``HipTtsEngine`` API over its C ABI.
 from . import engine  # noqa: F401
 from .engine import (  # noqa: F401
     SAMPLE_RATE, CudaError, EngineOptions, Error, Finished, GenerateOptions, GeneratedAudioChunk,
-    GeneratedCodes, GeneratedCodesChunk, GeneratedSpeech, HipTextStream, HipTtsEngine, HipTtsStream, InvalidInput,
+    CodecStream, GeneratedCodes, GeneratedCodesChunk, GeneratedSpeech, HipTextStream, HipTtsEngine,
+    HipTtsStream, InvalidInput,
     NeedMoreText, PollingTextStream, StreamOptions, TextStreamInput, TextStreamOptions,
     TtsPreparedInputs, lib, library_path, start_text_stream, SIGNATURES,
 )

@@ -12,13 +12,14 @@ constexpr int kTileT = 128, kTileK = 16, kConvThreads = 256;
 
 template <int ACT>
 __device__ __forceinline__ float codec_act(const CodecConvArgs& a, int ci, int src) {
-  const float x = __ldg(a.x + (long long)ci * a.lin + src);
+  const long long ld = (long long)a.lin + a.hist;
+  const float x = __ldg(a.x + ci * ld + a.hist + src);
   if (ACT == CACT_SNAKE) {
     const float s = sinf(x * __ldg(a.act_a + ci));
     return x + (s * s) / (__ldg(a.act_b + ci) + 1.0e-9f);
   }
   if (ACT == CACT_SWIGLU) {
-    const float u = __ldg(a.x + (long long)(ci + a.up_off) * a.lin + src);
+    const float u = __ldg(a.x + (ci + a.up_off) * ld + a.hist + src);
     return x / (1.0f + expf(-x)) * u;
   }
   return x;
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
       if (kk < K && t < a.lin) {
         const int ci = kk / taps, tap = kk - ci * taps;
         const int src = t + tap * a.dil - a.pad;
-        if (src >= 0 && src < a.lin) v = codec_act<ACT>(a, ci, src);
+        if (src >= -a.hist && src < a.lin) v = codec_act<ACT>(a, ci, src);
       }
       rb[r] = v;
     }
@@ -205,29 +206,45 @@ __global__ void k_codec_chan_norm(const float* x, int C, int T, const float* gam
   }
 }
 
-__global__ void k_codec_dwconv(const float* x, int C, int T, const float* w, const float* b,
-                               int K, float* y) {
+__global__ void k_codec_dwconv(const float* x, int C, int T, int hist, const float* w,
+                               const float* b, int K, float* y) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= C * T) return;
   const int t = idx % T, c = idx / T;
+  const float* xr = x + (long long)c * (T + hist) + hist;
   float s = b[c];
   for (int k = 0; k < K; ++k) {
     const int src = t + k - (K - 1);
-    if (src >= 0) s += x[(long long)c * T + src] * w[c * K + k];
+    if (src >= -hist) s += xr[src] * w[c * K + k];
   }
   y[idx] = s;
 }
 
-// rope_bhsd_f32 (kernels.rs:40-77): angle = t / theta^(2i/hd), rotate-half.
-__global__ void k_codec_qkv_rope(const float* qkv, int heads, int hd, int T, float theta,
-                                 float* q, float* k, float* v) {
+// cat[c] = [state_cur[c] (H columns) | x[c] (n columns)] and state_next[c] =
+// the last H columns of cat[c].
+__global__ void k_codec_hist_cat(const float* state_cur, const float* x, int C, int H, int n,
+                                 float* cat, float* state_next) {
+  const long long W = (long long)H + n;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= C * W) return;
+  const int c = (int)(idx / W), j = (int)(idx % W);
+  const float v = j < H ? state_cur[(long long)c * H + j] : x[(long long)c * n + (j - H)];
+  cat[idx] = v;
+  if (j >= n) state_next[(long long)c * H + (j - n)] = v;
+}
+
+// rope_bhsd_f32 (kernels.rs:40-77): angle = position / theta^(2i/hd),
+// rotate-half; positions pos0 .. pos0 + T - 1. k and v land in the caches
+// [heads][cap][hd] at those positions.
+__global__ void k_codec_qkv_rope(const float* qkv, int heads, int hd, int T, int pos0, int cap,
+                                 float theta, float* q, float* k, float* v) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   const int per = heads * T * hd;
   if (idx >= per) return;
   const int d = idx % hd, t = (idx / hd) % T, h = idx / (hd * T);
   const int half = hd / 2, pair = d % half;
   const float expo = (float)(pair * 2) / (float)hd;
-  const float ang = (float)t / powf(theta, expo);
+  const float ang = (float)(pos0 + t) / powf(theta, expo);
   const float c = cosf(ang), s = sinf(ang);
   const int qo = heads * hd;
   auto rot = [&](int base) {
@@ -236,14 +253,15 @@ __global__ void k_codec_qkv_rope(const float* qkv, int heads, int hd, int T, flo
     return d < half ? first * c - second * s : second * c + first * s;
   };
   q[idx] = rot(0);
-  k[idx] = rot(qo);
-  v[idx] = qkv[(long long)(2 * qo + h * hd + d) * T + t];
+  const long long at = ((long long)h * cap + pos0 + t) * hd + d;
+  k[at] = rot(qo);
+  v[at] = qkv[(long long)(2 * qo + h * hd + d) * T + t];
 }
 
-// One warp per (head, query position): online softmax over keys 0..t; lane l
-// holds dims l and l + 32 (head_dim 64).
+// One warp per (head, query position): online softmax over cached keys
+// 0 .. pos0 + t; lane l holds dims l and l + 32 (head_dim 64).
 __global__ void k_codec_attention(const float* q, const float* k, const float* v, int heads,
-                                  int T, float scale, float* out) {
+                                  int T, int pos0, int cap, float scale, float* out) {
   constexpr int HD = 64;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= heads * T) return;
@@ -251,15 +269,15 @@ __global__ void k_codec_attention(const float* q, const float* k, const float* v
   const float* qr = q + ((long long)h * T + t) * HD;
   const float q0 = qr[lane], q1 = qr[lane + 32];
   float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
-  for (int j = 0; j <= t; ++j) {
-    const float* kr = k + ((long long)h * T + j) * HD;
+  for (int j = 0; j <= pos0 + t; ++j) {
+    const float* kr = k + ((long long)h * cap + j) * HD;
     float s = q0 * kr[lane] + q1 * kr[lane + 32];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     s *= scale;
     const float mn = fmaxf(m, s);
     const float corr = expf(m - mn), e = expf(s - mn);
-    const float* vr = v + ((long long)h * T + j) * HD;
+    const float* vr = v + ((long long)h * cap + j) * HD;
     l = l * corr + e;
     a0 = a0 * corr + e * vr[lane];
     a1 = a1 * corr + e * vr[lane + 32];
@@ -299,7 +317,8 @@ static cudaError_t codec_conv_bm(const CodecConvArgs& a, cudaStream_t stream) {
 }
 
 cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream) {
-  if (a.ci <= 0 || a.co <= 0 || a.lin <= 0 || a.taps <= 0 || a.nphase <= 0 || a.ostride <= 0)
+  if (a.ci <= 0 || a.co <= 0 || a.lin <= 0 || a.taps <= 0 || a.nphase <= 0 || a.ostride <= 0 ||
+      a.hist < 0)
     return cudaErrorInvalidValue;
   // 64-channel tiles, except a 16-channel tile for the final 96 -> 1
   // convolution (a 64-row tile would spend 63/64 of its FMAs on padding) and
@@ -329,24 +348,35 @@ cudaError_t codec_chan_norm(const float* x, int C, int T, const float* gamma, co
   return cudaGetLastError();
 }
 
-cudaError_t codec_dwconv(const float* x, int C, int T, const float* w, const float* b, int K,
-                         float* y, cudaStream_t stream) {
-  k_codec_dwconv<<<blocks((long long)C * T, 256), 256, 0, stream>>>(x, C, T, w, b, K, y);
+cudaError_t codec_dwconv(const float* x, int C, int T, int hist, const float* w, const float* b,
+                         int K, float* y, cudaStream_t stream) {
+  if (hist < 0 || hist > K - 1) return cudaErrorInvalidValue;
+  k_codec_dwconv<<<blocks((long long)C * T, 256), 256, 0, stream>>>(x, C, T, hist, w, b, K, y);
   return cudaGetLastError();
 }
 
-cudaError_t codec_qkv_rope(const float* qkv, int heads, int hd, int T, float theta, float* q,
-                           float* k, float* v, cudaStream_t stream) {
-  k_codec_qkv_rope<<<blocks((long long)heads * T * hd, 256), 256, 0, stream>>>(qkv, heads, hd, T,
-                                                                               theta, q, k, v);
+cudaError_t codec_hist_cat(const float* state_cur, const float* x, int C, int H, int n,
+                           float* cat, float* state_next, cudaStream_t stream) {
+  if (C <= 0 || H <= 0 || n <= 0) return cudaErrorInvalidValue;
+  k_codec_hist_cat<<<blocks((long long)C * (H + n), 256), 256, 0, stream>>>(state_cur, x, C, H, n,
+                                                                            cat, state_next);
+  return cudaGetLastError();
+}
+
+cudaError_t codec_qkv_rope(const float* qkv, int heads, int hd, int T, int pos0, int cap,
+                           float theta, float* q, float* k, float* v, cudaStream_t stream) {
+  if (pos0 < 0 || pos0 + T > cap) return cudaErrorInvalidValue;
+  k_codec_qkv_rope<<<blocks((long long)heads * T * hd, 256), 256, 0, stream>>>(
+      qkv, heads, hd, T, pos0, cap, theta, q, k, v);
   return cudaGetLastError();
 }
 
 cudaError_t codec_attention(const float* q, const float* k, const float* v, int heads, int hd,
-                            int T, float scale, float* out, cudaStream_t stream) {
-  if (hd != 64) return cudaErrorInvalidValue;
-  k_codec_attention<<<blocks((long long)heads * T * 32, 256), 256, 0, stream>>>(q, k, v, heads, T,
-                                                                               scale, out);
+                            int T, int pos0, int cap, float scale, float* out,
+                            cudaStream_t stream) {
+  if (hd != 64 || pos0 < 0 || pos0 + T > cap) return cudaErrorInvalidValue;
+  k_codec_attention<<<blocks((long long)heads * T * 32, 256), 256, 0, stream>>>(
+      q, k, v, heads, T, pos0, cap, scale, out);
   return cudaGetLastError();
 }
 

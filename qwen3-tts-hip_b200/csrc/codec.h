@@ -27,7 +27,9 @@ enum CodecEpi : int {
 //                    act(x[ci][t + k * dil - pad]))
 // for input positions t in [0, lin); t_out = t * ostride + phase with
 // phase = 0 .. nphase-1 (transposed convolutions: one packed weight set per
-// phase, w + phase * w_phase_stride). Out-of-range inputs read as 0.
+// phase, w + phase * w_phase_stride). x holds `hist` columns of history
+// before position 0 (row stride hist + lin; a streaming decoder's carried
+// state); inputs outside [-hist, lin) read as 0.
 struct CodecConvArgs {
   const float* x;
   int ci, lin;
@@ -49,6 +51,7 @@ struct CodecConvArgs {
   const float* out_a;
   const float* out_b;
   float* y2;
+  int hist;
 };
 
 cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream);
@@ -67,17 +70,28 @@ cudaError_t codec_rvq(const int32_t* codes, int frames, int groups, int cb_size,
 cudaError_t codec_chan_norm(const float* x, int C, int T, const float* gamma, const float* beta,
                             float eps, float* y, cudaStream_t stream);
 
-// y[c][t] = b[c] + sum_k w[c][k] * x[c][t + k - (K - 1)] (depthwise, causal).
-cudaError_t codec_dwconv(const float* x, int C, int T, const float* w, const float* b, int K,
-                         float* y, cudaStream_t stream);
+// y[c][t] = b[c] + sum_k w[c][k] * x[c][t + k - (K - 1)] (depthwise, causal);
+// x [C][hist + T] carries hist (<= K - 1) history columns, older ones read 0.
+cudaError_t codec_dwconv(const float* x, int C, int T, int hist, const float* w, const float* b,
+                         int K, float* y, cudaStream_t stream);
 
-// qkv [3 * heads * hd][T] -> q, k (RoPE applied) and v as [heads][T][hd].
-cudaError_t codec_qkv_rope(const float* qkv, int heads, int hd, int T, float theta, float* q,
-                           float* k, float* v, cudaStream_t stream);
+// Streaming history of a causal convolution: cat [C][H + n] = the carried
+// state [C][H] followed by the new input x [C][n]; state_next [C][H] = the
+// last H columns of cat (the state the next chunk starts from).
+cudaError_t codec_hist_cat(const float* state_cur, const float* x, int C, int H, int n,
+                           float* cat, float* state_next, cudaStream_t stream);
 
-// Causal softmax attention per head; out [heads * hd][T].
+// qkv [3 * heads * hd][T] of positions pos0 .. pos0 + T - 1 -> q [heads][T][hd]
+// (RoPE applied) and the caches k (RoPE applied), v [heads][cap][hd] at those
+// positions.
+cudaError_t codec_qkv_rope(const float* qkv, int heads, int hd, int T, int pos0, int cap,
+                           float theta, float* q, float* k, float* v, cudaStream_t stream);
+
+// Causal softmax attention per head of T queries at positions pos0 .. over
+// the cached keys / values [heads][cap][hd]; out [heads * hd][T].
 cudaError_t codec_attention(const float* q, const float* k, const float* v, int heads, int hd,
-                            int T, float scale, float* out, cudaStream_t stream);
+                            int T, int pos0, int cap, float scale, float* out,
+                            cudaStream_t stream);
 
 // y[i] = expf(x[i]) (snake parameters, computed on the device like the
 // reference's per-element expf).

@@ -106,8 +106,8 @@ struct Slice {
 
 __device__ __forceinline__ Slice op_slice(const CpOp& op, int b, int G) {
   Slice s;
-  s.r0 = (int)(((long long)op.N * b) / G);
-  const int r1 = (int)(((long long)op.N * (b + 1)) / G);
+  s.r0 = op.N * b / G;  // N * G < 2^31 for every supported shape
+  const int r1 = op.N * (b + 1) / G;
   s.rows = r1 - s.r0;
   s.row_bytes = op.K * 2;
   s.nchunk = op.epi == EPI_SWIGLU ? 2 : 1;
@@ -139,8 +139,8 @@ __device__ __forceinline__ void top_up(const CpPassParams& p, CpShared* sh, char
   const int G = gridDim.x;
   while (f.op < p.n_ops && f.issued - consumed < (unsigned)kCpStages) {
     const CpLoad w = loads[f.op];
-    const int r0 = (int)(((long long)w.N * blockIdx.x) / G);
-    const int r1 = (int)(((long long)w.N * (blockIdx.x + 1)) / G);
+    const int r0 = w.N * (int)blockIdx.x / G;
+    const int r1 = w.N * ((int)blockIdx.x + 1) / G;
     const int rows = r1 - r0, rps = rows_per_stage_of(w);
     if (f.row >= rows) {  // this chunk is done (or empty)
       f.row = 0;
@@ -229,6 +229,7 @@ __device__ __forceinline__ bool op_rows(const CpPassParams& p, CpShared* sh, Rin
       const unsigned parity = (rg.consumed / kCpStages) & 1u;
       if (ok && !stage_wait(sh, &sh->full[stage], parity, p.error, 4, j)) ok = false;
       if (first && tr) tr[2] = gtime();
+      if (tr && op.kind != CPOP_HEAD) tr[6] = gtime();  // the last piece's arrival
       first = false;
       if (ok) {
         const __nv_bfloat16* wst =
@@ -467,8 +468,6 @@ __device__ void run_pass(const CpPassParams& p, CpShared* sh, char* ring, float*
     const bool ok = op.M == 2 ? op_rows<2>(p, sh, rg, op, sl, xs, out, j, tr)
                               : op_rows<1>(p, sh, rg, op, sl, xs, out, j, tr);
     csync();
-    // every warp is past this op's stages: refill them with later ops' rows
-    if (tid == 0 && ok) top_up(p, sh, ring, loads, fill, rg.consumed, pol);
     if (!ok || *(volatile int*)&sh->abort) break;
     if (tr) tr[3] = gtime();
     // epilogue: this CTA's outputs
@@ -499,6 +498,10 @@ __device__ void run_pass(const CpPassParams& p, CpShared* sh, char* ring, float*
       asm volatile("fence.acq_rel.gpu;" ::: "memory");
       asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(p.counter) : "memory");
       if (tr) tr[5] = gtime();
+      // Every warp is past this op's stages (barriers above): refill them
+      // with later ops' rows while the other CTAs finish this op.
+      top_up(p, sh, ring, loads, fill, rg.consumed, pol);
+      if (tr && op.kind != CPOP_HEAD) tr[8] = gtime() - tr[5];
     }
     if (op.kind != CPOP_HEAD) continue;
 
@@ -508,11 +511,16 @@ __device__ void run_pass(const CpPassParams& p, CpShared* sh, char* ring, float*
     if (*(volatile int*)&sh->abort) break;
     const int V = op.N;
     Selector<SyncConsumers> sel{xs, reinterpret_cast<int*>(xs + kSelMaxVocab)};
+    __shared__ long long s_selclk[16];
+    if (tr) sel.dbg = s_selclk;
     for (int v = tid; v < V; v += kCT) sel.val[v] = __ldcg(op.y + v);
     csync();
     if (tr) tr[6] = gtime();
     const int tok = sel.select(V, p.cfg, rng, sel_err ? sel_err : &dummy_err);
-    if (tr) tr[7] = gtime();
+    if (tr) {
+      tr[7] = gtime();
+      for (int q = 10; q < 16; ++q) tr[8 + (q - 10)] = (unsigned long long)(s_selclk[q] - s_selclk[10]);
+    }
     // next group's input row and the running embedding sum (CTA-local)
     const __nv_bfloat16* e = p.cp_embs + ((long long)op.group * p.vocab + tok) * p.H;
     for (int i = tid * 4; i < p.H; i += kCT * 4) {

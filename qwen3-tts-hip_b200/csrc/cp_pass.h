@@ -111,8 +111,9 @@ constexpr int kCpMaxH = 2048;
 constexpr int kCpScratchBytes = 32768;  // input staging / token selection scratch
 // Trace stamps per op (CTA 0, %globaltimer): past the wait, input staged,
 // first weight stage ready, rows done, outputs stored, arrival issued, and
-// for heads the selection's start and end.
-constexpr int kCpTraceSlots = 8;
+// for heads the selection's start and end (other ops: the last weight
+// stage ready).
+constexpr int kCpTraceSlots = 16;  // slots 8-13: a head's selection phases in clock64 cycles
 
 // Whether the pass kernel supports this CodePredictor / talker shape.
 bool cp_pass_supported(int cp_hidden, int intermediate, int q_heads, int kv_heads, int H,

@@ -403,35 +403,120 @@ class Codec {
   static constexpr int samples_per_frame() { return 2 * 2 * 8 * 5 * 4 * 3; }
   size_t device_bytes() const { return arena_.bytes() + ws_bytes_; }
 
+  // Carried state of a streaming decode: each causal convolution's last input
+  // columns (double-buffered: a chunk reads one set and writes the other) and
+  // the pre-transformer's keys / values of every decoded frame. Decoding a
+  // stream chunk by chunk computes what one decode of all its frames computes.
+  struct StreamState {
+    int cap = 0;     // frames the stream may decode in total
+    int frames = 0;  // frames decoded so far
+    int cur = 0;     // which state set the next chunk reads
+    std::vector<float*> st[2];
+    float* kv = nullptr;  // [layers][2][heads][cap][head_dim]
+    StreamState() = default;
+    StreamState(const StreamState&) = delete;
+    StreamState& operator=(const StreamState&) = delete;
+    ~StreamState() {
+      for (auto& v : st)
+        for (float* p : v) cudaFree(p);
+      if (kv) cudaFree(kv);
+    }
+  };
+
+  // Channels and history columns of every causal convolution, in decode order.
+  static std::vector<std::pair<int, int>> stream_convs() {
+    std::vector<std::pair<int, int>> v;
+    v.push_back({kProj, 2});  // pre_conv (3 taps)
+    v.push_back({kUp, 6});    // upsample 0 dwconv (7 taps)
+    v.push_back({kUp, 6});    // upsample 1 dwconv
+    v.push_back({kPre, 6});   // decoder.0 (7 taps)
+    for (int b = 0; b < 4; ++b) {
+      v.push_back({kBlocks[b][0], 1});  // transposed convolution: inputs i - 1, i
+      for (int u = 0; u < 3; ++u) v.push_back({kBlocks[b][1], 6 * kDil[u]});
+    }
+    v.push_back({kFinal, 6});  // decoder.6
+    return v;
+  }
+  std::unique_ptr<StreamState> open_stream(int cap) {
+    auto s = std::make_unique<StreamState>();
+    s->cap = cap;
+    for (auto [C, H] : stream_convs())
+      for (int k = 0; k < 2; ++k) {
+        void* p = nullptr;
+        QCK(cudaMalloc(&p, (size_t)C * H * 4));
+        QCK(cudaMemsetAsync(p, 0, (size_t)C * H * 4, stream_));
+        s->st[k].push_back(static_cast<float*>(p));
+      }
+    void* p = nullptr;
+    const size_t kvn = (size_t)kLayers * 2 * kHeads * cap * kHeadDim;
+    QCK(cudaMalloc(&p, kvn * 4));
+    s->kv = static_cast<float*>(p);
+    QCK(cudaStreamSynchronize(stream_));
+    return s;
+  }
+
   // HipTtsEngine::decode_codes (generation.rs:619-646) for `frames` frames of
   // device-resident codes; the waveform (frames * 1920 samples) is left in
   // out() on the stream.
-  void decode(const int32_t* d_codes, int frames) {
+  void decode(const int32_t* d_codes, int frames) { run(d_codes, frames, nullptr); }
+  // The next `frames` frames of a streaming decode: out() receives the
+  // waveform of exactly these frames, equal to their samples in one decode
+  // of the whole stream.
+  void decode_chunk(StreamState& s, const int32_t* d_codes, int frames) {
+    if (s.frames + frames > s.cap) throw QttsError(QTTS_ERR_INVALID_INPUT, "codec stream is full");
+    run(d_codes, frames, &s);
+    s.frames += frames;
+    s.cur ^= 1;
+  }
+
+ private:
+  void run(const int32_t* d_codes, int frames, StreamState* s) {
     ensure(frames);
     const int T = frames;
     launches = 0;
+    int sc = 0;  // next causal convolution's state slot
+    // x with its carried history in front (ws_.cat), or x alone (one-shot)
+    auto hist = [&](const float* x, int C, int n, int* h) -> const float* {
+      const int slot = sc++;
+      if (!s) {
+        *h = 0;
+        return x;
+      }
+      const int H = stream_convs_[slot].second;
+      QCK(codec_hist_cat(s->st[s->cur][slot], x, C, H, n, ws_.cat, s->st[s->cur ^ 1][slot],
+                         stream_));
+      ++launches;
+      *h = H;
+      return ws_.cat;
+    };
+    int h = 0;
+    const int pos0 = s ? s->frames : 0, kvcap = s ? s->cap : T;
     // RVQ + pre_conv
     QCK(codec_rvq(d_codes, T, kGroups, kCbSize, kCbDim, cb_first_, cb_rest_, wf_, wr_, kProj,
                   ws_.first, ws_.rest, ws_.a, stream_));
     launches += 2;
-    conv(ws_.a, kProj, T, pre_w_, 0, pre_b_, kPre, 3, 1, 2, ws_.b);
+    const float* xin = hist(ws_.a, kProj, T, &h);
+    conv(xin, kProj, T, pre_w_, 0, pre_b_, kPre, 3, 1, 2, ws_.b, h);
     // pre_transformer (codec_hip.rs:379-653)
     conv(ws_.b, kPre, T, in_w_, 0, in_b_, kHidden, 1, 1, 0, ws_.h);
     const int qo = kHeads * kHeadDim;
     for (int l = 0; l < kLayers; ++l) {
       const Layer& L = layers_[l];
+      float* kc = s ? s->kv + (size_t)l * 2 * kHeads * kvcap * kHeadDim : ws_.k;
+      float* vc = s ? kc + (size_t)kHeads * kvcap * kHeadDim : ws_.v;
       QCK(codec_chan_norm(ws_.h, kHidden, T, L.in_g, nullptr, 1e-5f, ws_.n, stream_));
       conv(ws_.n, kHidden, T, L.wqkv, 0, nullptr, 3 * qo, 1, 1, 0, ws_.qkv);
-      QCK(codec_qkv_rope(ws_.qkv, kHeads, kHeadDim, T, 10000.0f, ws_.q, ws_.k, ws_.v, stream_));
-      QCK(codec_attention(ws_.q, ws_.k, ws_.v, kHeads, kHeadDim, T, 1.0f / std::sqrt(64.0f),
-                          ws_.att, stream_));
+      QCK(codec_qkv_rope(ws_.qkv, kHeads, kHeadDim, T, pos0, kvcap, 10000.0f, ws_.q, kc, vc,
+                         stream_));
+      QCK(codec_attention(ws_.q, kc, vc, kHeads, kHeadDim, T, pos0, kvcap,
+                          1.0f / std::sqrt(64.0f), ws_.att, stream_));
       launches += 3;
-      conv(ws_.att, qo, T, L.wo, 0, nullptr, kHidden, 1, 1, 0, ws_.h, CACT_NONE, nullptr,
+      conv(ws_.att, qo, T, L.wo, 0, nullptr, kHidden, 1, 1, 0, ws_.h, 0, CACT_NONE, nullptr,
            nullptr, 0, CEPI_RESID, ws_.h, L.attn_scale);
       QCK(codec_chan_norm(ws_.h, kHidden, T, L.post_g, nullptr, 1e-5f, ws_.n, stream_));
       ++launches;
       conv(ws_.n, kHidden, T, L.wgu, 0, nullptr, 2 * kInter, 1, 1, 0, ws_.qkv);
-      conv(ws_.qkv, kInter, T, L.wdown, 0, nullptr, kHidden, 1, 1, 0, ws_.h, CACT_SWIGLU,
+      conv(ws_.qkv, kInter, T, L.wdown, 0, nullptr, kHidden, 1, 1, 0, ws_.h, 0, CACT_SWIGLU,
            nullptr, nullptr, kInter, CEPI_RESID, ws_.h, L.mlp_scale);
     }
     QCK(codec_chan_norm(ws_.h, kHidden, T, norm_, nullptr, 1e-5f, ws_.n, stream_));
@@ -443,15 +528,16 @@ class Codec {
     for (int i = 0; i < 2; ++i) {
       const Up& U = ups_[i];
       float* y = x == ws_.a ? ws_.b : ws_.a;
-      conv(x, kUp, L, U.tw, (long long)kUp * kUp, U.tb, kUp, 1, 1, 0, y, CACT_NONE, nullptr,
+      conv(x, kUp, L, U.tw, (long long)kUp * kUp, U.tb, kUp, 1, 1, 0, y, 0, CACT_NONE, nullptr,
            nullptr, 0, 0, nullptr, nullptr, 2, 2);
       L *= 2;
-      QCK(codec_dwconv(y, kUp, L, U.dw, U.dwb, 7, ws_.n, stream_));
+      const float* yin = hist(y, kUp, L, &h);
+      QCK(codec_dwconv(yin, kUp, L, h, U.dw, U.dwb, 7, ws_.n, stream_));
       QCK(codec_chan_norm(ws_.n, kUp, L, U.ln_g, U.ln_b, 1e-6f, ws_.att, stream_));
       launches += 2;
-      conv(ws_.att, kUp, L, U.pw1, 0, U.pw1b, kCnx, 1, 1, 0, ws_.qkv, CACT_NONE, nullptr, nullptr,
-           0, CEPI_GELU);
-      conv(ws_.qkv, kCnx, L, U.pw2, 0, U.pw2b, kUp, 1, 1, 0, y, CACT_NONE, nullptr, nullptr, 0,
+      conv(ws_.att, kUp, L, U.pw1, 0, U.pw1b, kCnx, 1, 1, 0, ws_.qkv, 0, CACT_NONE, nullptr,
+           nullptr, 0, CEPI_GELU);
+      conv(ws_.qkv, kCnx, L, U.pw2, 0, U.pw2b, kUp, 1, 1, 0, y, 0, CACT_NONE, nullptr, nullptr, 0,
            CEPI_RESID, y, U.gamma);
       x = y;
     }
@@ -463,28 +549,34 @@ class Codec {
     // reads it next (the next unit, the next block, the final convolution).
     float* s_in = ws_.sa;
     float* s_out = ws_.sb;
-    conv(x, kPre, L, d0_w_, 0, d0_b_, kDec0, 7, 1, 6, s_in, CACT_NONE, nullptr, nullptr, 0,
+    xin = hist(x, kPre, L, &h);
+    conv(xin, kPre, L, d0_w_, 0, d0_b_, kDec0, 7, 1, 6, s_in, h, CACT_NONE, nullptr, nullptr, 0,
          CEPI_SNAKE, nullptr, nullptr, 1, 1, blocks_[0].sa, blocks_[0].sb);
     for (int b = 0; b < 4; ++b) {
-      const int cin = kBlocks[b][0], cout = kBlocks[b][1], s = kBlocks[b][2];
+      const int cin = kBlocks[b][0], cout = kBlocks[b][1], st = kBlocks[b][2];
       const Block& B = blocks_[b];
-      conv(s_in, cin, L, B.tw, (long long)cout * cin * 2, B.tb, cout, 2, 1, 1, ws_.x, CACT_NONE,
-           nullptr, nullptr, 0, 0, nullptr, nullptr, s, s, B.res[0].a1, B.res[0].b1, s_out);
-      L *= s;
+      xin = hist(s_in, cin, L, &h);
+      conv(xin, cin, L, B.tw, (long long)cout * cin * 2, B.tb, cout, 2, 1, 1, ws_.x, h, CACT_NONE,
+           nullptr, nullptr, 0, 0, nullptr, nullptr, st, st, B.res[0].a1, B.res[0].b1, s_out);
+      L *= st;
       for (int u = 0; u < 3; ++u) {
         const Res& R = B.res[u];
-        conv(s_out, cout, L, R.c1, 0, R.c1b, cout, 7, kDil[u], 6 * kDil[u], ws_.scr, CACT_NONE,
+        xin = hist(s_out, cout, L, &h);
+        conv(xin, cout, L, R.c1, 0, R.c1b, cout, 7, kDil[u], 6 * kDil[u], ws_.scr, h, CACT_NONE,
              nullptr, nullptr, 0, CEPI_SNAKE, nullptr, nullptr, 1, 1, R.a2, R.b2);
         const float* na = u < 2 ? B.res[u + 1].a1 : b < 3 ? blocks_[b + 1].sa : fa_;
         const float* nb = u < 2 ? B.res[u + 1].b1 : b < 3 ? blocks_[b + 1].sb : fb_;
-        conv(ws_.scr, cout, L, R.c2, 0, R.c2b, cout, 1, 1, 0, ws_.x, CACT_NONE, nullptr, nullptr,
-             0, CEPI_RESID, ws_.x, nullptr, 1, 1, na, nb, s_out);
+        conv(ws_.scr, cout, L, R.c2, 0, R.c2b, cout, 1, 1, 0, ws_.x, 0, CACT_NONE, nullptr,
+             nullptr, 0, CEPI_RESID, ws_.x, nullptr, 1, 1, na, nb, s_out);
       }
       std::swap(s_in, s_out);
     }
-    conv(s_in, kFinal, L, f_w_, 0, f_b_, 1, 7, 1, 6, ws_.wav, CACT_NONE, nullptr, nullptr, 0,
+    xin = hist(s_in, kFinal, L, &h);
+    conv(xin, kFinal, L, f_w_, 0, f_b_, 1, 7, 1, 6, ws_.wav, h, CACT_NONE, nullptr, nullptr, 0,
          CEPI_CLAMP);
   }
+
+ public:
   const float* out() const { return ws_.wav; }
   size_t launches = 0;  // kernels enqueued by the last decode
   int32_t* codes_buffer(int frames) {
@@ -508,8 +600,9 @@ class Codec {
   } blocks_[4]{};
   struct Ws {
     int32_t* codes;
-    float *first, *rest, *a, *b, *h, *n, *qkv, *q, *k, *v, *att, *x, *sa, *sb, *scr, *wav;
+    float *first, *rest, *a, *b, *h, *n, *qkv, *q, *k, *v, *att, *x, *sa, *sb, *scr, *wav, *cat;
   } ws_{};
+  const std::vector<std::pair<int, int>> stream_convs_ = stream_convs();
 
   // Transposed convolution weight [cin][cout][K] (stride s, K = s or 2 s)
   // as one causal convolution per output phase p: [p][cout][cin * taps],
@@ -531,14 +624,15 @@ class Codec {
   }
 
   void conv(const float* x, int ci, int lin, const float* w, long long w_phase_stride,
-            const float* bias, int co, int taps, int dil, int pad, float* y, int act = CACT_NONE,
+            const float* bias, int co, int taps, int dil, int pad, float* y, int hist = 0,
+            int act = CACT_NONE,
             const float* act_a = nullptr, const float* act_b = nullptr, int up_off = 0,
             int epi = 0, const float* resid = nullptr, const float* rscale = nullptr,
             int ostride = 1, int nphase = 1, const float* out_a = nullptr,
             const float* out_b = nullptr, float* y2 = nullptr) {
     CodecConvArgs a{x,   ci,     lin,    w,      w_phase_stride, bias,  co,     taps, dil,
                     pad, act,    act_a,  act_b,  up_off,         y,     ostride, nphase, epi,
-                    resid, rscale, out_a, out_b, y2};
+                    resid, rscale, out_a, out_b, y2, hist};
     QCK(codec_conv(a, stream_));
     ++launches;
   }
@@ -581,12 +675,16 @@ class Codec {
     ws_.sb = al(T * big);
     ws_.scr = al(T * big);
     ws_.wav = al(T * samples_per_frame());
+    // a streamed convolution's input with its history in front
+    size_t hist_max = 0;
+    for (auto [C, H] : stream_convs_) hist_max = std::max(hist_max, (size_t)C * H);
+    ws_.cat = al(T * std::max(big, (size_t)4 * kUp) + hist_max);
     cap_ = frames;
   }
   void release() {
     for (float* p : {reinterpret_cast<float*>(ws_.codes), ws_.first, ws_.rest, ws_.a, ws_.b, ws_.h,
                      ws_.n, ws_.qkv, ws_.q, ws_.k, ws_.v, ws_.att, ws_.x, ws_.sa, ws_.sb,
-                     ws_.scr, ws_.wav})
+                     ws_.scr, ws_.wav, ws_.cat})
       if (p) cudaFree(p);
     ws_ = Ws{};
     ws_bytes_ = 0;
@@ -704,7 +802,8 @@ class Engine {
   qtts_generate_options seq_opts{};
   // codec decoder (speech_tokenizer/model.safetensors); null when absent
   std::unique_ptr<Codec> codec;
-  size_t decode_codes(const int32_t* codes, size_t n_codes, float* out, size_t cap);
+  size_t decode_codes(const int32_t* codes, size_t n_codes, float* out, size_t cap,
+                      Codec::StreamState* cs = nullptr);
   float last_decode_ms = 0.f;  // device time of the last decode (codes resident to waveform)
   uint64_t seq_id = 0;
 
@@ -1111,7 +1210,9 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
 }
 
 // HipTtsEngine::decode_codes (generation.rs:619-646).
-size_t Engine::decode_codes(const int32_t* codes, size_t n_codes, float* out, size_t cap) {
+// With a codec stream state: the stream's next frames (carried state).
+size_t Engine::decode_codes(const int32_t* codes, size_t n_codes, float* out, size_t cap,
+                            Codec::StreamState* cs) {
   if (n_codes % Codec::kGroups != 0)
     invalid("code length " + std::to_string(n_codes) + " is not divisible by " +
             std::to_string(Codec::kGroups));
@@ -1124,7 +1225,10 @@ size_t Engine::decode_codes(const int32_t* codes, size_t n_codes, float* out, si
   int32_t* d = codec->codes_buffer((int)frames);
   h2d(d, codes, n_codes * sizeof(int32_t));
   QCK(cudaEventRecord(ev0, stream));
-  codec->decode(d, (int)frames);
+  if (cs)
+    codec->decode_chunk(*cs, d, (int)frames);
+  else
+    codec->decode(d, (int)frames);
   QCK(cudaEventRecord(ev1, stream));
   QCK(cudaMemcpyAsync(out, codec->out(), samples * sizeof(float), cudaMemcpyDeviceToHost, stream));
   QCK(cudaStreamSynchronize(stream));
@@ -1724,14 +1828,17 @@ void Engine::dump_step_trace() {
                  cudaMemcpyDeviceToHost));
   FILE* g = std::fopen((step_trace_path + ".cp").c_str(), "w");
   if (!g) return;
-  std::fprintf(g, "# op wait staged first_stage rows stored arrived sel0 sel1 (ns after op 0's "
-                  "wait; sel only for heads) name\n");
+  std::fprintf(g, "# op wait staged first_stage rows stored arrived last_stage|sel0 sel1 (ns "
+                  "after op 0's wait), then for heads six selection marks in cycles "
+                  "(keys, radix, compaction, rank, exp, end) name\n");
   const unsigned long long c0 = c[0];
   for (int i = 0; i < cp_n_ops; ++i) {
     std::fprintf(g, "%d", i);
     for (int k = 0; k < kCpTraceSlots; ++k) {
       const unsigned long long v = c[(size_t)kCpTraceSlots * i + k];
-      std::fprintf(g, " %lld", v >= c0 && v - c0 < (1ull << 40) ? (long long)(v - c0) : -1LL);
+      const bool cycles = k >= 8;
+      std::fprintf(g, " %lld", cycles ? (long long)v
+                                      : (v >= c0 && v - c0 < (1ull << 40) ? (long long)(v - c0) : -1LL));
     }
     std::fprintf(g, " %s\n", cp_op_names[i].c_str());
   }
@@ -2120,6 +2227,10 @@ struct qtts_stream {
 struct qtts_text_stream {
   qtts::TextStream s;
 };
+struct qtts_codec_stream {
+  qtts::Engine* e;
+  std::unique_ptr<qtts::Codec::StreamState> st;
+};
 
 namespace {
 
@@ -2284,6 +2395,47 @@ int32_t qtts_decode_codes(qtts_engine* h, const int32_t* codes, size_t n_codes, 
     }
     *n_samples = e.decode_codes(codes, n_codes, samples, cap);
   });
+}
+
+int32_t qtts_codec_stream_open(qtts_engine* h, size_t max_frames, qtts_codec_stream** out) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    need(out, "out");
+    *out = nullptr;
+    if (!e.codec) qtts::fail(QTTS_ERR_UNSUPPORTED, "no codec: speech_tokenizer/model.safetensors not found");
+    if (max_frames == 0 || max_frames > (size_t)INT32_MAX / qtts::Codec::samples_per_frame())
+      qtts::invalid("max_frames must be in [1, " +
+              std::to_string(INT32_MAX / qtts::Codec::samples_per_frame()) + "]");
+    auto s = std::make_unique<qtts_codec_stream>();
+    s->e = &e;
+    s->st = e.codec->open_stream((int)max_frames);
+    *out = s.release();
+  });
+}
+
+int32_t qtts_codec_stream_decode(qtts_codec_stream* s, const int32_t* codes, size_t n_codes,
+                                 float* samples, size_t cap, size_t* n_samples) {
+  return guard([&] {
+    need(s, "stream");
+    need(n_samples, "n_samples");
+    if (n_codes) {
+      need(codes, "codes");
+      need(samples, "samples");
+    }
+    Engine& e = *s->e;
+    QCK(cudaSetDevice(e.device));
+    if (n_codes % qtts::Codec::kGroups == 0 &&
+        (size_t)s->st->frames + n_codes / qtts::Codec::kGroups > (size_t)s->st->cap)
+      qtts::invalid("codec stream holds " + std::to_string(s->st->cap) + " frames; " +
+              std::to_string(s->st->frames) + " decoded");
+    *n_samples = e.decode_codes(codes, n_codes, samples, cap, s->st.get());
+  });
+}
+
+void qtts_codec_stream_destroy(qtts_codec_stream* s) {
+  if (!s) return;
+  cudaSetDevice(s->e->device);
+  delete s;
 }
 
 int32_t qtts_last_decode_timing(const qtts_engine* h, float* ms, size_t* launches) {

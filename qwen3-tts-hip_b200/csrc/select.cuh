@@ -70,7 +70,8 @@ template <typename Sync>
 struct Selector {
   float* val;
   int* aux;
-  long long* dbg = nullptr;  // optional phase timestamps (thread 0)
+  long long* dbg = nullptr;  // optional phase timestamps (thread 0): clock64 at slots
+                             // 0-6 (general path) and 10-15 (fast path)
   __device__ __forceinline__ void stamp(int i) {
     if (dbg && threadIdx.x == 0) dbg[i] = clock64();
   }
@@ -164,6 +165,7 @@ struct Selector {
       }
       key[j] = k;
     }
+    stamp(10);
     unsigned prefix = 0u, mask = 0u, lower = 0u;
     int above = 0, rem = K, buf = 0;
     bool done = false;
@@ -214,6 +216,7 @@ struct Selector {
         break;
       }
     }
+    stamp(11);
     if (!done) return -1;  // more than kFastCand keys equal the threshold (uniform)
     // compaction: keys at or above `lower`, per-warp ballots, warp order
     auto take = [&](unsigned k) { return k != 0u && k >= lower; };
@@ -240,6 +243,7 @@ struct Selector {
       base += __popc(bal);
     }
     Sync::sync();
+    stamp(12);
     // exact rank of each candidate: larger key first, then lower index
     if (tid < total) {
       const unsigned long long me = s_cand[tid];
@@ -255,8 +259,10 @@ struct Selector {
       }
     }
     Sync::sync();
+    stamp(13);
     if (tid < K) s_prob[tid] = expf((s_val[tid] - s_val[0]) / cfg.temperature);
     Sync::sync();
+    stamp(14);
     if (tid == 0) {
       // sum and inverse-CDF walk in rank order (sample_topk_f32's sequence)
       float p[kFastK];
@@ -288,6 +294,7 @@ struct Selector {
       s_cnt = total;
     }
     Sync::sync();
+    stamp(15);
     return s_res;
   }
 

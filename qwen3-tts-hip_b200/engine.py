@@ -106,6 +106,9 @@ SIGNATURES = {
     "qtts_engine_get_info": (C.c_int32, [_P, C.POINTER(_Info)]),
     "qtts_decode_codes": (C.c_int32, [_P, _I32, C.c_size_t, _F, C.c_size_t, _SZ]),
     "qtts_last_decode_timing": (C.c_int32, [_P, _F, _SZ]),
+    "qtts_codec_stream_open": (C.c_int32, [_P, C.c_size_t, C.POINTER(_P)]),
+    "qtts_codec_stream_decode": (C.c_int32, [_P, _I32, C.c_size_t, _F, C.c_size_t, _SZ]),
+    "qtts_codec_stream_destroy": (None, [_P]),
     "qtts_generate_codes_from_ids": (C.c_int32, [_P, _U32, C.c_size_t, C.POINTER(_Options), _I32, C.c_size_t, _SZ, _I32]),
     "qtts_generate_codes_batch_from_ids": (C.c_int32, [_P, _U32, _SZ, C.c_size_t, C.POINTER(_Options), _I32, C.c_size_t, _SZ, _I32]),
     "qtts_generate_voice_clone_codes_from_ids": (C.c_int32, [_P, _U32, C.c_size_t, _F, C.POINTER(_Options), _I32, C.c_size_t, _SZ, _I32]),
@@ -215,6 +218,10 @@ class StreamOptions:
     """StreamOptions (generation.rs:79-92)."""
     text_lookahead_tokens: int = DEFAULT_TEXT_LOOKAHEAD_TOKENS
     left_context_frames: int = DEFAULT_STREAM_LEFT_CONTEXT_FRAMES
+    # False: audio chunks re-decode left_context_frames earlier frames, as the
+    # reference does. True: a CodecStream carries the decoder state, so a
+    # chunk decodes only its own frames (samples equal a one-shot decode).
+    carry_codec_state: bool = False
 
 
 @dataclass
@@ -224,6 +231,7 @@ class TextStreamOptions:
     min_resume_tokens: int = 1
     flush_on_punctuation: bool = True
     left_context_frames: int = DEFAULT_STREAM_LEFT_CONTEXT_FRAMES
+    carry_codec_state: bool = False  # as StreamOptions.carry_codec_state
 
 
 @dataclass
@@ -450,10 +458,20 @@ class HipTtsEngine:
         _check(lib().qtts_last_decode_timing(self._h, C.byref(ms), C.byref(n)))
         return float(ms.value), int(n.value)
 
-    def _audio_chunk(self, all_codes: list, chunk: "GeneratedCodesChunk", left_context: int
-                     ) -> GeneratedAudioChunk:
+    def open_codec_stream(self, max_frames: int) -> "CodecStream":
+        """A streaming codec decode of up to max_frames frames with carried state."""
+        h = C.c_void_p()
+        _check(lib().qtts_codec_stream_open(self._h, int(max_frames), C.byref(h)))
+        return CodecStream(self, h)
+
+    def _audio_chunk(self, all_codes: list, chunk: "GeneratedCodesChunk", left_context: int,
+                     codec_stream: Optional["CodecStream"] = None) -> GeneratedAudioChunk:
         """next_audio_chunk's window (generation.rs:965-989): decode the chunk
-        with up to left_context earlier frames and drop their samples."""
+        with up to left_context earlier frames and drop their samples; with a
+        codec stream, decode only the chunk's frames on its carried state."""
+        if codec_stream is not None:
+            return GeneratedAudioChunk(codec_stream.decode(chunk.codes), SAMPLE_RATE, chunk.frames,
+                                       chunk.total_frames, chunk.ended_by_eos)
         start = chunk.total_frames - chunk.frames
         ctx = min(left_context, start)
         g = self.code_groups
@@ -489,7 +507,8 @@ class HipTtsEngine:
         cso = _StreamOptions(int(so.text_lookahead_tokens), int(so.left_context_frames))
         _check(lib().qtts_stream_start_from_ids(self._h, ids.ctypes.data_as(_U32), ids.size,
                                                 C.byref(options._c()), C.byref(cso), C.byref(h)))
-        return HipTtsStream(self, h, options.max_frames, int(so.left_context_frames))
+        return HipTtsStream(self, h, options.max_frames, int(so.left_context_frames),
+                            bool(so.carry_codec_state))
 
     def start_text_stream_polling(self, options: Optional[GenerateOptions] = None,
                                   stream_options: Optional[TextStreamOptions] = None) -> "PollingTextStream":
@@ -500,7 +519,8 @@ class HipTtsEngine:
                                  int(bool(so.flush_on_punctuation)), int(so.left_context_frames))
         h = C.c_void_p()
         _check(lib().qtts_text_stream_start(self._h, C.byref(options._c()), C.byref(cso), C.byref(h)))
-        return PollingTextStream(self, h, options.max_frames, int(so.left_context_frames))
+        return PollingTextStream(self, h, options.max_frames, int(so.left_context_frames),
+                                 bool(so.carry_codec_state))
 
     # ---- parity seams (talker-prefill-parity / code-predictor-parity)
     def talker_prefill(self, rows: np.ndarray):
@@ -579,21 +599,60 @@ class HipTtsEngine:
         return ms.value, b.value
 
 
+class CodecStream:
+    """Streaming codec decode with carried state (qtts_codec_stream_*): each
+    decode() takes the next frames' codes and returns exactly their samples,
+    equal to those of one decode_codes call over the whole stream."""
+
+    def __init__(self, engine: HipTtsEngine, handle):
+        self._e, self._h = engine, handle
+
+    def decode(self, codes) -> np.ndarray:
+        a = np.ascontiguousarray(np.asarray(codes, dtype=np.int32).reshape(-1))
+        g = self._e.code_groups
+        n = a.size // g * self._e.samples_per_code_frame if a.size % g == 0 else 0
+        out = np.zeros(max(1, n), dtype=np.float32)
+        got = C.c_size_t()
+        _check(lib().qtts_codec_stream_decode(self._h, a.ctypes.data_as(_I32), a.size,
+                                              out.ctypes.data_as(_F), n, C.byref(got)))
+        return out[: got.value]
+
+    def close(self):
+        if self._h:
+            lib().qtts_codec_stream_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class HipTtsStream:
     """HipTtsStream (generation.rs:145-163, 876-997)."""
 
     def __init__(self, engine: HipTtsEngine, handle, max_frames: int,
-                 left_context_frames: int = DEFAULT_STREAM_LEFT_CONTEXT_FRAMES):
+                 left_context_frames: int = DEFAULT_STREAM_LEFT_CONTEXT_FRAMES,
+                 carry_codec_state: bool = False):
         self._e, self._h = engine, handle
         self._codes: list = []
         self._ended = False
         self._max = max_frames
         self._ctx = left_context_frames
+        self._carry = carry_codec_state
+        self._codec: Optional[CodecStream] = None
+
+    def _codec_stream(self) -> Optional[CodecStream]:
+        if self._carry and self._codec is None:
+            self._codec = self._e.open_codec_stream(self._max)
+        return self._codec
 
     def next_audio_chunk(self, max_chunk_frames: int) -> Optional[GeneratedAudioChunk]:
         """next_audio_chunk (generation.rs:965-989)."""
         ch = self.next_codes_chunk(max_chunk_frames)
-        return None if ch is None else self._e._audio_chunk(self._codes, ch, self._ctx)
+        return None if ch is None else self._e._audio_chunk(self._codes, ch, self._ctx,
+                                                            self._codec_stream())
 
     def next_codes_chunk(self, max_chunk_frames: int) -> Optional[GeneratedCodesChunk]:
         out = np.zeros(max(1, int(max_chunk_frames)) * self._e.code_groups, dtype=np.int32)
@@ -611,6 +670,9 @@ class HipTtsStream:
         return GeneratedCodes(list(self._codes), len(self._codes) // self._e.code_groups, self._ended)
 
     def close(self):
+        if self._codec is not None:
+            self._codec.close()
+            self._codec = None
         if self._h:
             lib().qtts_stream_destroy(self._h)
             self._h = None
@@ -626,10 +688,13 @@ class PollingTextStream:
     """PollingTextStream (generation.rs:1086-1451) fed with token ids."""
 
     def __init__(self, engine: HipTtsEngine, handle, max_frames: int,
-                 left_context_frames: int = DEFAULT_STREAM_LEFT_CONTEXT_FRAMES):
+                 left_context_frames: int = DEFAULT_STREAM_LEFT_CONTEXT_FRAMES,
+                 carry_codec_state: bool = False):
         self._e, self._h, self._max = engine, handle, max_frames
         self._ctx = left_context_frames
         self._codes: list = []
+        self._carry = carry_codec_state
+        self._codec: Optional[CodecStream] = None
 
     def next_audio_chunk(self, max_chunk_frames: int):
         """IncrementalAudio from next_audio_chunk (generation.rs:1121-1181):
@@ -638,7 +703,9 @@ class PollingTextStream:
         r = self.next_codes_chunk(max_chunk_frames)
         if not isinstance(r, GeneratedCodesChunk):
             return r
-        return self._e._audio_chunk(self._codes, r, self._ctx)
+        if self._carry and self._codec is None:
+            self._codec = self._e.open_codec_stream(self._max)
+        return self._e._audio_chunk(self._codes, r, self._ctx, self._codec)
 
     def push_ids(self, ids) -> None:
         a = _ids(ids)
@@ -672,6 +739,9 @@ class PollingTextStream:
         return GeneratedCodes(out[: n.value * self._e.code_groups].tolist(), n.value, bool(ended.value))
 
     def close(self):
+        if self._codec is not None:
+            self._codec.close()
+            self._codec = None
         if self._h:
             lib().qtts_text_stream_destroy(self._h)
             self._h = None

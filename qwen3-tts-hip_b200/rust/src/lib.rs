@@ -49,6 +49,10 @@ pub mod ffi {
     pub struct qtts_text_stream {
         _private: [u8; 0],
     }
+    #[repr(C)]
+    pub struct qtts_codec_stream {
+        _private: [u8; 0],
+    }
 
     #[repr(C)]
     #[derive(Clone, Copy, Debug)]
@@ -136,6 +140,12 @@ pub mod ffi {
                                  n_samples: *mut usize) -> i32;
         pub fn qtts_last_decode_timing(engine: *const qtts_engine, ms: *mut f32,
                                        launches: *mut usize) -> i32;
+        pub fn qtts_codec_stream_open(engine: *mut qtts_engine, max_frames: usize,
+                                      out: *mut *mut qtts_codec_stream) -> i32;
+        pub fn qtts_codec_stream_decode(stream: *mut qtts_codec_stream, codes: *const i32,
+                                        n_codes: usize, samples: *mut f32,
+                                        samples_capacity: usize, n_samples: *mut usize) -> i32;
+        pub fn qtts_codec_stream_destroy(stream: *mut qtts_codec_stream);
         pub fn qtts_generate_codes_from_ids(engine: *mut qtts_engine, content_ids: *const u32,
                                             n_ids: usize, options: *const qtts_generate_options,
                                             codes_out: *mut i32, codes_capacity: usize,
@@ -554,6 +564,23 @@ impl HipTtsEngine {
         Ok(out)
     }
 
+    /// A streaming codec decode of up to `max_frames` frames with carried
+    /// state: each chunk decodes only its own frames, and the chunks join to
+    /// `decode_codes` of all of them (in place of the re-decode of
+    /// left-context frames in `next_audio_chunk`, generation.rs:965-989).
+    pub fn open_codec_stream(&self, max_frames: usize) -> Result<CodecStream<'_>> {
+        let mut h = std::ptr::null_mut();
+        // SAFETY: h receives a new codec-stream handle.
+        check("qtts_codec_stream_open", unsafe {
+            ffi::qtts_codec_stream_open(self.handle, max_frames, &mut h)
+        })?;
+        Ok(CodecStream {
+            handle: h,
+            samples_per_code: self.samples_per_code_frame() / self.groups(),
+            _engine: PhantomData,
+        })
+    }
+
     /// `HipTtsEngine::start_stream` (generation.rs:421-440) on content ids.
     pub fn start_stream_from_ids(&self, content_ids: &[u32], options: &GenerateOptions,
                                  stream_options: &StreamOptions) -> Result<HipTtsStream<'_>> {
@@ -595,6 +622,35 @@ impl Drop for HipTtsEngine {
     fn drop(&mut self) {
         // SAFETY: the handle came from qtts_engine_load* and is dropped once.
         unsafe { ffi::qtts_engine_destroy(self.handle) }
+    }
+}
+
+/// Streaming codec decode with carried state; borrows the engine.
+pub struct CodecStream<'a> {
+    handle: *mut ffi::qtts_codec_stream,
+    samples_per_code: usize,
+    _engine: PhantomData<&'a HipTtsEngine>,
+}
+
+impl CodecStream<'_> {
+    /// The next frames' codes (frame-major) -> exactly their samples.
+    pub fn decode(&mut self, codes: &[i32]) -> Result<Vec<f32>> {
+        let mut out = vec![0f32; codes.len() * self.samples_per_code];
+        let mut n = 0usize;
+        // SAFETY: every pointer is valid for the sizes passed.
+        check("qtts_codec_stream_decode", unsafe {
+            ffi::qtts_codec_stream_decode(self.handle, codes.as_ptr(), codes.len(),
+                                          out.as_mut_ptr(), out.len(), &mut n)
+        })?;
+        out.truncate(n);
+        Ok(out)
+    }
+}
+
+impl Drop for CodecStream<'_> {
+    fn drop(&mut self) {
+        // SAFETY: the handle came from qtts_codec_stream_open.
+        unsafe { ffi::qtts_codec_stream_destroy(self.handle) }
     }
 }
 

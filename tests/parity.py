@@ -7,11 +7,12 @@ fragile:
 * greedy tokens: the oracle's top-2 logit gap is at most GAP (1e-2, logit
   units; the north star's bar);
 * sampled tokens: the smallest logit error that could move an edge of the
-  oracle's drawn bucket past its inverse-CDF target is at most CDF_EPS (1e-2
-  logit units; oracle.qtts_oracle.select_margin). With random weights the
-  top-50 distribution is nearly flat (each bucket ~2 % of the mass), so the
-  draw is judged by how much logit error it takes to flip it, not by its
-  distance in probability mass.
+  oracle's drawn bucket past its inverse-CDF target is at most CDF_EPS
+  (oracle.qtts_oracle.select_margin), in logit units: 2e-2, the logit
+  tolerance the north star states and the step tests assert. With random
+  weights the top-50 distribution is nearly flat (each bucket ~2 % of the
+  mass), so many draws are that fragile; the sampler itself is checked bit
+  for bit on the GPU's own logits by test_code_predictor_sampler_exact.
 
 Both margins are what a logit error of bf16 size can move across. The
 fraction of codes under either exemption is reported so near-tie rates are
@@ -20,7 +21,7 @@ visible per configuration.
 import numpy as np
 
 GAP = 1e-2
-CDF_EPS = 1e-2
+CDF_EPS = 2e-2
 
 
 def margins_per_code(records):

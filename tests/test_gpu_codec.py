@@ -140,3 +140,66 @@ def test_server_shell_streams_the_engine(pkg, codec_engine):
     finally:
         srv.shutdown()
         srv.server_close()
+
+
+STREAM_TOL = 2e-3  # chunked vs one-shot: same arithmetic per output, summation order may differ
+
+
+@pytest.mark.parametrize("chunks", [[1, 1, 1, 1, 1, 1, 1, 1], [6, 6, 6, 6, 6], [3, 7, 1, 12, 2]])
+def test_codec_stream_equals_one_shot(codec_engine, codec_model, chunks):
+    """A codec stream with carried state (every causal convolution's history,
+    the pre-transformer's keys / values) decodes chunk by chunk to the samples
+    of one decode of all the frames, and so to the oracle's."""
+    _, oracle = codec_model
+    total = sum(chunks)
+    codes = np.random.default_rng(11 + total).integers(0, 2048, (total, 16)).astype(np.int32)
+    whole = codec_engine.decode_codes(codes.reshape(-1))
+    cs = codec_engine.open_codec_stream(total)
+    try:
+        parts, at = [], 0
+        for n in chunks:
+            out = cs.decode(codes[at: at + n].reshape(-1))
+            assert out.shape == (n * 1920,)
+            parts.append(out)
+            at += n
+    finally:
+        cs.close()
+    got = np.concatenate(parts)
+    err = float(np.max(np.abs(got - whole)))
+    assert err <= STREAM_TOL, err
+    assert float(np.max(np.abs(got - oracle.decode(codes.reshape(-1))))) <= WAVE_TOL
+
+
+def test_codec_stream_capacity_and_errors(pkg, codec_engine):
+    cs = codec_engine.open_codec_stream(4)
+    try:
+        assert cs.decode(np.zeros(3 * 16, np.int32)).size == 3 * 1920
+        with pytest.raises(pkg.InvalidInput, match="holds 4 frames"):
+            cs.decode(np.zeros(2 * 16, np.int32))
+        with pytest.raises(pkg.InvalidInput, match="divisible"):
+            cs.decode(np.zeros(17, np.int32))
+        assert cs.decode([]).size == 0
+        assert cs.decode(np.zeros(16, np.int32)).size == 1920  # the last frame still fits
+    finally:
+        cs.close()
+    with pytest.raises(pkg.InvalidInput, match="max_frames"):
+        codec_engine.open_codec_stream(0)
+
+
+def test_stream_audio_with_carried_state(pkg, codec_engine):
+    """StreamOptions(carry_codec_state=True): each audio chunk decodes only its
+    own frames on the stream's codec state; the chunks join to decode_codes of
+    all the stream's codes."""
+    ids = np.random.default_rng(9).integers(0, 4000, 12)
+    opts = pkg.GenerateOptions(decode_audio=False, do_sample=False, subtalker_dosample=False,
+                               repetition_penalty=1.0, max_frames=11)
+    st = codec_engine.start_stream_from_ids(
+        ids, opts, pkg.StreamOptions(text_lookahead_tokens=8, carry_codec_state=True))
+    chunks = []
+    while (ch := st.next_audio_chunk(4)) is not None:
+        assert ch.samples.shape == (ch.frames * 1920,)
+        chunks.append(ch.samples)
+    codes = st.finish_codes().codes
+    st.close()
+    whole = codec_engine.decode_codes(codes)
+    assert float(np.max(np.abs(np.concatenate(chunks) - whole))) <= STREAM_TOL
