@@ -158,11 +158,57 @@ def measured_peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
+# committed ncu summaries holding a `dram_bytes_per_launch:` line, per trace kind
+TRAFFIC_FILES = {"attn+o+resid": "attention_decode_0p6b.txt", "gemv+swiglu": "gateup_gemv_0p6b.txt",
+                 "cp head+select": "cp_head_select_0p6b.txt"}
+
+
+def trace_bytes(kind, N, K):
+    """Weight bytes one launch of a traced kernel streams (bf16 [N, K]; SwiGLU
+    reads gate and up rows); the attention kernels' KV reads are left out."""
+    if kind == "attn":
+        return 0
+    return N * K * 2 * (2 if kind == "gemv+swiglu" else 1)
+
+
+def traced_frame_kernels(eng, ids, opts):
+    """Per kernel kind of one traced frame of the live graph: launches, chain
+    time per launch (own wait -> next kernel's wait), in-kernel time (own
+    wait -> last exit), share of the frame, bytes and GB/s. Sorted by share."""
+    import dataclasses
+    eng.step_trace_enable(True)
+    try:
+        eng.generate_codes_from_ids(ids, dataclasses.replace(opts, max_frames=10))
+        rows = eng.step_trace()
+    finally:
+        eng.step_trace_enable(False)
+    rows = [r for r in rows if r["wait_ns"] >= 0 and r["exit_ns"] >= 0]
+    if len(rows) < 2:
+        return None
+    span = rows[-1]["exit_ns"] - rows[0]["wait_ns"]
+    agg = {}
+    for i, r in enumerate(rows):
+        chain = (rows[i + 1]["wait_ns"] if i + 1 < len(rows) else r["exit_ns"]) - r["wait_ns"]
+        a = agg.setdefault(r["name"], [0, 0, 0])
+        a[0] += 1
+        a[1] += chain
+        a[2] += r["exit_ns"] - r["wait_ns"]
+    out = []
+    for name, (n, chain, ink) in agg.items():
+        kind, N, K = name.rsplit(" ", 2)[0], int(name.split("N=")[1].split()[0]), int(name.split("K=")[1])
+        b = trace_bytes(kind, N, K)
+        out.append({"kernel": name, "kind": kind, "launches": n, "chain_us": chain / n / 1e3,
+                    "in_kernel_us": ink / n / 1e3, "share": chain / span, "bytes_per_launch": b,
+                    "chain_gbs": b / (chain / n * 1e-9) / 1e9 if b else None})
+    out.sort(key=lambda x: -x["share"])
+    return out
+
+
 def committed_traffic(name="gateup_gemv_0p6b.txt"):
     """DRAM bytes per launch of a kernel from its committed ncu summary
     (`dram_bytes_per_launch:` line), or None."""
     p = ROOT / "profiles" / name
-    if not p.exists():
+    if not name or not p.is_file():
         return None
     for line in p.read_text().splitlines():
         if line.startswith("dram_bytes_per_launch:"):
@@ -581,6 +627,26 @@ def main():
             line_extra["roofline_gateup"] = gateup
         else:
             roofline = gateup
+    frame_kernels = None
+    if batch == 1 and not c.get("stream") and not cp_pass_ms:
+        frame_kernels = traced_frame_kernels(eng, ids, opts)
+        if frame_kernels:
+            top = frame_kernels[0]
+            gbs = top["bytes_per_launch"] / (top["chain_us"] * 1e-6) / 1e9
+            line_extra["roofline_gateup"] = roofline
+            roofline = {"bound": "hbm", "kernel": top["kernel"],
+                        "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": gbs / peaks["hbm_gbs"], "peak_kind": peak_kind,
+                        "bytes_per_launch": top["bytes_per_launch"],
+                        "ms_per_launch": top["chain_us"] * 1e-3,
+                        "in_kernel_ms_per_launch": top["in_kernel_us"] * 1e-3,
+                        "share_of_frame": top["share"],
+                        "timing": "live frame graph, %globaltimer step trace of one frame: per "
+                                  "launch, this kernel's first CTA past its dependency wait to the "
+                                  "next kernel's (the chain time it holds); in-kernel = to its "
+                                  "last CTA's exit",
+                        "traffic": committed_traffic(TRAFFIC_FILES.get(top["kind"], ""))}
+            line_extra["frame_kernels"] = frame_kernels
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()

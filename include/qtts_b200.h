@@ -274,6 +274,24 @@ int32_t qtts_code_predictor(qtts_engine* engine, const float* talker_hidden,
                             const float* semantic_embed, const qtts_generate_options* options,
                             int32_t* tokens_out, float* embedding_sum_out, float* logits_out);
 
+/* Measurement seam (no reference counterpart): the step trace. While
+ * enabled, frame 6 of every generation records for each kernel launch of the
+ * frame graph (%globaltimer, ns after the frame's first kernel entry; -1 when
+ * not recorded) the first CTA's entry, the first and last CTA past the
+ * dependency wait, the last CTA's exit and two in-kernel marks (the input
+ * staged, the dot products done), plus two per-CTA durations since the CTA's
+ * own wait (max over CTAs). Enabling or disabling recaptures the frame
+ * graphs. read: the last traced frame's launches in order (*n of them; at
+ * most cap copied). */
+typedef struct {
+  char name[48];  /* kernel kind and shape, e.g. "gemv+swiglu N=3072 K=1024" */
+  int64_t entry_ns, wait_ns, exit_ns, last_wait_ns, mark4_ns, mark5_ns;
+  uint64_t dur6_ns, dur7_ns;
+} qtts_trace_launch;
+int32_t qtts_step_trace_enable(qtts_engine* engine, int32_t on);
+int32_t qtts_step_trace_read(const qtts_engine* engine, qtts_trace_launch* out, size_t cap,
+                             size_t* n);
+
 /* Measurement hook (no reference counterpart): device time (CUDA events on
  * the engine stream, inside the frame graph) of the persistent CodePredictor
  * pass of the last frame the last generation call ran, and the weight bytes

@@ -111,6 +111,19 @@ def argmax_device(logits: np.ndarray) -> int:
     return best_i
 
 
+def _order_margin(vals, j: int) -> float:
+    """Half the logit gap between the drawn candidate j and its neighbours in
+    the sorted order: a logit error of that size can swap j with a neighbour,
+    which hands j's bucket of the CDF to the other token."""
+    best = float("inf")
+    v = np.asarray(vals, dtype=np.float64)
+    if j > 0:
+        best = min(best, (v[j - 1] - v[j]) / 2.0)
+    if j + 1 < v.size:
+        best = min(best, (v[j] - v[j + 1]) / 2.0)
+    return best
+
+
 def _cdf_margin(probs, j: int, target0, temperature: float) -> float:
     """How robust an inverse-CDF draw is, in logit units: the smallest logit
     error that could move an edge of the drawn bucket j past the target.
@@ -159,7 +172,12 @@ def sample_topk_device(logits: np.ndarray, top_k: int, temperature: float, u: np
             break
         target = np.float32(target - probs[i])
     tok = int(order[pick])
-    return (tok, _cdf_margin(probs, pick, target0, temperature)) if with_margin else tok
+    if not with_margin:
+        return tok
+    # neighbours include the first candidate past top_k (a swap there changes
+    # the candidate set when the draw is the last bucket)
+    return tok, min(_cdf_margin(probs, pick, target0, temperature),
+                    _order_margin(vals[: kept + 1], pick))
 
 
 def sample_cpu(logits: np.ndarray, cfg: SamplingConfig, rng, with_margin: bool = False):
@@ -172,6 +190,7 @@ def sample_cpu(logits: np.ndarray, cfg: SamplingConfig, rng, with_margin: bool =
     vals = logits[idx].astype(np.float32)
     order = np.lexsort((idx, -vals.astype(np.float64)))  # stable: ties keep index order
     idx, vals = idx[order], vals[order]
+    sorted_vals = vals
     if 0 < cfg.top_k < idx.size:
         idx, vals = idx[: cfg.top_k], vals[: cfg.top_k]
     mx = vals[0]
@@ -206,7 +225,10 @@ def sample_cpu(logits: np.ndarray, cfg: SamplingConfig, rng, with_margin: bool =
             break
         target = np.float32(target - p)
     tok = int(idx[pick])
-    return (tok, _cdf_margin(probs, pick, target0, cfg.temperature)) if with_margin else tok
+    if not with_margin:
+        return tok
+    return tok, min(_cdf_margin(probs, pick, target0, cfg.temperature),
+                    _order_margin(sorted_vals[: len(idx) + 1], pick))
 
 
 def select(logits: np.ndarray, cfg: SamplingConfig, rng) -> int:

@@ -6,6 +6,8 @@
 // the transposed convolutions.
 #pragma once
 
+#include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -55,6 +57,31 @@ struct CodecConvArgs {
 };
 
 cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream);
+
+// A convolution weight [rows][ci * taps] (fp32, tap fastest; rows
+// phase-major for transposed convolutions) repacked for the tensor-core
+// path: K tap-major (k = tap * cip + channel, channels zero-padded to cip, a
+// multiple of 64, so one 64-wide K step reads one input column) and split
+// into bf16 hi + lo, with the TMA maps of both halves.
+struct CodecTcWeight {
+  __nv_bfloat16* hi = nullptr;
+  __nv_bfloat16* lo = nullptr;
+  CUtensorMap mh, ml;
+  int rows = 0, ci = 0, taps = 0, cip = 0;
+};
+inline int codec_tc_padded_channels(int ci) { return (ci + 63) / 64 * 64; }
+cudaError_t configure_codec_tc();
+// Repacks and splits the device weight W into hi / lo (caller-allocated,
+// rows * taps * codec_tc_padded_channels(ci) each) and builds the maps.
+cudaError_t codec_tc_prepare(const float* W, int rows, int ci, int taps, __nv_bfloat16* hi,
+                             __nv_bfloat16* lo, CodecTcWeight* out, cudaStream_t stream);
+// Whether codec_conv_tc computes this convolution with this weight.
+bool codec_tc_supported(const CodecConvArgs& a, const CodecTcWeight& w);
+// codec_conv on the tensor cores (tcgen05): bf16 hi + lo splits of the weight
+// and of the transformed input, fp32 accumulation; `err` receives a nonzero
+// code if a pipeline wait times out.
+cudaError_t codec_conv_tc(const CodecConvArgs& a, const CodecTcWeight& w, int* err,
+                          cudaStream_t stream);
 
 // first[t][d] = cb_first[code0][d]; rest[t][d] = sum_{g=1..15} cb_rest[g-1][code_g][d]
 // (codes taken modulo the codebook size), then

@@ -26,6 +26,7 @@
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "codec.h"
@@ -396,6 +397,46 @@ class Codec {
     snake("decoder.decoder.5", kFinal, &fa_, &fb_);
     f_w_ = up(get("decoder.decoder.6.conv.weight", {1, kFinal, 7}));
     f_b_ = vec("decoder.decoder.6.conv.bias", 1);
+    err_ = arena_.alloc<int>(1);
+    // Tensor-core copies (bf16 hi + lo) of every convolution weight with at
+    // least 64 output channels (QTTS_CODEC_TC=0: CUDA-core kernel only).
+    const char* tz = std::getenv("QTTS_CODEC_TC");
+    if (!(tz && tz[0] == '0') && tc_available()) {
+      QCK(cudaDeviceSynchronize());  // the uploads above have landed
+      auto tcw = [&](const float* w, int rows, int ci, int taps) {
+        if (rows < 64) return;
+        CodecTcWeight t;
+        const size_t n = (size_t)rows * taps * codec_tc_padded_channels(ci);
+        __nv_bfloat16* hi = arena_.alloc<__nv_bfloat16>(n);
+        __nv_bfloat16* lo = arena_.alloc<__nv_bfloat16>(n);
+        QCK(codec_tc_prepare(w, rows, ci, taps, hi, lo, &t, stream_));
+        tc_w_[w] = t;
+      };
+      const int qo = kHeads * kHeadDim;
+      tcw(pre_w_, kPre, kProj, 3);
+      tcw(in_w_, kHidden, kPre, 1);
+      tcw(out_w_, kPre, kHidden, 1);
+      for (const Layer& L : layers_) {
+        tcw(L.wqkv, 3 * qo, kHidden, 1);
+        tcw(L.wo, kHidden, qo, 1);
+        tcw(L.wgu, 2 * kInter, kHidden, 1);
+        tcw(L.wdown, kHidden, kInter, 1);
+      }
+      for (const Up& U : ups_) {
+        tcw(U.tw, 2 * kUp, kUp, 1);
+        tcw(U.pw1, kCnx, kUp, 1);
+        tcw(U.pw2, kUp, kCnx, 1);
+      }
+      tcw(d0_w_, kDec0, kPre, 7);
+      for (int b = 0; b < 4; ++b) {
+        const int cin = kBlocks[b][0], cout = kBlocks[b][1], s = kBlocks[b][2];
+        tcw(blocks_[b].tw, s * cout, cin, 2);
+        for (const Res& R : blocks_[b].res) {
+          tcw(R.c1, cout, cout, 7);
+          tcw(R.c2, cout, cout, 1);
+        }
+      }
+    }
     QCK(cudaStreamSynchronize(stream_));
   }
   ~Codec() { release(); }
@@ -474,6 +515,7 @@ class Codec {
     ensure(frames);
     const int T = frames;
     launches = 0;
+    tc_launches = 0;
     int sc = 0;  // next causal convolution's state slot
     // x with its carried history in front (ws_.cat), or x alone (one-shot)
     auto hist = [&](const float* x, int C, int n, int* h) -> const float* {
@@ -578,7 +620,19 @@ class Codec {
 
  public:
   const float* out() const { return ws_.wav; }
-  size_t launches = 0;  // kernels enqueued by the last decode
+  size_t launches = 0;     // kernels enqueued by the last decode
+  size_t tc_launches = 0;  // of which tensor-core convolutions
+  // Throws if a tensor-core convolution reported a pipeline timeout (call
+  // after the stream has drained); the status is cleared.
+  void check_status() {
+    int e = 0;
+    QCK(cudaMemcpy(&e, err_, sizeof e, cudaMemcpyDeviceToHost));
+    if (e) {
+      QCK(cudaMemset(err_, 0, sizeof e));
+      throw QttsError(QTTS_ERR_CUDA, "codec tensor-core convolution: pipeline wait " +
+                                         std::to_string(e) + " timed out");
+    }
+  }
   int32_t* codes_buffer(int frames) {
     ensure(frames);
     return ws_.codes;
@@ -633,7 +687,13 @@ class Codec {
     CodecConvArgs a{x,   ci,     lin,    w,      w_phase_stride, bias,  co,     taps, dil,
                     pad, act,    act_a,  act_b,  up_off,         y,     ostride, nphase, epi,
                     resid, rscale, out_a, out_b, y2, hist};
-    QCK(codec_conv(a, stream_));
+    auto it = tc_w_.find(w);
+    if (it != tc_w_.end() && codec_tc_supported(a, it->second)) {
+      QCK(codec_conv_tc(a, it->second, err_, stream_));
+      ++tc_launches;
+    } else {
+      QCK(codec_conv(a, stream_));
+    }
     ++launches;
   }
 
@@ -700,6 +760,8 @@ class Codec {
         *f_b_ = nullptr;
   int cap_ = 0;
   size_t ws_bytes_ = 0;
+  int* err_ = nullptr;  // tensor-core pipeline status (nonzero: a wait ran out)
+  std::unordered_map<const float*, CodecTcWeight> tc_w_;
 };
 
 class Engine {
@@ -751,8 +813,9 @@ class Engine {
   std::vector<int> pinned_ids_storage;
 
   std::map<SampleKey, cudaGraphExec_t> graphs;
-  // Persistent CodePredictor pass (one cooperative launch per frame; the
-  // per-op kernels when QTTS_CP_PASS=0 or the shape is unsupported).
+  // Persistent CodePredictor pass (one cooperative launch per frame), opt-in
+  // with QTTS_CP_PASS=1: measured slower than the per-op kernels (343 vs 439
+  // frames/s, 0.6B sampled), which stay the default.
   bool use_cp_pass = false;
   int cp_grid = 0;
   CpOp* cp_ops = nullptr;
@@ -836,12 +899,14 @@ class Engine {
            nullptr, 1, c.hidden, c.intermediate, EPI_RESID, halt);
   }
 
-  // ---- step trace (QTTS_STEP_TRACE=<file>) ----
+  // ---- step trace (QTTS_STEP_TRACE=<file>, or qtts_step_trace_enable) ----
   // Frame `trace_frame` of each run records, per launch, the first CTA entry,
   // the first CTA past its dependency wait and the last CTA exit.
   std::string step_trace_path;
   unsigned long long* step_trace = nullptr;
   static constexpr int kTraceCap = 4096;
+  bool trace_on = false;
+  std::vector<qtts_trace_launch> trace_rows;  // the last traced frame
   bool trace_capture = false;
   std::vector<std::string> trace_names;
   size_t trace_frame = 6;
@@ -1042,6 +1107,7 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   QCK(configure_kernels());
   QCK(configure_cp_pass());
   QCK(configure_tc_kernels());
+  QCK(configure_codec_tc());
   QCK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   QCK(cudaEventCreate(&ev0));
   QCK(cudaEventCreate(&ev1));
@@ -1178,9 +1244,10 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   tp_b = arena.alloc<float>((size_t)tp_rows * text_inter);
   tp_c = arena.alloc<float>((size_t)tp_rows * T.hidden);
   {
+    step_trace = arena.alloc<unsigned long long>(8 * (size_t)kTraceCap);
     if (const char* tp = std::getenv("QTTS_STEP_TRACE")) {
       step_trace_path = tp;
-      step_trace = arena.alloc<unsigned long long>(8 * (size_t)kTraceCap);
+      trace_on = true;
     }
     if (const char* cr = std::getenv("QTTS_CRUMBS"); cr && cr[0] == '1') {
       QCK(cudaHostAlloc(&crumbs_host, 64, cudaHostAllocMapped));
@@ -1193,7 +1260,7 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
     fuse_attn_o = !(fz && fz[0] == '0');
     const char* cz = std::getenv("QTTS_CP_PASS");
     cp_grid = cp_pass_grid(dev);
-    use_cp_pass = !(cz && cz[0] == '0') && cp_grid > 0 &&
+    use_cp_pass = cz && cz[0] == '1' && cp_grid > 0 &&
                   cp_pass_supported(C.hidden, C.intermediate, C.q_heads, C.kv_heads, T.hidden,
                                     C.vocab, cp_grid) &&
                   C.groups <= kCpPositions;
@@ -1232,6 +1299,7 @@ size_t Engine::decode_codes(const int32_t* codes, size_t n_codes, float* out, si
   QCK(cudaEventRecord(ev1, stream));
   QCK(cudaMemcpyAsync(out, codec->out(), samples * sizeof(float), cudaMemcpyDeviceToHost, stream));
   QCK(cudaStreamSynchronize(stream));
+  codec->check_status();
   QCK(cudaEventElapsedTime(&last_decode_ms, ev0, ev1));
   return samples;
 }
@@ -1533,7 +1601,7 @@ void Engine::build_cp_pass() {
   cp_err = arena.alloc<int>(2);
   QCK(cudaMemset(cp_counter, 0, sizeof(unsigned long long)));
   QCK(cudaMemset(cp_err, 0, 2 * sizeof(int)));
-  if (step_trace) cp_trace = arena.alloc<unsigned long long>(kCpTraceSlots * ops.size());
+  cp_trace = arena.alloc<unsigned long long>(kCpTraceSlots * ops.size());
 }
 
 void Engine::launch_cp(const SampleKey& k, float* dbg_logits, float* emb_sum_out) {
@@ -1581,7 +1649,7 @@ cudaGraphExec_t Engine::frame_graph(const SampleKey& k) {
   if (it != graphs.end()) return it->second;
   cudaGraph_t g = nullptr;
   const size_t before = launches;
-  trace_capture = step_trace != nullptr && !k.last;
+  trace_capture = trace_on && !k.last;
   if (trace_capture) trace_names.clear();
   QCK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
   try {
@@ -1773,7 +1841,7 @@ size_t Engine::run_frames(size_t n) {
   bool traced = false;
   for (size_t i = 0; i < n; ++i) {
     const bool is_last = begin + i + 1 >= seq_max_frames;
-    const bool trace_now = step_trace && !is_last && begin + i == trace_frame;
+    const bool trace_now = trace_on && !is_last && begin + i == trace_frame;
     if (trace_now) {
       QCK(cudaMemsetAsync(step_trace, 0xff, 2 * kTraceCap * sizeof(unsigned long long), stream));
       QCK(cudaMemsetAsync(step_trace + 2 * kTraceCap, 0,
@@ -1807,18 +1875,35 @@ void Engine::dump_step_trace() {
   std::vector<unsigned long long> t(8 * (size_t)kTraceCap);
   QCK(cudaMemcpy(t.data(), step_trace, t.size() * sizeof(unsigned long long),
                  cudaMemcpyDeviceToHost));
+  unsigned long long t0 = ~0ull;
+  for (size_t i = 1; i <= trace_names.size(); ++i) t0 = std::min(t0, t[i]);
+  auto rel = [&](unsigned long long v) {
+    return v == ~0ull || v == 0 ? -1LL : (long long)(v - t0);
+  };
+  trace_rows.assign(trace_names.size(), qtts_trace_launch{});
+  for (size_t i = 1; i <= trace_names.size(); ++i) {
+    qtts_trace_launch& r = trace_rows[i - 1];
+    std::snprintf(r.name, sizeof r.name, "%s", trace_names[i - 1].c_str());
+    r.entry_ns = rel(t[i]);
+    r.wait_ns = rel(t[kTraceCap + i]);
+    r.exit_ns = rel(t[2 * kTraceCap + i]);
+    r.last_wait_ns = rel(t[3 * kTraceCap + i]);
+    r.mark4_ns = rel(t[4 * kTraceCap + i]);
+    r.mark5_ns = rel(t[5 * kTraceCap + i]);
+    r.dur6_ns = t[6 * kTraceCap + i];
+    r.dur7_ns = t[7 * kTraceCap + i];
+  }
+  if (step_trace_path.empty()) return;
   FILE* f = std::fopen(step_trace_path.c_str(), "w");
   if (!f) return;
   std::fprintf(f, "# id entry wait exit last_wait mark4 mark5 (ns after the first entry) "
                   "dur6 dur7 (ns after a CTA's own wait, max over CTAs) name\n");
-  unsigned long long t0 = ~0ull;
-  for (size_t i = 1; i <= trace_names.size(); ++i) t0 = std::min(t0, t[i]);
-  for (size_t i = 1; i <= trace_names.size(); ++i) {
-    auto rel = [&](unsigned long long v) { return v == ~0ull || v == 0 ? -1LL : (long long)(v - t0); };
-    std::fprintf(f, "%zu %lld %lld %lld %lld %lld %lld %llu %llu %s\n", i, rel(t[i]),
-                 rel(t[kTraceCap + i]), rel(t[2 * kTraceCap + i]), rel(t[3 * kTraceCap + i]),
-                 rel(t[4 * kTraceCap + i]), rel(t[5 * kTraceCap + i]), t[6 * kTraceCap + i],
-                 t[7 * kTraceCap + i], trace_names[i - 1].c_str());
+  for (size_t i = 0; i < trace_rows.size(); ++i) {
+    const qtts_trace_launch& r = trace_rows[i];
+    std::fprintf(f, "%zu %lld %lld %lld %lld %lld %lld %llu %llu %s\n", i + 1,
+                 (long long)r.entry_ns, (long long)r.wait_ns, (long long)r.exit_ns,
+                 (long long)r.last_wait_ns, (long long)r.mark4_ns, (long long)r.mark5_ns,
+                 (unsigned long long)r.dur6_ns, (unsigned long long)r.dur7_ns, r.name);
   }
   std::fclose(f);
   if (!cp_trace) return;
@@ -2951,6 +3036,30 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
       QCK(cudaMemcpy(logits_out, e.dbg_logits, (size_t)na * C.vocab * 4, cudaMemcpyDeviceToHost));
     e.seq_ended = true;  // the talker state was not advanced: no stream may continue
     ++e.seq_id;
+  });
+}
+
+int32_t qtts_step_trace_enable(qtts_engine* h, int32_t on) {
+  return guard([&] {
+    Engine& e = engine_of(h);
+    if (e.trace_on == (on != 0)) return;
+    e.trace_on = on != 0;
+    // the frame graphs carry the trace ids fixed at capture: recapture
+    QCK(cudaStreamSynchronize(e.stream));
+    for (auto& kv : e.graphs) cudaGraphExecDestroy(kv.second);
+    e.graphs.clear();
+    e.trace_rows.clear();
+  });
+}
+
+int32_t qtts_step_trace_read(const qtts_engine* h, qtts_trace_launch* out, size_t cap,
+                             size_t* n) {
+  return guard([&] {
+    need(h, "engine");
+    need(n, "n");
+    const Engine& e = *h->e;
+    *n = e.trace_rows.size();
+    if (out) std::memcpy(out, e.trace_rows.data(), std::min(cap, *n) * sizeof(qtts_trace_launch));
   });
 }
 

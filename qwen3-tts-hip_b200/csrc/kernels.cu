@@ -242,6 +242,11 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
 #pragma unroll
     for (int j = 0; j < KCH; ++j) w[r][j] = ldg_stream(src + j * 256, pol);
   }
+  // A branch (never taken) between the weight loads and the dependency wait
+  // keeps the two in separate basic blocks, so the SASS scheduler cannot sink
+  // the loads past the wait: with both in one block the loads were issued
+  // after it and the decode frame measured 9% slower (390 vs 427 frames/s).
+  if (a.K < 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.W) : "memory");
   pdl_wait();
   trace_mark(a.trace_id, 1);
   const unsigned long long tw = trace_clock(a.trace_id);

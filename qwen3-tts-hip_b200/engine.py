@@ -78,6 +78,12 @@ class _Chunk(C.Structure):
                 ("ended_by_eos", C.c_int32), ("status", C.c_int32)]
 
 
+class _TraceLaunch(C.Structure):
+    _fields_ = [("name", C.c_char * 48), ("entry_ns", C.c_int64), ("wait_ns", C.c_int64),
+                ("exit_ns", C.c_int64), ("last_wait_ns", C.c_int64), ("mark4_ns", C.c_int64),
+                ("mark5_ns", C.c_int64), ("dur6_ns", C.c_uint64), ("dur7_ns", C.c_uint64)]
+
+
 class _Info(C.Structure):
     _fields_ = [("hidden", C.c_uint32), ("vocab", C.c_uint32), ("cp_hidden", C.c_uint32),
                 ("cp_vocab", C.c_uint32), ("num_code_groups", C.c_uint32),
@@ -129,6 +135,8 @@ SIGNATURES = {
     "qtts_code_predictor": (C.c_int32, [_P, _F, _F, C.POINTER(_Options), _I32, _F, _F]),
     "qtts_selftest_device_wait": (C.c_int32, [_P, C.c_uint32]),
     "qtts_last_cp_pass_timing": (C.c_int32, [_P, _F, C.POINTER(C.c_double)]),
+    "qtts_step_trace_enable": (C.c_int32, [_P, C.c_int32]),
+    "qtts_step_trace_read": (C.c_int32, [_P, C.POINTER(_TraceLaunch), C.c_size_t, _SZ]),
     "qtts_last_timings": (C.c_int32, [_P, _F, _F, _SZ]),
     "qtts_last_launch_count": (C.c_int32, [_P, _SZ]),
     "qtts_profile_projection": (C.c_int32, [_P, C.c_int32, C.c_int32, _F, C.POINTER(C.c_double)]),
@@ -576,6 +584,21 @@ class HipTtsEngine:
             return None
         _check(st)
         return ms.value, nb.value
+
+    def step_trace_enable(self, on: bool) -> None:
+        """Step trace of frame 6 of every generation (recaptures the graphs)."""
+        _check(lib().qtts_step_trace_enable(self._h, int(bool(on))))
+
+    def step_trace(self) -> list:
+        """The last traced frame's launches in order: dicts of name and the
+        globaltimer stamps (ns after the frame's first entry; -1 = none)."""
+        n = C.c_size_t()
+        _check(lib().qtts_step_trace_read(self._h, None, 0, C.byref(n)))
+        rows = (_TraceLaunch * max(1, n.value))()
+        _check(lib().qtts_step_trace_read(self._h, rows, n.value, C.byref(n)))
+        keys = [f for f, _ in _TraceLaunch._fields_[1:]]
+        return [dict(name=r.name.decode(), **{k: int(getattr(r, k)) for k in keys})
+                for r in rows[: n.value]]
 
     def selftest_device_wait(self, limit_us: int) -> None:
         """Runs a bounded device wait that nothing satisfies; raises the

@@ -56,6 +56,20 @@ pub mod ffi {
 
     #[repr(C)]
     #[derive(Clone, Copy, Debug)]
+    pub struct qtts_trace_launch {
+        pub name: [c_char; 48],
+        pub entry_ns: i64,
+        pub wait_ns: i64,
+        pub exit_ns: i64,
+        pub last_wait_ns: i64,
+        pub mark4_ns: i64,
+        pub mark5_ns: i64,
+        pub dur6_ns: u64,
+        pub dur7_ns: u64,
+    }
+
+    #[repr(C)]
+    #[derive(Clone, Copy, Debug)]
     pub struct qtts_generate_options {
         pub speaker: *const c_char,
         pub language: *const c_char,
@@ -213,6 +227,9 @@ pub mod ffi {
                                    semantic_embed: *const f32,
                                    options: *const qtts_generate_options, tokens_out: *mut i32,
                                    embedding_sum_out: *mut f32, logits_out: *mut f32) -> i32;
+        pub fn qtts_step_trace_enable(engine: *mut qtts_engine, on: i32) -> i32;
+        pub fn qtts_step_trace_read(engine: *const qtts_engine, out: *mut qtts_trace_launch,
+                                    cap: usize, n: *mut usize) -> i32;
         pub fn qtts_last_cp_pass_timing(engine: *const qtts_engine, ms: *mut f32,
                                         weight_bytes: *mut f64) -> i32;
         pub fn qtts_selftest_device_wait(engine: *mut qtts_engine, limit_us: u32) -> i32;
