@@ -421,43 +421,57 @@ __device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, flo
       *reinterpret_cast<uint2*>(kv_ptr(at.kv, at.layer, 0, g, pos) + d0) = kcur;
       *reinterpret_cast<uint2*>(kv_ptr(at.kv, at.layer, 1, g, pos) + d0) = vcur;
     }
-    float d[2][kCpFusedPositions];
+    // partial scores of this lane's 4 dims: d[16 j + p] for q head j, position p
+    float d[2 * kCpFusedPositions];
 #pragma unroll
     for (int p = 0; p < kCpFusedPositions; ++p) {
       const uint2 ku = p < pos ? kc[p] : kcur;
       const float k0 = bf16lo(ku.x), k1 = bf16hi(ku.x), k2 = bf16lo(ku.y), k3 = bf16hi(ku.y);
 #pragma unroll
       for (int j = 0; j < 2; ++j)
-        d[j][p] = (q[j].x * at.scale) * k0 + (q[j].y * at.scale) * k1 +
-                  (q[j].z * at.scale) * k2 + (q[j].w * at.scale) * k3;
+        d[kCpFusedPositions * j + p] = (q[j].x * at.scale) * k0 + (q[j].y * at.scale) * k1 +
+                                       (q[j].z * at.scale) * k2 + (q[j].w * at.scale) * k3;
     }
     trace_dur(trace_id, 6, tw);  // cached rows and projections in registers
+    // Reduce-scatter over the warp (31 shuffles instead of 32 x 5): at each
+    // step a lane keeps the half of its values that its lane-id bit selects
+    // and adds its partner's copy of that half, so lane l ends with the full
+    // score of pair l (q head l / 16, position l % 16).
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
+    for (int w = 16; w >= 1; w >>= 1) {
+      const bool upper = (lane & w) != 0;
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
+      for (int i = 0; i < w; ++i) {
+        const float send = upper ? d[i] : d[i + w];
+        const float keep = upper ? d[i + w] : d[i];
+        d[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+      }
+    }
+    // softmax over the positions 0..pos of each q head (one half-warp each)
+    const int p_own = lane & (kCpFusedPositions - 1);
+    const float sc = p_own < T ? d[0] : -INFINITY;
+    float m = sc;
 #pragma unroll
-        for (int p = 0; p < kCpFusedPositions; ++p)
-          d[j][p] += __shfl_xor_sync(0xffffffffu, d[j][p], o);
+    for (int o = kCpFusedPositions / 2; o > 0; o >>= 1)
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float e = p_own < T ? expf(sc - m) : 0.f;
+    float l = e;
+#pragma unroll
+    for (int o = kCpFusedPositions / 2; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    const float wgt = e / l;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      float m = -INFINITY;
-#pragma unroll
-      for (int p = 0; p < kCpFusedPositions; ++p)
-        if (p < T) m = fmaxf(m, d[j][p]);
-      float l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int p = 0; p < kCpFusedPositions; ++p) {
+        const float wp = __shfl_sync(0xffffffffu, wgt, kCpFusedPositions * j + p);
         if (p >= T) continue;
-        const float e = expf(d[j][p] - m);
         const uint2 vu = p < pos ? vc[p] : vcur;
-        l += e;
-        acc[0] = fmaf(e, bf16lo(vu.x), acc[0]); acc[1] = fmaf(e, bf16hi(vu.x), acc[1]);
-        acc[2] = fmaf(e, bf16lo(vu.y), acc[2]); acc[3] = fmaf(e, bf16hi(vu.y), acc[3]);
+        acc[0] = fmaf(wp, bf16lo(vu.x), acc[0]); acc[1] = fmaf(wp, bf16hi(vu.x), acc[1]);
+        acc[2] = fmaf(wp, bf16lo(vu.y), acc[2]); acc[3] = fmaf(wp, bf16hi(vu.y), acc[3]);
       }
-      const float il = 1.0f / l;
       *reinterpret_cast<float4*>(xs + (2 * g + j) * kHeadDim + d0) =
-          make_float4(acc[0] * il, acc[1] * il, acc[2] * il, acc[3] * il);
+          make_float4(acc[0], acc[1], acc[2], acc[3]);
     }
   }
   trace_dur(trace_id, 7, tw);  // warp 0's heads done

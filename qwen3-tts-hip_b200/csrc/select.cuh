@@ -139,6 +139,9 @@ struct Selector {
   // tie at the threshold; the caller then runs the general path.
   static constexpr int kFastK = 64;
   static constexpr int kFastCand = 128;
+  // PER: keys per thread (V <= PER * 256); the CodePredictor's 2048-entry
+  // vocab needs 8, the talker's 3072 needs 16.
+  template <int PER>
   __device__ __forceinline__ int select_fast(int V, const SampleCfg& cfg, float u) {
     __shared__ unsigned s_wc[2][kSelThreads / 32][16];
     __shared__ int s_wn[kSelThreads / 32];
@@ -148,7 +151,7 @@ struct Selector {
     __shared__ __align__(16) float s_prob[kFastK];
     __shared__ int s_res, s_cnt;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr int kPer = kSelMaxVocab / kSelThreads;
+    constexpr int kPer = PER;
     const int K = min(cfg.top_k, V);
     unsigned key[kPer];
 #pragma unroll
@@ -346,7 +349,8 @@ struct Selector {
     float u_dev = 0.f;
     if (device_path && tid == 0) u_dev = rng.next();
     if (device_path && min(cfg.top_k, V) <= kFastK) {
-      const int r = select_fast(V, cfg, u_dev);
+      const int r = V <= 8 * kSelThreads ? select_fast<8>(V, cfg, u_dev)
+                                         : select_fast<kSelMaxVocab / kSelThreads>(V, cfg, u_dev);
       if (r >= 0) return r;
     }
     stamp(0);
