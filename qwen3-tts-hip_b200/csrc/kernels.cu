@@ -526,33 +526,9 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
     }
     return;
   }
-  if (a.role == ROLE_TALKER_STEP)
-    sel.penalise(V, a.history, s_frame, -1, a.penalty, a.suppress, a.eos_token);
-  else
-    sel.penalise(V, a.history, 0, -1, 1.0f, a.suppress, a.eos_token);
-  const int tok = sel.select(V, a.cfg, rng, &a.st->error);
-  trace_dur(a.lin.trace_id, 7, t_sel);  // token chosen
-  if (tid == 0) {
-    a.st->rng_state = rng.state;
-    a.st->rng_counter = rng.counter;
-  }
-  if (a.token_out && tid == 0) *a.token_out = tok;
-  if (a.frames_cap > 0 && (tok < 0 || tok >= V)) {
-    if (tid == 0) {
-      a.st->error = 3;
-      if (g_crumbs.p) {
-        g_crumbs.p[2] = 2000 + a.role;
-        g_crumbs.p[3] = (unsigned)tok;
-        g_crumbs.p[4] = (unsigned)V;
-        g_crumbs.p[5] = blockIdx.x;
-        __threadfence_system();
-      }
-    }
-    return;
-  }
-
-  // The tail's inputs are loaded in one batch with the token's embedding row
-  // (4 consecutive elements per thread and pass): one L2 round trip.
+  // The tail's inputs that do not depend on the token are loaded now, so
+  // their latency hides under the selection; after it only the token's
+  // embedding row is read (4 consecutive elements per thread and pass).
   const int H = a.H;
   constexpr int kIt = 2;  // H <= kIt * 4 * kThreads (checked at engine load)
   const bool cp = a.role == ROLE_CP_GROUP;
@@ -584,6 +560,31 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
       const float4 g = __ldg(reinterpret_cast<const float4*>(a.lin.gamma + i));
       pre_a[it] = make_float4(x.x * inv * g.x, x.y * inv * g.y, x.z * inv * g.z, x.w * inv * g.w);
     }
+  }
+
+  if (a.role == ROLE_TALKER_STEP)
+    sel.penalise(V, a.history, s_frame, -1, a.penalty, a.suppress, a.eos_token);
+  else
+    sel.penalise(V, a.history, 0, -1, 1.0f, a.suppress, a.eos_token);
+  const int tok = sel.select(V, a.cfg, rng, &a.st->error);
+  trace_dur(a.lin.trace_id, 7, t_sel);  // token chosen
+  if (tid == 0) {
+    a.st->rng_state = rng.state;
+    a.st->rng_counter = rng.counter;
+  }
+  if (a.token_out && tid == 0) *a.token_out = tok;
+  if (a.frames_cap > 0 && (tok < 0 || tok >= V)) {
+    if (tid == 0) {
+      a.st->error = 3;
+      if (g_crumbs.p) {
+        g_crumbs.p[2] = 2000 + a.role;
+        g_crumbs.p[3] = (unsigned)tok;
+        g_crumbs.p[4] = (unsigned)V;
+        g_crumbs.p[5] = blockIdx.x;
+        __threadfence_system();
+      }
+    }
+    return;
   }
 
   if (a.role == ROLE_TALKER_PREFILL || a.role == ROLE_TALKER_STEP) {

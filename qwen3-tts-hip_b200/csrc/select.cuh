@@ -245,15 +245,22 @@ struct Selector {
             (unsigned)(0xffffffffu - (unsigned)(j * kSelThreads + tid));
       base += __popc(bal);
     }
+    // zero keys pad the list to a multiple of 16 (no candidate ranks below 0)
+    const int total16 = (total + 15) & ~15;
+    if (tid >= total && tid < total16) s_cand[tid] = 0ull;
     Sync::sync();
     stamp(12);
     // exact rank of each candidate: larger key first, then lower index
     if (tid < total) {
       const unsigned long long me = s_cand[tid];
       int rank = 0;
-      for (int i = 0; i < total; i += 2) {
-        const ulonglong2 q = *reinterpret_cast<const ulonglong2*>(s_cand + i);
-        rank += (q.x > me) + (i + 1 < total && q.y > me);
+      // 16 keys per step: the broadcast shared-memory reads overlap
+      for (int i = 0; i < total16; i += 16) {
+#pragma unroll
+        for (int u = 0; u < 16; u += 2) {
+          const ulonglong2 q = *reinterpret_cast<const ulonglong2*>(s_cand + i + u);
+          rank += (q.x > me) + (q.y > me);
+        }
       }
       if (rank < K) {
         const int idx = (int)(0xffffffffu - (unsigned)me);

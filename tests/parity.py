@@ -6,22 +6,22 @@ fragile:
 
 * greedy tokens: the oracle's top-2 logit gap is at most GAP (1e-2, logit
   units; the north star's bar);
-* sampled tokens: the smallest logit error that could move an edge of the
-  oracle's drawn bucket past its inverse-CDF target is at most CDF_EPS
-  (oracle.qtts_oracle.select_margin), in logit units: 2e-2, the logit
-  tolerance the north star states and the step tests assert. With random
-  weights the top-50 distribution is nearly flat (each bucket ~2 % of the
-  mass), so many draws are that fragile; the sampler itself is checked bit
-  for bit on the GPU's own logits by test_code_predictor_sampler_exact.
+* sampled tokens: the smallest logit error that could change the oracle's
+  draw is at most CDF_EPS (oracle.qtts_oracle.select_margin, logit units):
+  an edge of the drawn bucket crossing the inverse-CDF target, or the drawn
+  candidate swapping order with a neighbour. CDF_EPS = 5e-3: every differing
+  sampled code measured at full size (0.6B and 1.7B, 240 frames, LCG and
+  Philox, streaming, 16-request batches) had a margin below 3.4e-3. With
+  random weights the top-50 distribution is nearly flat, so a good share of
+  draws is that fragile; the sampler itself is checked bit for bit on the
+  GPU's own logits by test_code_predictor_sampler_exact.
 
-Both margins are what a logit error of bf16 size can move across. The
-fraction of codes under either exemption is reported so near-tie rates are
-visible per configuration.
+The fraction of codes under the exemption is printed per configuration.
 """
 import numpy as np
 
 GAP = 1e-2
-CDF_EPS = 2e-2
+CDF_EPS = 5e-3
 
 
 def margins_per_code(records):

@@ -1,10 +1,11 @@
 """Parity of the sm_100a path (through the C ABI) against the CPU oracle.
 
 Bar: tokens identical wherever the oracle's top-2 logit
-gap exceeds 1e-2; logits within 2e-2 max-abs; sampled runs in the reference's
-LCG draw order reproduce the oracle's tokens. Rollouts are checked with the
-oracle teacher-forced along the GPU's own codes, so a near-tie does not make
-later frames incomparable.
+gap exceeds 1e-2; logits within 2e-2 max-abs; sampled runs (in the
+reference's LCG draw order, and Philox) reproduce the oracle's tokens wherever
+the draw is robust to a 5e-3 logit error (tests/parity.py). Rollouts are
+checked with the oracle teacher-forced along the GPU's own codes, so a
+near-tie does not make later frames incomparable.
 """
 import json
 import shutil
@@ -470,7 +471,7 @@ for shape, d in [('tiny', {str(model_dirs['tiny'])!r}), ('tiny_proj', {str(model
     sc = O.SamplingConfig(True, 50, 1.0, 0.9)
     codes2, _, recs2 = m.rollout(pre, tr, pad, 12, sc, sc, penalty=1.05, seed=4, forced_codes=out2.codes)
     ms = [x for r in recs2 for x in [r.talker_margin] + r.cp_margins]
-    bad2 = [i for i, (a, b) in enumerate(zip(out2.codes, codes2)) if a != b and ms[i] > 2e-2]
+    bad2 = [i for i, (a, b) in enumerate(zip(out2.codes, codes2)) if a != b and ms[i] > 5e-3]
     assert not bad2, (shape, bad2)
 print("alternate path ok")
 """
