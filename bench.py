@@ -160,6 +160,7 @@ def measured_peaks():
 
 # committed ncu summaries holding a `dram_bytes_per_launch:` line, per trace kind
 TRAFFIC_FILES = {"attn+o+resid": "attention_decode_0p6b.txt", "gemv+swiglu": "gateup_gemv_0p6b.txt",
+                 "gemv+resid": "down_gemv_0p6b.txt",
                  "cp head+select": "cp_head_select_0p6b.txt"}
 
 
@@ -378,9 +379,22 @@ def codec_main(args, c):
             dist.destroy_process_group()
         return
     clocks = clk.summary()
-    sm_max = clocks.get("sm_max_mhz") or 1965.0
-    sms = torch.cuda.get_device_properties(local).multi_processor_count
-    peak = sms * 128 * 2 * sm_max * 1e6 / 1e12  # fp32 FMA lanes per SM x 2 FLOP x clock
+    # streaming: 6-frame chunks of the same codes, with carried decoder state
+    # against the reference's re-decode of 25 left-context frames per chunk
+    chunk, ctx = 6, 25
+    cs = eng.open_codec_stream(T)
+    carried_ms = windowed_ms = 0.0
+    for s0 in range(0, T, chunk):
+        cs.decode(codes[s0:s0 + chunk].reshape(-1))
+        carried_ms += eng.last_decode_timing()[0]
+        a = max(0, s0 - ctx)
+        eng.decode_codes(codes[a:s0 + chunk].reshape(-1))
+        windowed_ms += eng.last_decode_timing()[0]
+    cs.close()
+    peaks, peak_kind = measured_peaks()
+    # each fp32 product is three bf16 tensor-core products (hi*hi, hi*lo, lo*hi),
+    # so the ceiling of this method is a third of the bf16 tensor peak
+    peak = peaks["bf16_tflops"] / 3.0
     achieved = flops * args.steps / (dev_ms / 1000.0) / 1e12
     line = {
         "metric": metric, "value": frames_all / (dev_ms_max / 1000.0), "unit": "frames/s",
@@ -393,12 +407,20 @@ def codec_main(args, c):
         "e2e": {"value": frames_all / wall_max, "unit": "frames/s",
                 "h2d_bytes_per_step": int(flat.nbytes), "d2h_bytes_per_step": int(wav.nbytes)},
         "gpu_launches": int(launches_all),
-        "roofline": {"bound": "fp32", "kernel": "whole decode (k_codec_conv carries >99 % of "
-                                                 "the FLOPs)",
+        "roofline": {"bound": "tensor", "kernel": "whole decode (k_codec_conv_tc carries >97 % "
+                                                   "of the FLOPs)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak,
-                     "peak_kind": "nominal fp32 CUDA-core: SMs x 128 lanes x 2 x max SM clock",
+                     "peak_kind": f"{peak_kind} bf16 tensor peak / 3 (fp32 products as three "
+                                  "bf16 MMA products); achieved counts the fp32 algorithm's FLOPs",
                      "flops_per_step": flops, "traffic": None},
+        "streaming": {"chunk_frames": chunk, "frames": T,
+                      "carried_state_ms_per_chunk": carried_ms / ((T + chunk - 1) // chunk),
+                      "redecode_ms_per_chunk": windowed_ms / ((T + chunk - 1) // chunk),
+                      "redecode_context_frames": ctx,
+                      "note": "device time per 6-frame audio chunk: qtts_codec_stream_decode "
+                              "(carried state) vs qtts_decode_codes of the chunk plus up to 25 "
+                              "context frames (the reference's next_audio_chunk)"},
         "clocks": clocks,
     }
     if not args.no_cpu_baseline:
@@ -497,7 +519,6 @@ def main():
         dist.barrier()
 
     eng = pkg.HipTtsEngine.load_with_options(mdir, pkg.EngineOptions(local, 512))
-    workload["cp_pass_grid"] = int(eng.info.cp_pass_grid)  # persistent CodePredictor pass CTAs
     opts = options(pkg, c, seed=rank)
     if reqs is not None:
         bopts = [options(pkg, c, seed=b) for b in range(batch)]
@@ -550,7 +571,6 @@ def main():
         run_step()
 
     dev_ms, wall_s, frames, launches, last = 0.0, 0.0, 0, 0, None
-    cp_pass_ms = []
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -569,9 +589,6 @@ def main():
             frames += out.frames
             launches += tm["kernels"]
             last = (out, tm)
-            cpt = eng.last_cp_pass_timing()
-            if cpt and not c.get("stream") and batch == 1:
-                cp_pass_ms.append(cpt[0])
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -579,7 +596,6 @@ def main():
         [dev_ms, wall_s], [frames, launches], world, "cuda")
     frames_all, launches_all = int(frames_all), int(launches_all)
 
-    cp_pass = eng.last_cp_pass_timing()  # (ms, bytes) of the last frame's pass
     # secondary: the talker gate|up GEMV (+ RMSNorm prologue, SwiGLU epilogue)
     # in a chain of its own launches
     ms_k, bytes_k = eng.profile_projection(0, 280)
@@ -609,26 +625,8 @@ def main():
                   "bytes_per_launch": bytes_k, "ms_per_launch": ms_k,
                   "timing": "CUDA events around 280 back-to-back launches on the engine stream",
                   "traffic": committed_traffic()}
-        if cp_pass_ms:
-            # dominant kernel: the persistent CodePredictor pass (one launch per
-            # frame), timed live inside the frame graph by event nodes around it
-            cp_ms = statistics.mean(cp_pass_ms)
-            cp_gbs = cp_pass[1] / (cp_ms * 1e-3) / 1e9
-            roofline = {"bound": "hbm",
-                        "kernel": "k_cp_pass (persistent CodePredictor pass: 2-row prefill, "
-                                  "14 decode groups, 15 heads + token selection)",
-                        "achieved": cp_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                        "frac": cp_gbs / peaks["hbm_gbs"], "peak_kind": peak_kind,
-                        "bytes_per_launch": cp_pass[1], "ms_per_launch": cp_ms,
-                        "share_of_frame": cp_ms / frame_ms,
-                        "timing": "CUDA event nodes around the pass in the live frame graph, "
-                                  "last frame of every timed step",
-                        "traffic": committed_traffic("cp_pass_0p6b.txt")}
-            line_extra["roofline_gateup"] = gateup
-        else:
-            roofline = gateup
-    frame_kernels = None
-    if batch == 1 and not c.get("stream") and not cp_pass_ms:
+        roofline = gateup
+    if batch == 1 and not c.get("stream"):
         frame_kernels = traced_frame_kernels(eng, ids, opts)
         if frame_kernels:
             top = frame_kernels[0]

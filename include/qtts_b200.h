@@ -109,10 +109,7 @@ typedef struct {
   uint32_t codec_eos;
   size_t max_cache_steps;
   size_t device_bytes; /* weights + KV + workspaces held on the device */
-  /* CTAs of the persistent CodePredictor pass (one per SM), 0 when the
-   * CodePredictor runs as one kernel per op. */
-  int32_t cp_pass_grid;
-  int32_t reserved;
+  int32_t reserved[2];
   int32_t has_codec;          /* speech_tokenizer/model.safetensors was loaded */
   uint32_t samples_per_frame; /* waveform samples per code frame (24 kHz): 1920 */
 } qtts_engine_info;
@@ -292,16 +289,10 @@ int32_t qtts_step_trace_enable(qtts_engine* engine, int32_t on);
 int32_t qtts_step_trace_read(const qtts_engine* engine, qtts_trace_launch* out, size_t cap,
                              size_t* n);
 
-/* Measurement hook (no reference counterpart): device time (CUDA events on
- * the engine stream, inside the frame graph) of the persistent CodePredictor
- * pass of the last frame the last generation call ran, and the weight bytes
- * one pass streams. QTTS_ERR_UNSUPPORTED when the pass is off. */
-int32_t qtts_last_cp_pass_timing(const qtts_engine* engine, float* ms, double* weight_bytes);
-
 /* Self-test of the library's bounded device waits (no reference
  * counterpart): one kernel waits for a device counter that nothing
- * increments, bounded by limit_us microseconds (at most 5 s), the same way the
- * persistent CodePredictor pass waits for the other CTAs. Returns
+ * increments, bounded by limit_us microseconds (at most 5 s), with the
+ * acquire loads and %globaltimer bound every spin-wait of the library uses. Returns
  * QTTS_ERR_DEVICE_STATE ("a bounded device wait ran out") once the bound
  * expires; the engine stays usable afterwards. */
 int32_t qtts_selftest_device_wait(qtts_engine* engine, uint32_t limit_us);

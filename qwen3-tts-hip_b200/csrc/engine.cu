@@ -30,7 +30,6 @@
 #include <vector>
 
 #include "codec.h"
-#include "cp_pass.h"
 #include "gemm_tc.h"
 #include "json.h"
 #include "kernels.h"
@@ -813,25 +812,8 @@ class Engine {
   std::vector<int> pinned_ids_storage;
 
   std::map<SampleKey, cudaGraphExec_t> graphs;
-  // Persistent CodePredictor pass (one cooperative launch per frame), opt-in
-  // with QTTS_CP_PASS=1: measured slower than the per-op kernels (343 vs 439
-  // frames/s, 0.6B sampled), which stay the default.
-  bool use_cp_pass = false;
-  int cp_grid = 0;
-  CpOp* cp_ops = nullptr;
-  CpLoad* cp_loads = nullptr;
-  int cp_n_ops = 0;
-  unsigned long long* cp_counter = nullptr;
-  int* cp_err = nullptr;
-  unsigned long long* cp_trace = nullptr;  // with QTTS_STEP_TRACE: [ops][4] stamps of CTA 0
-  std::vector<std::string> cp_op_names;
-  cudaEvent_t cp_ev[2] = {nullptr, nullptr};  // around the pass inside the frame graph
-  float last_cp_ms = 0.f;        // the pass of the last frame of the last burst
-  double cp_weight_bytes = 0.0;  // weight bytes one pass streams
   unsigned long long* selftest_ctr = nullptr;  // qtts_selftest_device_wait
   int* selftest_status = nullptr;
-  void build_cp_pass();
-  void launch_cp(const SampleKey& k, float* dbg_logits = nullptr, float* emb_sum_out = nullptr);
   // tcgen05 projections for M >= tc_min_rows rows (QTTS_TC=0 disables)
   // Which projections use it is fixed per call site, not per row count, so a
   // row gets identical arithmetic however the rows are batched (one-shot vs
@@ -1105,7 +1087,6 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   if (dev < 0 || dev >= ndev) invalid("device " + std::to_string(dev) + " not present");
   QCK(cudaSetDevice(dev));
   QCK(configure_kernels());
-  QCK(configure_cp_pass());
   QCK(configure_tc_kernels());
   QCK(configure_codec_tc());
   QCK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
@@ -1244,7 +1225,8 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
   tp_b = arena.alloc<float>((size_t)tp_rows * text_inter);
   tp_c = arena.alloc<float>((size_t)tp_rows * T.hidden);
   {
-    step_trace = arena.alloc<unsigned long long>(8 * (size_t)kTraceCap);
+    // eight slots per launch, then 16 x 16 token-selection phase stamps
+    step_trace = arena.alloc<unsigned long long>(8 * (size_t)kTraceCap + 256);
     if (const char* tp = std::getenv("QTTS_STEP_TRACE")) {
       step_trace_path = tp;
       trace_on = true;
@@ -1258,13 +1240,6 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
     }
     const char* fz = std::getenv("QTTS_FUSE_ATTN_O");
     fuse_attn_o = !(fz && fz[0] == '0');
-    const char* cz = std::getenv("QTTS_CP_PASS");
-    cp_grid = cp_pass_grid(dev);
-    use_cp_pass = cz && cz[0] == '1' && cp_grid > 0 &&
-                  cp_pass_supported(C.hidden, C.intermediate, C.q_heads, C.kv_heads, T.hidden,
-                                    C.vocab, cp_grid) &&
-                  C.groups <= kCpPositions;
-    if (use_cp_pass) build_cp_pass();
   }
   {
     // HipCodecInitial::load (codec_hip.rs:214-336); optional here so the
@@ -1329,8 +1304,6 @@ Engine::~Engine() {
   if (stage) cudaFreeHost(stage);
   if (bt.st_host) cudaFreeHost(bt.st_host);
   for (auto& ev : bt.ev)
-    if (ev) cudaEventDestroy(ev);
-  for (auto& ev : cp_ev)
     if (ev) cudaEventDestroy(ev);
   if (ev0) cudaEventDestroy(ev0);
   if (ev1) cudaEventDestroy(ev1);
@@ -1449,14 +1422,6 @@ void Engine::enqueue_frame(const SampleKey& k) {
   const int* halt = &st->halt;
   const StackCfg& C = cfg.cp;
   const int H = cfg.talker.hidden;
-  if (use_cp_pass) {
-    launch_cp(k);
-    if (!k.last) {
-      stack_step(talker, tb, tkv, &st->talker_pos, 0, halt);
-      talker_head(ROLE_TALKER_STEP, tb.x, k.t, k.penalty, halt, cp_prefix_target());
-    }
-    return;
-  }
   if (has_proj())
     linear(proj_w, cp_prefix, H, nullptr, 0.f, cb.x, C.hidden, nullptr, 0, proj_b, 2, C.hidden,
            H, EPI_BIAS, halt);
@@ -1473,175 +1438,6 @@ void Engine::enqueue_frame(const SampleKey& k) {
     stack_step(talker, tb, tkv, &st->talker_pos, 0, halt);
     talker_head(ROLE_TALKER_STEP, tb.x, k.t, k.penalty, halt, cp_prefix_target());
   }
-}
-
-// Op list of the persistent CodePredictor pass (the same sequence as the
-// CodePredictor part of enqueue_frame): built once per engine; the sampling
-// configuration travels in the launch parameters.
-void Engine::build_cp_pass() {
-  const StackCfg& C = cfg.cp;
-  const int H = cfg.talker.hidden;
-  const bool proj = has_proj();
-  DevStack& S = cp;
-  StackBufs& B = cb;
-  std::vector<CpOp> ops;
-  auto name = [&](const std::string& n) { cp_op_names.push_back(n); };
-  auto gemv = [&](const __nv_bfloat16* W, int N, int K, int M, int epi, const float* gamma,
-                  int x_src, const float* x, int ldx, float* y, int ldy, int wait) {
-    CpOp o{};
-    o.kind = CPOP_GEMV;
-    o.epi = epi;
-    o.M = M;
-    o.N = N;
-    o.K = K;
-    o.W = W;
-    o.gamma = gamma;
-    o.eps = C.eps;
-    o.x_src = x_src;
-    o.x = x;
-    o.ldx = ldx;
-    o.y = y;
-    o.ldy = ldy;
-    o.wait = wait;
-    return o;
-  };
-  // One decoder layer on M rows at positions pos0.. whose input (and residual)
-  // is `in_src` / `in`.
-  auto layer = [&](int l, int M, int pos0, int in_src, const float* in, int ld_in, int wait_qkv,
-                   const std::string& tag) {
-    ops.push_back(gemv(S.wqkv[l], S.qkv_w, C.hidden, M, EPI_STORE, S.in_g[l], in_src, in, ld_in,
-                       B.qkv, S.qkv_w, wait_qkv));
-    name(tag + " qkv");
-    CpOp o = gemv(S.wo[l], C.hidden, S.q_out, M, EPI_RESID, nullptr, CPSRC_GLOBAL, nullptr, 0,
-                  B.h1, C.hidden, 1);
-    o.kind = CPOP_ATTN_O;
-    o.r_src = in_src;
-    o.resid = in;
-    o.ldr = ld_in;
-    o.qkv = B.qkv;
-    o.ld_qkv = S.qkv_w;
-    o.q_gamma = S.q_g[l];
-    o.k_gamma = S.k_g[l];
-    o.layer = l;
-    o.pos0 = pos0;
-    ops.push_back(o);
-    name(tag + " attn+o");
-    ops.push_back(gemv(S.wgu[l], C.intermediate, C.hidden, M, EPI_SWIGLU, S.post_g[l],
-                       CPSRC_GLOBAL, B.h1, C.hidden, B.act, C.intermediate, 1));
-    name(tag + " gate|up");
-    CpOp d = gemv(S.wdown[l], C.hidden, C.intermediate, M, EPI_RESID, nullptr, CPSRC_GLOBAL,
-                  B.act, C.intermediate, B.x, C.hidden, 1);
-    d.r_src = CPSRC_GLOBAL;
-    d.resid = B.h1;
-    d.ldr = C.hidden;
-    ops.push_back(d);
-    name(tag + " down");
-  };
-  auto head = [&](int g, const float* x) {
-    CpOp o = gemv(cp_heads + (size_t)g * C.vocab * C.hidden, C.vocab, C.hidden, 1, EPI_STORE,
-                  cp_norm_g, CPSRC_GLOBAL, x, C.hidden, logits, C.vocab, 1);
-    o.kind = CPOP_HEAD;
-    o.group = g;
-    ops.push_back(o);
-    name("head " + std::to_string(g));
-  };
-  auto projection = [&](int M, int x_src, const float* x) {
-    CpOp o = gemv(proj_w, C.hidden, H, M, EPI_BIAS, nullptr, x_src, x, H, B.x, C.hidden, 0);
-    o.bias = proj_b;
-    ops.push_back(o);
-    name("projection");
-  };
-  // 2-row prefill at positions 0, 1 (code_predictor.rs:366-392)
-  // The talker head leaves the two prefix rows in cp_prefix_target(): the
-  // projection's input for 1.7B, else the CodePredictor's input rows B.x.
-  if (proj) projection(2, CPSRC_GLOBAL, cp_prefix);
-  for (int l = 0; l < C.layers; ++l) {
-    const bool first = l == 0 && !proj;  // rows written before the launch: no wait
-    layer(l, 2, 0, CPSRC_GLOBAL, B.x, C.hidden, first ? 0 : 1, "prefill L" + std::to_string(l));
-  }
-  head(0, B.x + C.hidden);
-  // groups 1..14 at position g + 1 (code_predictor.rs:393-471)
-  for (int g = 1; g < C.groups - 1; ++g) {
-    if (proj) projection(1, CPSRC_LOCAL, nullptr);
-    for (int l = 0; l < C.layers; ++l) {
-      const bool local = l == 0 && !proj;
-      layer(l, 1, g + 1, local ? CPSRC_LOCAL : CPSRC_GLOBAL, local ? nullptr : B.x, C.hidden,
-            local ? 0 : 1, "g" + std::to_string(g) + " L" + std::to_string(l));
-    }
-    head(g, B.x);
-  }
-  // The ring is refilled between ops, so every op's rows must fit in it at
-  // once; the op list must fit the shared-memory weight table.
-  bool fits = ops.size() <= (size_t)kCpMaxOps;
-  for (const CpOp& o : ops) {
-    const int rows = (o.N + cp_grid - 1) / cp_grid;
-    const int rps = kCpStageBytes / (2 * o.K);
-    const int pieces = (o.epi == EPI_SWIGLU ? 2 : 1) * ((rows + rps - 1) / rps);
-    if (rps < 1 || pieces > kCpStages) fits = false;
-  }
-  if (!fits) {
-    use_cp_pass = false;
-    cp_op_names.clear();
-    return;
-  }
-  std::vector<CpLoad> loads(ops.size());
-  for (size_t i = 0; i < ops.size(); ++i)
-    loads[i] = CpLoad{ops[i].W, ops[i].N, (short)ops[i].K,
-                      (short)(ops[i].epi == EPI_SWIGLU ? 2 : 1)};
-  cp_loads = arena.alloc<CpLoad>(loads.size());
-  QCK(cudaMemcpy(cp_loads, loads.data(), loads.size() * sizeof(CpLoad), cudaMemcpyHostToDevice));
-  cp_n_ops = (int)ops.size();
-  cp_weight_bytes = 0.0;
-  for (const CpOp& o : ops)
-    cp_weight_bytes += 2.0 * o.K * (double)o.N * (o.epi == EPI_SWIGLU ? 2 : 1);
-  for (auto& ev : cp_ev) QCK(cudaEventCreate(&ev));
-  cp_ops = arena.alloc<CpOp>(ops.size());
-  QCK(cudaMemcpy(cp_ops, ops.data(), ops.size() * sizeof(CpOp), cudaMemcpyHostToDevice));
-  cp_counter = arena.alloc<unsigned long long>(1);
-  cp_err = arena.alloc<int>(2);
-  QCK(cudaMemset(cp_counter, 0, sizeof(unsigned long long)));
-  QCK(cudaMemset(cp_err, 0, 2 * sizeof(int)));
-  cp_trace = arena.alloc<unsigned long long>(kCpTraceSlots * ops.size());
-}
-
-void Engine::launch_cp(const SampleKey& k, float* dbg_logits, float* emb_sum_out) {
-  const StackCfg& C = cfg.cp;
-  CpPassParams p{};
-  p.ops = cp_ops;
-  p.loads = cp_loads;
-  p.n_ops = cp_n_ops;
-  p.counter = cp_counter;
-  p.error = cp_err;
-  p.st = st;
-  p.q_heads = C.q_heads;
-  p.kv_heads = C.kv_heads;
-  p.scale = 1.0f / std::sqrt((float)C.head_dim);
-  p.rope_cos = cp.rope_cos;
-  p.rope_sin = cp.rope_sin;
-  p.cache = ckv.pool;  // page 0: [layer][K|V][kv_head][16][128]
-  p.H = cfg.talker.hidden;
-  p.groups = C.groups;
-  p.vocab = C.vocab;
-  p.cp_embs = cp_embs;
-  p.cfg = k.s;
-  p.codes = codes;
-  p.history = history;
-  p.talker_codec_emb = codec_emb;
-  p.trailing = trailing;
-  p.tts_pad = tts_pad;
-  p.step_in = tb.x;
-  p.trace = trace_capture ? cp_trace : nullptr;
-  p.dbg_logits = dbg_logits;
-  p.emb_sum_out = emb_sum_out;
-  // inside a captured frame graph the events must be external record nodes
-  // (a plain record under capture only orders work and keeps no time)
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  QCK(cudaStreamIsCapturing(stream, &cs));
-  const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
-  QCK(cudaEventRecordWithFlags(cp_ev[0], stream, flags));
-  QCK(launch_cp_pass(p, cp_grid, stream));
-  QCK(cudaEventRecordWithFlags(cp_ev[1], stream, flags));
-  ++launches;
 }
 
 cudaGraphExec_t Engine::frame_graph(const SampleKey& k) {
@@ -1780,10 +1576,6 @@ void Engine::begin(int P, int n_trailing, const qtts_generate_options& o) {
   s.rng_seed = o.seed;
   *st_host = s;
   QCK(cudaMemcpyAsync(st, st_host, sizeof(SeqState), cudaMemcpyHostToDevice, stream));
-  if (cp_counter) {
-    QCK(cudaMemsetAsync(cp_counter, 0, sizeof(unsigned long long), stream));
-    QCK(cudaMemsetAsync(cp_err, 0, 2 * sizeof(int), stream));
-  }
   QCK(cudaEventRecord(ev0, stream));
   const size_t l0 = launches;
   stack_rows(talker, tb, tkv, P, 0, nullptr);
@@ -1809,14 +1601,6 @@ void Engine::sync_state() {
   stream_sync();
   if (st_host->error)
     fail(QTTS_ERR_DEVICE_STATE, "cannot sample from logits with no finite values");
-  if (cp_err) {
-    int e[2] = {0, 0};
-    QCK(cudaMemcpy(e, cp_err, sizeof e, cudaMemcpyDeviceToHost));
-    if (e[0])
-      fail(QTTS_ERR_DEVICE_STATE, "CodePredictor pass stopped: a bounded device wait ran out "
-                                  "(code " + std::to_string(e[0]) + ", op " +
-                                  std::to_string(e[1]) + ")");
-  }
   if (tc_err) {
     int e = 0;
     QCK(cudaMemcpy(&e, tc_err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -1845,7 +1629,7 @@ size_t Engine::run_frames(size_t n) {
     if (trace_now) {
       QCK(cudaMemsetAsync(step_trace, 0xff, 2 * kTraceCap * sizeof(unsigned long long), stream));
       QCK(cudaMemsetAsync(step_trace + 2 * kTraceCap, 0,
-                          6 * kTraceCap * sizeof(unsigned long long), stream));
+                          (6 * kTraceCap + 256) * sizeof(unsigned long long), stream));
       QCK(set_step_trace(step_trace, kTraceCap, stream));
     }
     QCK(cudaGraphLaunch(is_last ? gl : gf, stream));
@@ -1857,7 +1641,6 @@ size_t Engine::run_frames(size_t n) {
   }
   QCK(cudaEventRecord(ev2, stream));
   sync_state();
-  if (use_cp_pass) QCK(cudaEventElapsedTime(&last_cp_ms, cp_ev[0], cp_ev[1]));
   if (traced) dump_step_trace();
   float ms = 0.f;
   QCK(cudaEventElapsedTime(&ms, ev1, ev2));
@@ -1906,28 +1689,28 @@ void Engine::dump_step_trace() {
                  (unsigned long long)r.dur6_ns, (unsigned long long)r.dur7_ns, r.name);
   }
   std::fclose(f);
-  if (!cp_trace) return;
-  // the persistent CodePredictor pass: per op, CTA 0's stamps (kCpTraceSlots)
-  std::vector<unsigned long long> c((size_t)kCpTraceSlots * cp_n_ops);
-  QCK(cudaMemcpy(c.data(), cp_trace, c.size() * sizeof(unsigned long long),
-                 cudaMemcpyDeviceToHost));
-  FILE* g = std::fopen((step_trace_path + ".cp").c_str(), "w");
-  if (!g) return;
-  std::fprintf(g, "# op wait staged first_stage rows stored arrived last_stage|sel0 sel1 (ns "
-                  "after op 0's wait), then for heads six selection marks in cycles "
-                  "(keys, radix, compaction, rank, exp, end) name\n");
-  const unsigned long long c0 = c[0];
-  for (int i = 0; i < cp_n_ops; ++i) {
-    std::fprintf(g, "%d", i);
-    for (int k = 0; k < kCpTraceSlots; ++k) {
-      const unsigned long long v = c[(size_t)kCpTraceSlots * i + k];
-      const bool cycles = k >= 8;
-      std::fprintf(g, " %lld", cycles ? (long long)v
-                                      : (v >= c0 && v - c0 < (1ull << 40) ? (long long)(v - c0) : -1LL));
+  {
+    // token selection phases of the traced frame's heads (clock64 cycles
+    // between the Selector's stamps; slots 0-6 general path, 10-15 fast path)
+    std::vector<long long> sv(256);
+    QCK(cudaMemcpy(sv.data(), step_trace + 8 * (size_t)kTraceCap, sv.size() * sizeof(long long),
+                   cudaMemcpyDeviceToHost));
+    FILE* g = std::fopen((step_trace_path + ".sel").c_str(), "w");
+    if (g) {
+      std::fprintf(g, "# head (0 talker, 1+g CodePredictor group g): clock64 at the Selector's "
+                      "stamps 0..15, relative to the first nonzero one\n");
+      for (int h = 0; h < 16; ++h) {
+        long long base = 0;
+        for (int k = 0; k < 16; ++k)
+          if (sv[16 * h + k] && (!base || sv[16 * h + k] < base)) base = sv[16 * h + k];
+        std::fprintf(g, "%d", h);
+        for (int k = 0; k < 16; ++k)
+          std::fprintf(g, " %lld", sv[16 * h + k] ? sv[16 * h + k] - base : -1LL);
+        std::fprintf(g, "\n");
+      }
+      std::fclose(g);
     }
-    std::fprintf(g, " %s\n", cp_op_names[i].c_str());
   }
-  std::fclose(g);
 }
 
 // ---- batched serving -------------------------------------------------------
@@ -2462,8 +2245,7 @@ int32_t qtts_engine_get_info(const qtts_engine* h, qtts_engine_info* out) {
     out->codec_eos = e.cfg.codec_eos;
     out->max_cache_steps = e.max_cache_steps;
     out->device_bytes = e.arena.bytes() + (e.codec ? e.codec->device_bytes() : 0);
-    out->cp_pass_grid = e.use_cp_pass ? e.cp_grid : 0;
-    out->reserved = 0;
+    out->reserved[0] = out->reserved[1] = 0;
     out->has_codec = e.codec ? 1 : 0;
     out->samples_per_frame = qtts::Codec::samples_per_frame();
   });
@@ -2992,25 +2774,6 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
     e.h2d(e.st, e.st_host, sizeof(s));
     const qtts::SampleCfg sc = qtts::sub_cfg(opt);
     const int na = C.groups - 1;
-    if (e.use_cp_pass) {
-      // the persistent pass the frame graph runs, with every head's logits
-      // and the embedding sum copied out for parity checks
-      QCK(cudaMemsetAsync(e.cp_counter, 0, sizeof(unsigned long long), e.stream));
-      QCK(cudaMemsetAsync(e.cp_err, 0, 2 * sizeof(int), e.stream));
-      const qtts::SampleKey k{qtts::talker_cfg(opt), sc, 1.0f, 1};
-      e.launch_cp(k, e.dbg_logits, e.emb_sum);
-      e.sync_state();
-      std::vector<int32_t> row(C.groups);
-      e.read_codes(0, 1, row.data());
-      if (tokens_out) std::memcpy(tokens_out, row.data() + 1, na * 4);
-      if (emb_sum_out) QCK(cudaMemcpy(emb_sum_out, e.emb_sum, H * 4, cudaMemcpyDeviceToHost));
-      if (logits_out)
-        QCK(cudaMemcpy(logits_out, e.dbg_logits, (size_t)na * C.vocab * 4,
-                       cudaMemcpyDeviceToHost));
-      e.seq_ended = true;
-      ++e.seq_id;
-      return;
-    }
     // Eager CodePredictor pass with per-group logits kept for parity checks.
     if (e.has_proj())
       e.linear(e.proj_w, e.cp_prefix, H, nullptr, 0.f, e.cb.x, C.hidden, nullptr, 0, e.proj_b, 2,
@@ -3060,16 +2823,6 @@ int32_t qtts_step_trace_read(const qtts_engine* h, qtts_trace_launch* out, size_
     const Engine& e = *h->e;
     *n = e.trace_rows.size();
     if (out) std::memcpy(out, e.trace_rows.data(), std::min(cap, *n) * sizeof(qtts_trace_launch));
-  });
-}
-
-int32_t qtts_last_cp_pass_timing(const qtts_engine* h, float* ms, double* weight_bytes) {
-  return guard([&] {
-    need(h, "engine");
-    const Engine& e = *h->e;
-    if (!e.use_cp_pass) qtts::fail(QTTS_ERR_UNSUPPORTED, "the persistent CodePredictor pass is off");
-    if (ms) *ms = e.last_cp_ms;
-    if (weight_bytes) *weight_bytes = e.cp_weight_bytes;
   });
 }
 

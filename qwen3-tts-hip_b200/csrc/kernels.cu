@@ -503,6 +503,11 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
 
   const int V = a.lin.N;
   Selector<SyncBlock> sel{smem, reinterpret_cast<int*>(smem + kSelMaxVocab)};
+  // traced frames: the selection's phase stamps (clock64) land after the
+  // trace's eight slots, 16 per head (row 0 the talker, 1 + g CodePredictor group g)
+  if (a.lin.trace_id > 0 && g_trace.buf)
+    sel.dbg = reinterpret_cast<long long*>(g_trace.buf + 8 * (size_t)g_trace.cap) +
+              16 * (a.role == ROLE_CP_GROUP ? 1 + a.group : 0);
   const int tid = threadIdx.x;
   // The RNG state is read alongside the logits (the sampler draws early).
   Rng rng{a.st->rng_kind, a.st->rng_state, a.st->rng_seed, a.st->rng_counter};
@@ -1170,6 +1175,39 @@ cudaError_t launch_attn_o(const AttnDecodeArgs& at, const LinearArgs& o, cudaStr
 cudaError_t set_crumbs_kernels(unsigned* host_mapped_dev_ptr) {
   const Crumbs c{host_mapped_dev_ptr};
   return cudaMemcpyToSymbol(g_crumbs, &c, sizeof(c));
+}
+
+namespace {
+// Self-test of the bounded waits: one thread polls a counter for a target
+// that nothing will reach, with an acquire load and a %globaltimer bound, and
+// reports the expiry through `status`. Nothing else is in flight in the CTA.
+__global__ void k_wait_selftest(const unsigned long long* counter, unsigned long long target,
+                                unsigned long long limit_ns, int* status) {
+  if (threadIdx.x != 0) return;
+  auto now = [] {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+  };
+  const unsigned long long t0 = now();
+  int expired = 0;
+  for (;;) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(counter) : "memory");
+    if (v >= target) break;
+    if (now() - t0 > limit_ns) {
+      expired = 1;
+      break;
+    }
+  }
+  *status = expired;
+}
+}  // namespace
+
+cudaError_t launch_wait_selftest(const unsigned long long* counter, unsigned long long target,
+                                 unsigned long long limit_ns, int* status, cudaStream_t stream) {
+  k_wait_selftest<<<1, 32, 0, stream>>>(counter, target, limit_ns, status);
+  return cudaGetLastError();
 }
 
 cudaError_t set_step_trace(unsigned long long* buf, int capacity, cudaStream_t stream) {

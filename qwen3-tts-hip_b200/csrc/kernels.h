@@ -182,6 +182,10 @@ cudaError_t set_crumbs_gemm(unsigned* host_mapped_dev_ptr);
 // CTAs of the time since the CTA's own dependency wait); nullptr disables.
 // Stream-ordered.
 cudaError_t set_step_trace(unsigned long long* buf, int capacity, cudaStream_t stream);
+// One thread waits (bounded by limit_ns) for *counter >= target; *status = 1
+// when the wait ran out, 0 when the target was reached.
+cudaError_t launch_wait_selftest(const unsigned long long* counter, unsigned long long target,
+                                 unsigned long long limit_ns, int* status, cudaStream_t stream);
 cudaError_t launch_qk_prep(const QkPrepArgs& a, cudaStream_t stream);
 cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t stream);
 

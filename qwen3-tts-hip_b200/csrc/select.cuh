@@ -1,6 +1,6 @@
-// Block-wide token selection shared by the standalone head kernel and the
-// persistent frame kernel. 256 threads; `Sync` is the block barrier in use
-// (all threads, or the 8 consumer warps of a warp-specialised CTA).
+// Block-wide token selection of the head kernels (the last CTA of k_head,
+// one CTA per sequence in k_select_batch). 256 threads; `Sync` is the block
+// barrier in use.
 //
 // Semantics follow the reference:
 //   greedy      argmax_rows_f32 (src/gpu/kernels.rs:177-220): start -FLT_MAX,
@@ -29,9 +29,6 @@ constexpr int kSelSmallK = 256;
 
 struct SyncBlock {
   __device__ static void sync() { __syncthreads(); }
-};
-struct SyncConsumers {  // named barrier 1 over the 8 consumer warps
-  __device__ static void sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 };
 
 __device__ __forceinline__ unsigned order_key(float f) {

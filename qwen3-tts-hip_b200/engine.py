@@ -89,7 +89,7 @@ class _Info(C.Structure):
                 ("cp_vocab", C.c_uint32), ("num_code_groups", C.c_uint32),
                 ("talker_layers", C.c_uint32), ("cp_layers", C.c_uint32),
                 ("codec_eos", C.c_uint32), ("max_cache_steps", C.c_size_t),
-                ("device_bytes", C.c_size_t), ("cp_pass_grid", C.c_int32), ("reserved", C.c_int32),
+                ("device_bytes", C.c_size_t), ("reserved", C.c_int32 * 2),
                 ("has_codec", C.c_int32), ("samples_per_frame", C.c_uint32)]
 
 
@@ -134,7 +134,6 @@ SIGNATURES = {
     "qtts_talker_decode_step_static": (C.c_int32, [_P, _F, C.c_size_t, _F, _F, _I32]),
     "qtts_code_predictor": (C.c_int32, [_P, _F, _F, C.POINTER(_Options), _I32, _F, _F]),
     "qtts_selftest_device_wait": (C.c_int32, [_P, C.c_uint32]),
-    "qtts_last_cp_pass_timing": (C.c_int32, [_P, _F, C.POINTER(C.c_double)]),
     "qtts_step_trace_enable": (C.c_int32, [_P, C.c_int32]),
     "qtts_step_trace_read": (C.c_int32, [_P, C.POINTER(_TraceLaunch), C.c_size_t, _SZ]),
     "qtts_last_timings": (C.c_int32, [_P, _F, _F, _SZ]),
@@ -574,16 +573,6 @@ class HipTtsEngine:
         _check(lib().qtts_code_predictor(self._h, _fptr(th), _fptr(se), C.byref(options._c()),
                                          toks.ctypes.data_as(_I32), _fptr(esum), _fptr(logits)))
         return toks.tolist(), esum, logits
-
-    def last_cp_pass_timing(self):
-        """(ms, weight bytes) of the persistent CodePredictor pass in the last
-        frame of the last generation call, or None when the pass is off."""
-        ms, nb = C.c_float(), C.c_double()
-        st = lib().qtts_last_cp_pass_timing(self._h, C.byref(ms), C.byref(nb))
-        if st == ERR_UNSUPPORTED:
-            return None
-        _check(st)
-        return ms.value, nb.value
 
     def step_trace_enable(self, on: bool) -> None:
         """Step trace of frame 6 of every generation (recaptures the graphs)."""

@@ -126,8 +126,7 @@ pub mod ffi {
         pub codec_eos: u32,
         pub max_cache_steps: usize,
         pub device_bytes: usize,
-        pub cp_pass_grid: i32,
-        pub reserved: i32,
+        pub reserved: [i32; 2],
         pub has_codec: i32,
         pub samples_per_frame: u32,
     }
@@ -230,8 +229,6 @@ pub mod ffi {
         pub fn qtts_step_trace_enable(engine: *mut qtts_engine, on: i32) -> i32;
         pub fn qtts_step_trace_read(engine: *const qtts_engine, out: *mut qtts_trace_launch,
                                     cap: usize, n: *mut usize) -> i32;
-        pub fn qtts_last_cp_pass_timing(engine: *const qtts_engine, ms: *mut f32,
-                                        weight_bytes: *mut f64) -> i32;
         pub fn qtts_selftest_device_wait(engine: *mut qtts_engine, limit_us: u32) -> i32;
         pub fn qtts_last_timings(engine: *const qtts_engine, prefill_ms: *mut f32,
                                  frames_ms: *mut f32, frames: *mut usize) -> i32;

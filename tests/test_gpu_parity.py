@@ -427,18 +427,15 @@ def test_full_size_1p7b(pkg, tmp_path_factory):
     e.close()
 
 
-@pytest.mark.parametrize("env", [{"QTTS_CP_PASS": "1"},
-                                 {"QTTS_FUSE_ATTN_O": "0"},
+@pytest.mark.parametrize("env", [{"QTTS_FUSE_ATTN_O": "0"},
                                  {"QTTS_TC_CP": "1"},
                                  {"QTTS_TC": "0"}],
-                         ids=["persistent-cp-pass", "unfused-cp-attn", "cp-tc-prefill",
-                              "cuda-core-prefill"])
+                         ids=["unfused-cp-attn", "cp-tc-prefill", "cuda-core-prefill"])
 def test_alternate_path_parity(model_dirs, tmp_path, env):
-    """The alternate paths against the oracle: the CodePredictor as one
-    persistent kernel per frame (QTTS_CP_PASS=1) instead of one kernel per op,
-    its attention as a separate kernel (QTTS_FUSE_ATTN_O=0), its 2-row prefill
-    on the tcgen05 GEMM (QTTS_TC_CP=1), and the talker prefill on CUDA cores
-    only (QTTS_TC=0). Run in a child process so the engine reads the setting at
+    """The alternate paths against the oracle: the CodePredictor attention as
+    a separate kernel (QTTS_FUSE_ATTN_O=0), its 2-row prefill on the tcgen05
+    GEMM (QTTS_TC_CP=1), and the talker prefill on CUDA cores only
+    (QTTS_TC=0). Run in a child process so the engine reads the setting at
     load."""
     import os
     import subprocess
