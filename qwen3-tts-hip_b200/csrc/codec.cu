@@ -184,25 +184,59 @@ __global__ void k_codec_rvq_project(const float* first, const float* rest, const
   y[(long long)c * frames + t] = s;
 }
 
-__global__ void k_codec_chan_norm(const float* x, int C, int T, const float* gamma,
-                                  const float* beta, float eps, float* y) {
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= T) return;
+// 32 time steps per CTA (one per lane, so every load is a coalesced 128-byte
+// row segment) and 32 warps splitting the channels, four loads in flight per
+// thread; the per-warp sums meet in shared memory. Short inputs (streamed
+// chunks) then still spread a channel sum over 32 warps.
+constexpr int kNormWarps = 32;
+__global__ void __launch_bounds__(kNormWarps * 32) k_codec_chan_norm(const float* x, int C, int T,
+                                                                  const float* gamma,
+                                                                  const float* beta, float eps,
+                                                                  float* y) {
+  __shared__ float s_sum[kNormWarps][33], s_sq[kNormWarps][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * 32 + lane;
+  const bool on = t < T;
   float s = 0.f, ss = 0.f;
-  for (int c = 0; c < C; ++c) {
-    const float v = x[(long long)c * T + t];
-    s += v;
-    ss += v * v;
+  if (on) {
+    int c = warp;
+    for (; c + 3 * kNormWarps < C; c += 4 * kNormWarps) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = x[(long long)(c + u * kNormWarps) * T + t];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        s += v[u];
+        ss += v[u] * v[u];
+      }
+    }
+    for (; c < C; c += kNormWarps) {
+      const float v = x[(long long)c * T + t];
+      s += v;
+      ss += v * v;
+    }
   }
+  s_sum[warp][lane] = s;
+  s_sq[warp][lane] = ss;
+  __syncthreads();
+  s = 0.f;
+  ss = 0.f;
+#pragma unroll 8
+  for (int w = 0; w < kNormWarps; ++w) {
+    s += s_sum[w][lane];
+    ss += s_sq[w][lane];
+  }
+  if (!on) return;
   if (beta) {  // LayerNorm (codec_layernorm_f32, kernels.rs:613-660)
     const float mean = s / (float)C;
     const float var = fmaxf(ss / (float)C - mean * mean, 0.0f);
     const float inv = rsqrtf(var + eps);
-    for (int c = 0; c < C; ++c)
+    for (int c = warp; c < C; c += kNormWarps)
       y[(long long)c * T + t] = (x[(long long)c * T + t] - mean) * inv * gamma[c] + beta[c];
   } else {  // RMSNorm (rmsnorm_f32, kernels.rs:2-37)
     const float inv = rsqrtf(ss / (float)C + eps);
-    for (int c = 0; c < C; ++c) y[(long long)c * T + t] = x[(long long)c * T + t] * inv * gamma[c];
+    for (int c = warp; c < C; c += kNormWarps)
+      y[(long long)c * T + t] = x[(long long)c * T + t] * inv * gamma[c];
   }
 }
 
@@ -344,7 +378,7 @@ cudaError_t codec_rvq(const int32_t* codes, int frames, int groups, int cb_size,
 
 cudaError_t codec_chan_norm(const float* x, int C, int T, const float* gamma, const float* beta,
                             float eps, float* y, cudaStream_t stream) {
-  k_codec_chan_norm<<<blocks(T, 128), 128, 0, stream>>>(x, C, T, gamma, beta, eps, y);
+  k_codec_chan_norm<<<blocks(T, 32), kNormWarps * 32, 0, stream>>>(x, C, T, gamma, beta, eps, y);
   return cudaGetLastError();
 }
 

@@ -77,11 +77,24 @@ cudaError_t codec_tc_prepare(const float* W, int rows, int ci, int taps, __nv_bf
                              __nv_bfloat16* lo, CodecTcWeight* out, cudaStream_t stream);
 // Whether codec_conv_tc computes this convolution with this weight.
 bool codec_tc_supported(const CodecConvArgs& a, const CodecTcWeight& w);
+// Split-K workspace of the tensor-core convolution: partial tiles
+// [tiles][splits][128][128] fp32 and one ticket per tile (zero at rest, reset
+// by the kernel). `sms`: the device's SM count.
+constexpr int kCodecTcMaxSplits = 32;
+struct CodecTcSplit {
+  float* ws = nullptr;
+  size_t ws_floats = 0;
+  unsigned* tickets = nullptr;
+  int max_tiles = 0;
+  int sms = 0;
+};
 // codec_conv on the tensor cores (tcgen05): bf16 hi + lo splits of the weight
-// and of the transformed input, fp32 accumulation; `err` receives a nonzero
-// code if a pipeline wait times out.
+// and of the transformed input, fp32 accumulation; convolutions with few
+// output tiles split K over the workspace when `split` is given (the partial
+// tiles are summed in a fixed order: results are deterministic). `err`
+// receives a nonzero code if a pipeline wait times out.
 cudaError_t codec_conv_tc(const CodecConvArgs& a, const CodecTcWeight& w, int* err,
-                          cudaStream_t stream);
+                          const CodecTcSplit* split, cudaStream_t stream);
 
 // first[t][d] = cb_first[code0][d]; rest[t][d] = sum_{g=1..15} cb_rest[g-1][code_g][d]
 // (codes taken modulo the codebook size), then

@@ -23,6 +23,8 @@
 #include <cudaTypedefs.h>
 #include <math.h>
 
+#include <algorithm>
+
 #include "codec.h"
 #include "common.cuh"
 #include "gemm_tc.h"
@@ -57,7 +59,7 @@ __device__ __forceinline__ float snake_f(float x, float a, float b) {
 template <int ACT>
 __global__ void __launch_bounds__(kCtThreads, 1)
     k_codec_conv_tc(const __grid_constant__ CUtensorMap mh, const __grid_constant__ CUtensorMap ml,
-                    CodecConvArgs a, int cip, int* err) {
+                    CodecConvArgs a, int cip, int* err, CodecTcSplit sp) {
   extern __shared__ uint8_t ct_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(ct_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -72,7 +74,11 @@ __global__ void __launch_bounds__(kCtThreads, 1)
   const int t0 = (blockIdx.x / a.nphase) * kCtCols;
   const int co0 = blockIdx.y * kCtRows;
   const int wrow = ph * a.co + co0;  // first weight row of this tile (phase-major rows)
-  const int nk = a.taps * cip / kCtK;
+  // split K over blockIdx.z: this CTA runs K steps [kb0, kb0 + nk)
+  const int nk_all = a.taps * cip / kCtK;
+  const int kb0 = (int)((long long)nk_all * blockIdx.z / gridDim.z);
+  const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb0;
+  __shared__ int s_last;
 
   const int pre = min(kCtStages, nk);
   if (threadIdx.x == 0) {
@@ -86,10 +92,10 @@ __global__ void __launch_bounds__(kCtThreads, 1)
     for (int i = 0; i < pre; ++i) {
       uint8_t* st = smem + i * kCtStage;
       mbar_expect_tx(&full[i], 2 * kCtW);
-      tma_load_2d(st, &mh, i * kCtK, wrow, &full[i]);
-      tma_load_2d(st + kCtW / 2, &mh, i * kCtK, wrow + kCtRows / 2, &full[i]);
-      tma_load_2d(st + kCtW, &ml, i * kCtK, wrow, &full[i]);
-      tma_load_2d(st + kCtW + kCtW / 2, &ml, i * kCtK, wrow + kCtRows / 2, &full[i]);
+      tma_load_2d(st, &mh, (kb0 + i) * kCtK, wrow, &full[i]);
+      tma_load_2d(st + kCtW / 2, &mh, (kb0 + i) * kCtK, wrow + kCtRows / 2, &full[i]);
+      tma_load_2d(st + kCtW, &ml, (kb0 + i) * kCtK, wrow, &full[i]);
+      tma_load_2d(st + kCtW + kCtW / 2, &ml, (kb0 + i) * kCtK, wrow + kCtRows / 2, &full[i]);
     }
   }
   if (warp == 1) tmem_alloc(tmem_slot, kCtTmemCols);
@@ -108,10 +114,10 @@ __global__ void __launch_bounds__(kCtThreads, 1)
       }
       uint8_t* st = smem + s * kCtStage;
       mbar_expect_tx(&full[s], 2 * kCtW);
-      tma_load_2d(st, &mh, i * kCtK, wrow, &full[s]);
-      tma_load_2d(st + kCtW / 2, &mh, i * kCtK, wrow + kCtRows / 2, &full[s]);
-      tma_load_2d(st + kCtW, &ml, i * kCtK, wrow, &full[s]);
-      tma_load_2d(st + kCtW + kCtW / 2, &ml, i * kCtK, wrow + kCtRows / 2, &full[s]);
+      tma_load_2d(st, &mh, (kb0 + i) * kCtK, wrow, &full[s]);
+      tma_load_2d(st + kCtW / 2, &mh, (kb0 + i) * kCtK, wrow + kCtRows / 2, &full[s]);
+      tma_load_2d(st + kCtW, &ml, (kb0 + i) * kCtK, wrow, &full[s]);
+      tma_load_2d(st + kCtW + kCtW / 2, &ml, (kb0 + i) * kCtK, wrow + kCtRows / 2, &full[s]);
       ++issued;
     }
     // No copy may still be landing and no commit still due on a stage barrier
@@ -155,7 +161,7 @@ __global__ void __launch_bounds__(kCtThreads, 1)
     // K is tap-major (k = tap * cip + channel), so one step reads 64 channels
     // of a single input column, which is in range or not as a whole
     auto load_step = [&](int i, float (&v)[32], float (&u)[NU]) {
-      const int kg = i * kCtK;
+      const int kg = (kb0 + i) * kCtK;
       const int tap = kg / cip;
       const int c0 = kg - tap * cip + 32 * h;
       const int src = t + tap * a.dil - a.pad;
@@ -229,26 +235,73 @@ __global__ void __launch_bounds__(kCtThreads, 1)
     const float rs = row_ok && a.rscale ? __ldg(a.rscale + co) : 1.f;
     const float sa = row_ok && a.out_a ? __ldg(a.out_a + co) : 0.f;
     const float sb = row_ok && a.out_a ? __ldg(a.out_b + co) : 0.f;
-    for (int c0 = cbeg; c0 < cbeg + kCtCols / 2; c0 += 16) {
-      if (t0 + c0 >= a.lin) break;  // warp-uniform
-      float v[16], w[16];
-      tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0, v);
-      tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(c0 + kCtCols), w);
-      if (!row_ok) continue;
+    // Split K: every CTA of a tile stores its partial tile; the last to
+    // finish (ticket) sums all of them in split order, so the result does not
+    // depend on which CTA finished last.
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    const int r = lane_base + lane;
+    float* part = sp.ws + (((long long)tile * gridDim.z + blockIdx.z) * kCtRows + r) * kCtCols;
+    bool final_cta = true;
+    if (gridDim.z > 1) {
+      for (int c0 = cbeg; c0 < cbeg + kCtCols / 2; c0 += 16) {
+        float v[16], w[16];
+        tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0, v);
+        tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(c0 + kCtCols), w);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int tt = t0 + c0 + j;
-        if (tt >= a.lin) break;
-        float o = v[j] + w[j] + b;
-        if (a.epi & CEPI_GELU) o = 0.5f * o * (1.0f + erff(o * 0.7071067811865476f));
-        const long long at = (long long)co * lout + (long long)tt * a.ostride + ph;
-        if (a.epi & CEPI_RESID) o = a.resid[at] + o * rs;
-        if (a.epi & CEPI_CLAMP) o = fminf(fmaxf(o, -1.0f), 1.0f);
-        if (a.epi & CEPI_SNAKE) {
-          a.y[at] = snake_f(o, sa, sb);
+        for (int j = 0; j < 16; j += 4)
+          __stcg(reinterpret_cast<float4*>(part + c0 + j),
+                 make_float4(v[j] + w[j], v[j + 1] + w[j + 1], v[j + 2] + w[j + 2],
+                             v[j + 3] + w[j + 3]));
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"n"(kCtBuilders) : "memory");
+      if (bt == 0) {
+        const unsigned tk = atomicAdd(&sp.tickets[tile], 1u);
+        s_last = tk == gridDim.z - 1u;
+        if (s_last) sp.tickets[tile] = 0u;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kCtBuilders) : "memory");
+      final_cta = s_last != 0;
+      if (final_cta) __threadfence();
+    }
+    if (final_cta) {
+      const float* base = sp.ws + ((long long)tile * gridDim.z * kCtRows + r) * kCtCols;
+      for (int c0 = cbeg; c0 < cbeg + kCtCols / 2; c0 += 16) {
+        if (t0 + c0 >= a.lin) break;  // warp-uniform
+        float v[16], w[16];
+        if (gridDim.z == 1) {
+          tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)c0, v);
+          tmem_ld16(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(c0 + kCtCols), w);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] += w[j];
         } else {
-          a.y[at] = o;
-          if (a.y2) a.y2[at] = snake_f(o, sa, sb);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0.f;
+          for (unsigned z = 0; z < gridDim.z; ++z) {
+            const float* q = base + (long long)z * kCtRows * kCtCols + c0;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              const float4 f = __ldcg(reinterpret_cast<const float4*>(q + j));
+              v[j] += f.x; v[j + 1] += f.y; v[j + 2] += f.z; v[j + 3] += f.w;
+            }
+          }
+        }
+        if (!row_ok) continue;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int tt = t0 + c0 + j;
+          if (tt >= a.lin) break;
+          float o = v[j] + b;
+          if (a.epi & CEPI_GELU) o = 0.5f * o * (1.0f + erff(o * 0.7071067811865476f));
+          const long long at = (long long)co * lout + (long long)tt * a.ostride + ph;
+          if (a.epi & CEPI_RESID) o = a.resid[at] + o * rs;
+          if (a.epi & CEPI_CLAMP) o = fminf(fmaxf(o, -1.0f), 1.0f);
+          if (a.epi & CEPI_SNAKE) {
+            a.y[at] = snake_f(o, sa, sb);
+          } else {
+            a.y[at] = o;
+            if (a.y2) a.y2[at] = snake_f(o, sa, sb);
+          }
         }
       }
     }
@@ -274,9 +327,9 @@ __global__ void k_split_hi_lo(const float* w, int rows, int ci, int taps, int ci
 }
 
 template <int ACT>
-cudaError_t launch_ct(const CodecTcWeight& w, const CodecConvArgs& a, int* err, dim3 grid,
-                      cudaStream_t stream) {
-  k_codec_conv_tc<ACT><<<grid, kCtThreads, kCtSmem, stream>>>(w.mh, w.ml, a, w.cip, err);
+cudaError_t launch_ct(const CodecTcWeight& w, const CodecConvArgs& a, int* err,
+                      const CodecTcSplit& sp, dim3 grid, cudaStream_t stream) {
+  k_codec_conv_tc<ACT><<<grid, kCtThreads, kCtSmem, stream>>>(w.mh, w.ml, a, w.cip, err, sp);
   return cudaGetLastError();
 }
 
@@ -322,15 +375,26 @@ bool codec_tc_supported(const CodecConvArgs& a, const CodecTcWeight& w) {
 }
 
 cudaError_t codec_conv_tc(const CodecConvArgs& a, const CodecTcWeight& w, int* err,
-                          cudaStream_t stream) {
+                          const CodecTcSplit* split, cudaStream_t stream) {
   if (a.ci <= 0 || a.co <= 0 || a.lin <= 0 || a.taps <= 0 || a.nphase <= 0 || a.ostride <= 0 ||
       a.hist < 0 || !codec_tc_supported(a, w))
     return cudaErrorInvalidValue;
-  const dim3 grid((unsigned)((a.lin + kCtCols - 1) / kCtCols) * a.nphase,
-                  (unsigned)((a.co + kCtRows - 1) / kCtRows), 1);
-  if (a.act == CACT_SNAKE) return launch_ct<CACT_SNAKE>(w, a, err, grid, stream);
-  if (a.act == CACT_SWIGLU) return launch_ct<CACT_SWIGLU>(w, a, err, grid, stream);
-  return launch_ct<CACT_NONE>(w, a, err, grid, stream);
+  dim3 grid((unsigned)((a.lin + kCtCols - 1) / kCtCols) * a.nphase,
+            (unsigned)((a.co + kCtRows - 1) / kCtRows), 1);
+  // Few tiles (short inputs: streamed chunks, the pre-transformer) leave most
+  // SMs idle while each CTA walks the whole K range: split K so that about
+  // one CTA runs per SM, keeping at least two K steps per split.
+  CodecTcSplit sp = split ? *split : CodecTcSplit{};
+  const int tiles = (int)(grid.x * grid.y);
+  const int nk = a.taps * w.cip / kCtK;
+  if (sp.ws && sp.tickets && sp.sms > 0 && 2 * tiles <= sp.sms) {
+    int splits = std::min({sp.sms / tiles, nk / 2, kCodecTcMaxSplits});
+    while (splits > 1 && (size_t)tiles * splits * kCtRows * kCtCols > sp.ws_floats) --splits;
+    if (splits > 1 && tiles <= sp.max_tiles) grid.z = splits;
+  }
+  if (a.act == CACT_SNAKE) return launch_ct<CACT_SNAKE>(w, a, err, sp, grid, stream);
+  if (a.act == CACT_SWIGLU) return launch_ct<CACT_SWIGLU>(w, a, err, sp, grid, stream);
+  return launch_ct<CACT_NONE>(w, a, err, sp, grid, stream);
 }
 
 }  // namespace qtts

@@ -397,6 +397,18 @@ class Codec {
     f_w_ = up(get("decoder.decoder.6.conv.weight", {1, kFinal, 7}));
     f_b_ = vec("decoder.decoder.6.conv.bias", 1);
     err_ = arena_.alloc<int>(1);
+    {
+      // split-K workspace of the tensor-core convolutions (one partial tile
+      // per SM) and the tiles' tickets
+      int dev = 0, sms = 0;
+      QCK(cudaGetDevice(&dev));
+      QCK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+      split_.sms = sms;
+      split_.max_tiles = sms;
+      split_.ws_floats = (size_t)sms * 128 * 128;
+      split_.ws = arena_.alloc<float>(split_.ws_floats);
+      split_.tickets = arena_.alloc<unsigned>(sms);
+    }
     // Tensor-core copies (bf16 hi + lo) of every convolution weight with at
     // least 64 output channels (QTTS_CODEC_TC=0: CUDA-core kernel only).
     const char* tz = std::getenv("QTTS_CODEC_TC");
@@ -688,7 +700,7 @@ class Codec {
                     resid, rscale, out_a, out_b, y2, hist};
     auto it = tc_w_.find(w);
     if (it != tc_w_.end() && codec_tc_supported(a, it->second)) {
-      QCK(codec_conv_tc(a, it->second, err_, stream_));
+      QCK(codec_conv_tc(a, it->second, err_, &split_, stream_));
       ++tc_launches;
     } else {
       QCK(codec_conv(a, stream_));
@@ -760,6 +772,7 @@ class Codec {
   int cap_ = 0;
   size_t ws_bytes_ = 0;
   int* err_ = nullptr;  // tensor-core pipeline status (nonzero: a wait ran out)
+  CodecTcSplit split_;
   std::unordered_map<const float*, CodecTcWeight> tc_w_;
 };
 
