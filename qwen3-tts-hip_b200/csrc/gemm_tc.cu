@@ -183,6 +183,10 @@ __global__ void __launch_bounds__(kTcThreads, BN <= 16 ? 2 : 1)
   } else if (warp >= 2) {
     const int et = threadIdx.x - 64;  // 0..127 over the activation / epilogue warps
     pdl_wait();
+    // Dependents may launch once every CTA is past its wait: their weight
+    // tiles then stream in while this GEMM runs (they still wait for its end
+    // before reading its output).
+    if (et == 0) pdl_trigger();
     const bool halted = a.halt && __ldcg(a.halt);
     // ---- activation producer: hi/lo tiles of gamma * x for every K step ----
     // thread et owns 16-byte chunk c = et % 8 (8 consecutive K) of rows et / 8 + 16 j
