@@ -170,18 +170,24 @@ __global__ void k_codec_rvq_gather(const int32_t* codes, int frames, int groups,
   }
 }
 
+// One warp per output (channel c, frame t): lanes split the codebook
+// dimension (coalesced weight and embedding rows), then a warp reduction.
 __global__ void k_codec_rvq_project(const float* first, const float* rest, const float* wf,
                                     const float* wr, int frames, int cb_dim, int out_dim,
                                     float* y) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= frames * out_dim) return;
-  const int t = idx % frames, c = idx / frames;
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long long)frames * out_dim) return;
+  const int t = (int)(w % frames), c = (int)(w / frames);
+  const float* a = wf + (long long)c * cb_dim;
+  const float* b = wr + (long long)c * cb_dim;
+  const float* f = first + (long long)t * cb_dim;
+  const float* r = rest + (long long)t * cb_dim;
   float s = 0.f;
-  for (int d = 0; d < cb_dim; ++d) {
-    s += wf[(long long)c * cb_dim + d] * first[(long long)t * cb_dim + d];
-    s += wr[(long long)c * cb_dim + d] * rest[(long long)t * cb_dim + d];
-  }
-  y[(long long)c * frames + t] = s;
+  for (int d = lane; d < cb_dim; d += 32) s += a[d] * f[d] + b[d] * r[d];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) y[(long long)c * frames + t] = s;
 }
 
 // 32 time steps per CTA (one per lane, so every load is a coalesced 128-byte
@@ -292,34 +298,67 @@ __global__ void k_codec_qkv_rope(const float* qkv, int heads, int hd, int T, int
   v[at] = qkv[(long long)(2 * qo + h * hd + d) * T + t];
 }
 
-// One warp per (head, query position): online softmax over cached keys
-// 0 .. pos0 + t; lane l holds dims l and l + 32 (head_dim 64).
+// One warp per (head, query position), keys in chunks of 32 with one key per
+// lane: a lane scores its key against the whole query (q in registers), the
+// warp updates the online softmax once per chunk, and lane l accumulates
+// output dims 2l, 2l + 1 with the chunk's weights broadcast by shuffles.
 __global__ void k_codec_attention(const float* q, const float* k, const float* v, int heads,
                                   int T, int pos0, int cap, float scale, float* out) {
   constexpr int HD = 64;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= heads * T) return;
   const int h = warp / T, t = warp % T;
-  const float* qr = q + ((long long)h * T + t) * HD;
-  const float q0 = qr[lane], q1 = qr[lane + 32];
-  float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
-  for (int j = 0; j <= pos0 + t; ++j) {
-    const float* kr = k + ((long long)h * cap + j) * HD;
-    float s = q0 * kr[lane] + q1 * kr[lane + 32];
+  const float4* qr = reinterpret_cast<const float4*>(q + ((long long)h * T + t) * HD);
+  float4 qv[HD / 4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    s *= scale;
-    const float mn = fmaxf(m, s);
-    const float corr = expf(m - mn), e = expf(s - mn);
-    const float* vr = v + ((long long)h * cap + j) * HD;
-    l = l * corr + e;
-    a0 = a0 * corr + e * vr[lane];
-    a1 = a1 * corr + e * vr[lane + 32];
+  for (int i = 0; i < HD / 4; ++i) {
+    qv[i] = __ldg(qr + i);  // the same row in every lane: broadcast
+    qv[i].x *= scale; qv[i].y *= scale; qv[i].z *= scale; qv[i].w *= scale;
+  }
+  const float* kh = k + (long long)h * cap * HD;
+  const float* vh = v + (long long)h * cap * HD;
+  const int n = pos0 + t + 1;  // keys 0 .. pos0 + t
+  float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
+  for (int j0 = 0; j0 < n; j0 += 32) {
+    const int j = j0 + lane;
+    float sc = -INFINITY;
+    if (j < n) {
+      const float4* kr = reinterpret_cast<const float4*>(kh + (long long)j * HD);
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < HD / 4; i += 2) {
+        const float4 a = __ldg(kr + i), b = __ldg(kr + i + 1);
+        s0 = fmaf(qv[i].x, a.x, s0); s0 = fmaf(qv[i].y, a.y, s0);
+        s0 = fmaf(qv[i].z, a.z, s0); s0 = fmaf(qv[i].w, a.w, s0);
+        s1 = fmaf(qv[i + 1].x, b.x, s1); s1 = fmaf(qv[i + 1].y, b.y, s1);
+        s1 = fmaf(qv[i + 1].z, b.z, s1); s1 = fmaf(qv[i + 1].w, b.w, s1);
+      }
+      sc = s0 + s1;
+    }
+    float cm = sc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+    const float mn = fmaxf(m, cm);
+    const float corr = expf(m - mn);
+    const float e = j < n ? expf(sc - mn) : 0.f;
+    float es = e;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) es += __shfl_xor_sync(0xffffffffu, es, o);
+    l = l * corr + es;
+    a0 *= corr;
+    a1 *= corr;
+    const int cnt = min(32, n - j0);
+    for (int jj = 0; jj < cnt; ++jj) {
+      const float w = __shfl_sync(0xffffffffu, e, jj);
+      const float2 vv = __ldg(reinterpret_cast<const float2*>(vh + (long long)(j0 + jj) * HD) + lane);
+      a0 = fmaf(w, vv.x, a0);
+      a1 = fmaf(w, vv.y, a1);
+    }
     m = mn;
   }
   const float il = 1.0f / l;
-  out[(long long)(h * HD + lane) * T + t] = a0 * il;
-  out[(long long)(h * HD + lane + 32) * T + t] = a1 * il;
+  out[(long long)(h * HD + 2 * lane) * T + t] = a0 * il;
+  out[(long long)(h * HD + 2 * lane + 1) * T + t] = a1 * il;
 }
 
 __global__ void k_codec_exp(const float* x, int n, float* y) {
@@ -371,7 +410,7 @@ cudaError_t codec_rvq(const int32_t* codes, int frames, int groups, int cb_size,
                       cudaStream_t stream) {
   k_codec_rvq_gather<<<frames, 256, 0, stream>>>(codes, frames, groups, cb_size, cb_dim,
                                                  cb_first, cb_rest, first, rest);
-  k_codec_rvq_project<<<blocks((long long)frames * out_dim, 256), 256, 0, stream>>>(
+  k_codec_rvq_project<<<blocks((long long)frames * out_dim * 32, 256), 256, 0, stream>>>(
       first, rest, wf, wr, frames, cb_dim, out_dim, y);
   return cudaGetLastError();
 }
