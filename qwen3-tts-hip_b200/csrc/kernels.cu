@@ -835,39 +835,63 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
         vf[i][2] = bf16lo(vu[i].y); vf[i][3] = bf16hi(vu[i].y);
       }
     }
-    float d[G][kAttnBatch];
+    // partial scores of this lane's 4 dims, d[8 g + i] for q head g, position p0 + i
+    constexpr int V = G * kAttnBatch;
+    static_assert((V & (V - 1)) == 0 && V <= 32, "scores per batch: a power of two <= 32");
+    float d[V];
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
       for (int i = 0; i < kAttnBatch; ++i)
-        d[g][i] = q[g][0] * kf[i][0] + q[g][1] * kf[i][1] + q[g][2] * kf[i][2] + q[g][3] * kf[i][3];
+        d[kAttnBatch * g + i] =
+            q[g][0] * kf[i][0] + q[g][1] * kf[i][1] + q[g][2] * kf[i][2] + q[g][3] * kf[i][3];
+    // Reduce-scatter over lane bits below V: a lane keeps the half its bit
+    // selects plus its partner's copy, ending with score (lane % V) summed
+    // over those lanes; the remaining lane bits finish the sum.
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
+    for (int w = V / 2; w >= 1; w >>= 1) {
+      const bool upper = (lane & w) != 0;
 #pragma unroll
-      for (int g = 0; g < G; ++g)
+      for (int u = 0; u < w; ++u) {
+        const float send = upper ? d[u] : d[u + w];
+        const float keep = upper ? d[u + w] : d[u];
+        d[u] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+      }
+    }
+    float sc = d[0];
 #pragma unroll
-        for (int i = 0; i < kAttnBatch; ++i) d[g][i] += __shfl_xor_sync(0xffffffffu, d[g][i], o);
+    for (int o = V; o < 32; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+    const int bi = lane & (kAttnBatch - 1);  // position within the batch of this lane's score
+    if (p0 + bi >= T) sc = -INFINITY;
+    // per q head (kAttnBatch consecutive lanes): the batch max, then the sum
+    float gm = sc;
+#pragma unroll
+    for (int o = kAttnBatch / 2; o > 0; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+    const int myg = (lane % V) / kAttnBatch;
+    float mbs[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) mbs[g] = fmaxf(m[g], __shfl_sync(0xffffffffu, gm, kAttnBatch * g));
+    float mine = mbs[0];
+#pragma unroll
+    for (int g = 1; g < G; ++g)
+      if (myg == g) mine = mbs[g];
+    const float pe = p0 + bi < T ? expf(sc - mine) : 0.f;
+    float ls = pe;
+#pragma unroll
+    for (int o = kAttnBatch / 2; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float mb = m[g];
+      const float corr = expf(m[g] - mbs[g]);  // m = -inf on the first batch: corr = 0
+      l[g] = l[g] * corr + __shfl_sync(0xffffffffu, ls, kAttnBatch * g);
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) acc[g][jj] *= corr;
 #pragma unroll
       for (int i = 0; i < kAttnBatch; ++i) {
-        if (p0 + i >= T) d[g][i] = -INFINITY;
-        mb = fmaxf(mb, d[g][i]);
+        const float w = __shfl_sync(0xffffffffu, pe, kAttnBatch * g + i);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) acc[g][jj] = fmaf(w, vf[i][jj], acc[g][jj]);
       }
-      const float corr = expf(m[g] - mb);  // m = -inf on the first batch: corr = 0
-      float ls = 0.f, av[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int i = 0; i < kAttnBatch; ++i) {
-        const float pe = expf(d[g][i] - mb);
-        ls += pe;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) av[j] = fmaf(pe, vf[i][j], av[j]);
-      }
-      l[g] = l[g] * corr + ls;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[g][j] = acc[g][j] * corr + av[j];
-      m[g] = mb;
+      m[g] = mbs[g];
     }
 #pragma unroll
     for (int i = 0; i < kAttnBatch; ++i) { ku[i] = nk[i]; vu[i] = nv[i]; }
