@@ -844,6 +844,13 @@ class Engine {
   };
   // CodePredictor attention inside the O projection (QTTS_FUSE_ATTN_O=0: separate kernels)
   bool fuse_attn_o = true;
+  // Layer-0 projections of every CodePredictor input token (groups 1..14 take
+  // the previous group's token embedding as their input, so its QKV row depends
+  // on the token alone): [groups-2][vocab][qkv_w], computed at load with the
+  // tensor-core GEMM; the heads copy the selected row. Off with
+  // QTTS_CP_QKV_TABLE=0 and for models with the CodePredictor input projection.
+  float* cp_qkv0 = nullptr;
+  void build_cp_qkv_table();
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
   float last_prefill_ms = 0.f, last_frames_ms = 0.f;
   size_t last_frames = 0;
@@ -915,7 +922,7 @@ class Engine {
   unsigned* crumbs_host = nullptr;  // QTTS_CRUMBS=1: last kernel ids entered / left
   void stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int pos0, const int* halt);
   void stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* pos_ptr, int pos_const,
-                  const int* halt);
+                  const int* halt, bool qkv0_given = false);
   HeadArgs head_args(int role, const SampleCfg& c, const int* halt);
   void talker_head(int role, const float* x, const SampleCfg& c, float penalty, const int* halt,
                    float* cp_prefix_dst);
@@ -1253,6 +1260,8 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
     }
     const char* fz = std::getenv("QTTS_FUSE_ATTN_O");
     fuse_attn_o = !(fz && fz[0] == '0');
+    const char* qz = std::getenv("QTTS_CP_QKV_TABLE");
+    if (!(qz && qz[0] == '0') && !has_proj() && tc.tokens) build_cp_qkv_table();
   }
   {
     // HipCodecInitial::load (codec_hip.rs:214-336); optional here so the
@@ -1349,13 +1358,16 @@ void Engine::stack_rows(DevStack& S, StackBufs& B, const KvView& kv, int M, int 
 }
 
 // One position through all layers (decode_step_layer_on_stream, decode.rs:1694-1894).
+// qkv0_given: layer 0's projections are already in B.qkv (a row of the
+// precomputed CodePredictor table, written by the previous group's head).
 void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* pos_ptr,
-                        int pos_const, const int* halt) {
+                        int pos_const, const int* halt, bool qkv0_given) {
   const StackCfg& c = S.c;
   const float scale = 1.0f / std::sqrt((float)c.head_dim);
   for (int l = 0; l < c.layers; ++l) {
-    linear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr, 1,
-           S.qkv_w, c.hidden, EPI_STORE, halt);
+    if (!(l == 0 && qkv0_given))
+      linear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr, 1,
+             S.qkv_w, c.hidden, EPI_STORE, halt);
     AttnDecodeArgs da{B.qkv,   S.q_g[l],  S.k_g[l], c.eps,   S.rope_cos, S.rope_sin,
                       kv,      l,         pos_ptr,  pos_const, c.q_heads, scale,
                       B.attn,  halt};
@@ -1424,6 +1436,11 @@ void Engine::cp_head(int group, const float* x, const SampleCfg& c, const int* h
   a.step_in = tb.x;
   a.trailing = trailing;
   a.tts_pad = tts_pad;
+  if (cp_qkv0 && group < C.groups - 2) {
+    a.qkv_table = cp_qkv0 + (size_t)group * C.vocab * cp.qkv_w;
+    a.qkv_out = cb.qkv;
+    a.qkv_w = cp.qkv_w;
+  }
   a.lin.trace_id = trace_tag("cp head+select", C.vocab, C.hidden);
   QCK(launch_head(a, stream));
   ++launches;
@@ -1444,13 +1461,36 @@ void Engine::enqueue_frame(const SampleKey& k) {
     if (has_proj())
       linear(proj_w, cp_next, H, nullptr, 0.f, cb.x, C.hidden, nullptr, 0, proj_b, 1, C.hidden,
              H, EPI_BIAS, halt);
-    stack_step(cp, cb, ckv, nullptr, g + 1, halt);
+    stack_step(cp, cb, ckv, nullptr, g + 1, halt, cp_qkv0 != nullptr);
     cp_head(g, cb.x, k.s, halt);
   }
   if (!k.last) {
     stack_step(talker, tb, tkv, &st->talker_pos, 0, halt);
     talker_head(ROLE_TALKER_STEP, tb.x, k.t, k.penalty, halt, cp_prefix_target());
   }
+}
+
+// Layer-0 QKV rows of every CodePredictor input token: the rows of group g's
+// embedding table (bf16, widened to fp32) through the input RMSNorm and the
+// QKV projection of CodePredictor layer 0, one tensor-core GEMM per group.
+void Engine::build_cp_qkv_table() {
+  const StackCfg& C = cfg.cp;
+  const int V = C.vocab, H = cfg.talker.hidden, W = cp.qkv_w;
+  const int n = C.groups - 2;  // heads 0 .. groups-3 feed groups 1 .. groups-2
+  if (n <= 0 || H != C.hidden) return;
+  cp_qkv0 = arena.alloc<float>((size_t)n * V * W);
+  float* rows = arena.alloc<float>((size_t)V * H);
+  int* ids = arena.alloc<int>(V);
+  std::vector<int> iv(V);
+  for (int i = 0; i < V; ++i) iv[i] = i;
+  h2d(ids, iv.data(), (size_t)V * 4);
+  TcScope tcs(tc_scope, true);
+  for (int g = 0; g < n; ++g) {
+    QCK(launch_gather_rows(cp_embs + (size_t)g * V * H, ids, V, H, rows, stream));
+    linear(cp.wqkv[0], rows, H, cp.in_g[0], C.eps, cp_qkv0 + (size_t)g * V * W, W, nullptr, 0,
+           nullptr, V, W, H, EPI_STORE, nullptr);
+  }
+  stream_sync();
 }
 
 cudaGraphExec_t Engine::frame_graph(const SampleKey& k) {
@@ -2798,7 +2838,7 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
       if (e.has_proj())
         e.linear(e.proj_w, e.cp_next, H, nullptr, 0.f, e.cb.x, C.hidden, nullptr, 0, e.proj_b, 1,
                  C.hidden, H, qtts::EPI_BIAS, nullptr);
-      e.stack_step(e.cp, e.cb, e.ckv, nullptr, g + 1, nullptr);
+      e.stack_step(e.cp, e.cb, e.ckv, nullptr, g + 1, nullptr, e.cp_qkv0 != nullptr);
       e.cp_head(g, e.cb.x, sc, nullptr);
       QCK(cudaMemcpyAsync(e.dbg_logits + (size_t)g * C.vocab, e.logits, C.vocab * 4,
                                 cudaMemcpyDeviceToDevice, e.stream));

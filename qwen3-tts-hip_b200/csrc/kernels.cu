@@ -613,6 +613,12 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
       if (tok == a.eos_token) a.st->halt = 1;
     }
   } else if (cp) {
+    if (a.qkv_table) {
+      // the next group's layer-0 projections: a row of the precomputed table
+      const float4* src = reinterpret_cast<const float4*>(a.qkv_table + (long long)tok * a.qkv_w);
+      float4* dst = reinterpret_cast<float4*>(a.qkv_out);
+      for (int i = tid; i < a.qkv_w / 4; i += kThreads) dst[i] = __ldg(src + i);
+    }
     const __nv_bfloat16* e = a.cp_emb + (long long)tok * H;
     uint2 ev[kIt];
 #pragma unroll

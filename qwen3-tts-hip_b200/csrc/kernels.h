@@ -97,6 +97,11 @@ struct HeadArgs {
   int* token_out;          // optional: selected token
   int frames_cap;          // > 0: checked bound of the frame counter (codes rows)
   int talker_vocab;        // > 0: checked bound of the semantic token
+  // optional: the next group's layer-0 QKV row of every token of this
+  // group's vocab ([Vcp, qkv_w]); the selected token's row is copied to qkv_out
+  const float* qkv_table;
+  float* qkv_out;
+  int qkv_w;
 };
 
 // Batched heads: per-sequence views of `h` at the given element strides;
