@@ -847,9 +847,11 @@ class Engine {
   // Layer-0 projections of every CodePredictor input token (groups 1..14 take
   // the previous group's token embedding as their input, so its QKV row depends
   // on the token alone): [groups-2][vocab][qkv_w], computed at load with the
-  // tensor-core GEMM; the heads copy the selected row. Off with
-  // QTTS_CP_QKV_TABLE=0 and for models with the CodePredictor input projection.
+  // tensor-core GEMM; the heads copy the selected row (and, for models with
+  // the CodePredictor input projection, the projected input row, cp_x0).
+  // Off with QTTS_CP_QKV_TABLE=0.
   float* cp_qkv0 = nullptr;
+  float* cp_x0 = nullptr;  // with the input projection: [groups-2][vocab][cp hidden] projected rows
   void build_cp_qkv_table();
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
   float last_prefill_ms = 0.f, last_frames_ms = 0.f;
@@ -1261,7 +1263,7 @@ Engine::Engine(const std::string& dir, int dev, size_t mcs) : max_cache_steps(mc
     const char* fz = std::getenv("QTTS_FUSE_ATTN_O");
     fuse_attn_o = !(fz && fz[0] == '0');
     const char* qz = std::getenv("QTTS_CP_QKV_TABLE");
-    if (!(qz && qz[0] == '0') && !has_proj() && tc.tokens) build_cp_qkv_table();
+    if (!(qz && qz[0] == '0') && tc.tokens) build_cp_qkv_table();
   }
   {
     // HipCodecInitial::load (codec_hip.rs:214-336); optional here so the
@@ -1440,6 +1442,11 @@ void Engine::cp_head(int group, const float* x, const SampleCfg& c, const int* h
     a.qkv_table = cp_qkv0 + (size_t)group * C.vocab * cp.qkv_w;
     a.qkv_out = cb.qkv;
     a.qkv_w = cp.qkv_w;
+    if (cp_x0) {
+      a.x_table = cp_x0 + (size_t)group * C.vocab * C.hidden;
+      a.x_out = cb.x;
+      a.x_w = C.hidden;
+    }
   }
   a.lin.trace_id = trace_tag("cp head+select", C.vocab, C.hidden);
   QCK(launch_head(a, stream));
@@ -1458,7 +1465,7 @@ void Engine::enqueue_frame(const SampleKey& k) {
   stack_rows(cp, cb, ckv, 2, 0, halt);
   cp_head(0, cb.x + C.hidden, k.s, halt);
   for (int g = 1; g < C.groups - 1; ++g) {
-    if (has_proj())
+    if (has_proj() && !cp_x0)
       linear(proj_w, cp_next, H, nullptr, 0.f, cb.x, C.hidden, nullptr, 0, proj_b, 1, C.hidden,
              H, EPI_BIAS, halt);
     stack_step(cp, cb, ckv, nullptr, g + 1, halt, cp_qkv0 != nullptr);
@@ -1475,10 +1482,11 @@ void Engine::enqueue_frame(const SampleKey& k) {
 // QKV projection of CodePredictor layer 0, one tensor-core GEMM per group.
 void Engine::build_cp_qkv_table() {
   const StackCfg& C = cfg.cp;
-  const int V = C.vocab, H = cfg.talker.hidden, W = cp.qkv_w;
+  const int V = C.vocab, H = cfg.talker.hidden, Hc = C.hidden, W = cp.qkv_w;
   const int n = C.groups - 2;  // heads 0 .. groups-3 feed groups 1 .. groups-2
-  if (n <= 0 || H != C.hidden) return;
+  if (n <= 0 || (!has_proj() && H != Hc)) return;
   cp_qkv0 = arena.alloc<float>((size_t)n * V * W);
+  if (has_proj()) cp_x0 = arena.alloc<float>((size_t)n * V * Hc);
   float* rows = arena.alloc<float>((size_t)V * H);
   int* ids = arena.alloc<int>(V);
   std::vector<int> iv(V);
@@ -1487,8 +1495,15 @@ void Engine::build_cp_qkv_table() {
   TcScope tcs(tc_scope, true);
   for (int g = 0; g < n; ++g) {
     QCK(launch_gather_rows(cp_embs + (size_t)g * V * H, ids, V, H, rows, stream));
-    linear(cp.wqkv[0], rows, H, cp.in_g[0], C.eps, cp_qkv0 + (size_t)g * V * W, W, nullptr, 0,
-           nullptr, V, W, H, EPI_STORE, nullptr);
+    const float* x = rows;
+    if (has_proj()) {  // small_to_mtp_projection of every token (code_predictor.rs:754-817)
+      float* xg = cp_x0 + (size_t)g * V * Hc;
+      linear(proj_w, rows, H, nullptr, 0.f, xg, Hc, nullptr, 0, proj_b, V, Hc, H, EPI_BIAS,
+             nullptr);
+      x = xg;
+    }
+    linear(cp.wqkv[0], x, Hc, cp.in_g[0], C.eps, cp_qkv0 + (size_t)g * V * W, W, nullptr, 0,
+           nullptr, V, W, Hc, EPI_STORE, nullptr);
   }
   stream_sync();
 }
@@ -2835,7 +2850,7 @@ int32_t qtts_code_predictor(qtts_engine* h, const float* talker_hidden, const fl
     e.cp_head(0, e.cb.x + C.hidden, sc, nullptr);
     QCK(cudaMemcpyAsync(e.dbg_logits, e.logits, C.vocab * 4, cudaMemcpyDeviceToDevice, e.stream));
     for (int g = 1; g < C.groups - 1; ++g) {
-      if (e.has_proj())
+      if (e.has_proj() && !e.cp_x0)
         e.linear(e.proj_w, e.cp_next, H, nullptr, 0.f, e.cb.x, C.hidden, nullptr, 0, e.proj_b, 1,
                  C.hidden, H, qtts::EPI_BIAS, nullptr);
       e.stack_step(e.cp, e.cb, e.ckv, nullptr, g + 1, nullptr, e.cp_qkv0 != nullptr);

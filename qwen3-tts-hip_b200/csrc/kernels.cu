@@ -618,6 +618,11 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
       const float4* src = reinterpret_cast<const float4*>(a.qkv_table + (long long)tok * a.qkv_w);
       float4* dst = reinterpret_cast<float4*>(a.qkv_out);
       for (int i = tid; i < a.qkv_w / 4; i += kThreads) dst[i] = __ldg(src + i);
+      if (a.x_table) {
+        const float4* xs4 = reinterpret_cast<const float4*>(a.x_table + (long long)tok * a.x_w);
+        float4* xd = reinterpret_cast<float4*>(a.x_out);
+        for (int i = tid; i < a.x_w / 4; i += kThreads) xd[i] = __ldg(xs4 + i);
+      }
     }
     const __nv_bfloat16* e = a.cp_emb + (long long)tok * H;
     uint2 ev[kIt];

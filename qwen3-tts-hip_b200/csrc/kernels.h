@@ -102,6 +102,11 @@ struct HeadArgs {
   const float* qkv_table;
   float* qkv_out;
   int qkv_w;
+  // optional, with qkv_table: the next group's projected input row of every
+  // token ([Vcp, x_w], models with the CodePredictor input projection)
+  const float* x_table;
+  float* x_out;
+  int x_w;
 };
 
 // Batched heads: per-sequence views of `h` at the given element strides;
