@@ -959,7 +959,7 @@ class Engine {
                float* y, int ldy, const float* resid, int ldr, const float* bias, int M, int N,
                int K, Epilogue epi, float* rms_out = nullptr);
   void batch_stack_step(DevStack& S, StackBufs& B, const KvView& kv, int pt_stride,
-                        const int* pos_ptr, int pos_const, int nb);
+                        const int* pos_ptr, int pos_const, int nb, bool qkv0_given = false);
   void batch_head(int role, int group, const float* x, const SampleCfg& c, float penalty, int nb);
   void enqueue_batch_frame(const SampleKey& k, int nb);
   cudaGraphExec_t batch_graph(const SampleKey& k, int nb);
@@ -1846,12 +1846,13 @@ void Engine::blinear(const __nv_bfloat16* W, const float* x, int ldx, const floa
 
 // One position through all layers for nb sequences (rows of B.x).
 void Engine::batch_stack_step(DevStack& S, StackBufs& B, const KvView& kv, int pt_stride,
-                              const int* pos_ptr, int pos_const, int nb) {
+                              const int* pos_ptr, int pos_const, int nb, bool qkv0_given) {
   const StackCfg& c = S.c;
   const float scale = 1.0f / std::sqrt((float)c.head_dim);
   for (int l = 0; l < c.layers; ++l) {
-    blinear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr, nb,
-            S.qkv_w, c.hidden, EPI_STORE);
+    if (!(l == 0 && qkv0_given))  // else: rows of the precomputed table, written by the heads
+      blinear(S.wqkv[l], B.x, c.hidden, S.in_g[l], c.eps, B.qkv, S.qkv_w, nullptr, 0, nullptr,
+              nb, S.qkv_w, c.hidden, EPI_STORE);
     AttnDecodeArgs da{};
     da.qkv = B.qkv;
     da.q_gamma = S.q_g[l];
@@ -1932,6 +1933,18 @@ void Engine::batch_head(int role, int group, const float* x, const SampleCfg& c,
   bh.next_stride = has_proj() ? T.hidden : C.hidden;
   bh.step_stride = T.hidden;
   bh.trail_stride = (long long)(max_cache_steps + 1) * T.hidden;
+  if (!talker_role && cp_qkv0 && group < C.groups - 2) {
+    a.qkv_table = cp_qkv0 + (size_t)group * C.vocab * cp.qkv_w;
+    a.qkv_out = bt.cb.qkv;
+    a.qkv_w = cp.qkv_w;
+    bh.qkv_stride = cp.qkv_w;
+    if (cp_x0) {
+      a.x_table = cp_x0 + (size_t)group * C.vocab * C.hidden;
+      a.x_out = bt.cb.x;
+      a.x_w = C.hidden;
+      bh.x_stride = C.hidden;
+    }
+  }
   QCK(launch_select_batch(bh, nb, stream));
   ++launches;
 }
@@ -1956,10 +1969,10 @@ void Engine::enqueue_batch_frame(const SampleKey& k, int nb) {
   }
   batch_head(ROLE_CP_GROUP, 0, bt.cb.x, k.s, 1.0f, nb);
   for (int g = 1; g < C.groups - 1; ++g) {
-    if (has_proj())
+    if (has_proj() && !cp_x0)
       blinear(proj_w, bt.cp_next, (int)H, nullptr, 0.f, bt.cb.x, C.hidden, nullptr, 0, proj_b, nb,
               C.hidden, (int)H, EPI_BIAS);
-    batch_stack_step(cp, bt.cb, bt.ckv, 1, nullptr, g + 1, nb);
+    batch_stack_step(cp, bt.cb, bt.ckv, 1, nullptr, g + 1, nb, cp_qkv0 != nullptr);
     batch_head(ROLE_CP_GROUP, g, bt.cb.x, k.s, 1.0f, nb);
   }
   if (!k.last) {

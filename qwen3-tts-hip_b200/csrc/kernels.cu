@@ -707,6 +707,8 @@ __global__ void __launch_bounds__(kThreads) k_select_batch(BatchHeadArgs bh) {
   if (a.emb_sum) a.emb_sum += (long long)b * a.H;
   if (a.step_in) a.step_in += (long long)b * bh.step_stride;
   if (a.trailing) a.trailing += (long long)b * bh.trail_stride;
+  if (a.qkv_out) a.qkv_out += (long long)b * bh.qkv_stride;
+  if (a.x_out) a.x_out += (long long)b * bh.x_stride;
   a.token_out = nullptr;
   head_select_act(a, bh.logits + (long long)b * bh.logits_ld, __ldcg(bh.rms + b), smem);
 }

@@ -117,6 +117,7 @@ struct BatchHeadArgs {
   int logits_ld;
   const float* rms;        // [B]
   long long hist_stride, codes_stride, next_stride, step_stride, trail_stride;
+  long long qkv_stride, x_stride;  // per-sequence rows of h.qkv_out / h.x_out
 };
 
 struct AttnDecodeArgs {
