@@ -4,6 +4,7 @@
 #include <math.h>
 
 #include "codec.h"
+#include "common.cuh"
 
 namespace qtts {
 namespace {
@@ -39,6 +40,8 @@ __device__ __forceinline__ float snake(float x, float a, float b) {
 // im2col) with the input transform applied once per loaded element.
 template <int ACT, int TAPS, int BM>  // TAPS 0: taps read at run time
 __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  pdl_trigger();
   constexpr int MR = BM / 16, AL = BM * kTileK / kConvThreads;
   static_assert(AL >= 1 && MR >= 1, "row tile must give every thread an A element");
   const int taps = TAPS ? TAPS : a.taps;
@@ -154,6 +157,8 @@ __global__ void __launch_bounds__(kConvThreads) k_codec_conv(CodecConvArgs a) {
 __global__ void k_codec_rvq_gather(const int32_t* codes, int frames, int groups, int cb_size,
                                    int cb_dim, const float* cb_first, const float* cb_rest,
                                    float* first, float* rest) {
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  pdl_trigger();
   const int t = blockIdx.x;
   if (t >= frames) return;
   auto code_of = [&](int g) {
@@ -175,6 +180,8 @@ __global__ void k_codec_rvq_gather(const int32_t* codes, int frames, int groups,
 __global__ void k_codec_rvq_project(const float* first, const float* rest, const float* wf,
                                     const float* wr, int frames, int cb_dim, int out_dim,
                                     float* y) {
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  pdl_trigger();
   const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= (long long)frames * out_dim) return;
@@ -199,6 +206,8 @@ __global__ void __launch_bounds__(kNormWarps * 32) k_codec_chan_norm(const float
                                                                   const float* gamma,
                                                                   const float* beta, float eps,
                                                                   float* y) {
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  pdl_trigger();
   __shared__ float s_sum[kNormWarps][33], s_sq[kNormWarps][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t = blockIdx.x * 32 + lane;
@@ -248,6 +257,8 @@ __global__ void __launch_bounds__(kNormWarps * 32) k_codec_chan_norm(const float
 
 __global__ void k_codec_dwconv(const float* x, int C, int T, int hist, const float* w,
                                const float* b, int K, float* y) {
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  pdl_trigger();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= C * T) return;
   const int t = idx % T, c = idx / T;
@@ -264,6 +275,8 @@ __global__ void k_codec_dwconv(const float* x, int C, int T, int hist, const flo
 // the last H columns of cat[c].
 __global__ void k_codec_hist_cat(const float* state_cur, const float* x, int C, int H, int n,
                                  float* cat, float* state_next) {
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  pdl_trigger();
   const long long W = (long long)H + n;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= C * W) return;
@@ -278,6 +291,8 @@ __global__ void k_codec_hist_cat(const float* state_cur, const float* x, int C, 
 // [heads][cap][hd] at those positions.
 __global__ void k_codec_qkv_rope(const float* qkv, int heads, int hd, int T, int pos0, int cap,
                                  float theta, float* q, float* k, float* v) {
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  pdl_trigger();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   const int per = heads * T * hd;
   if (idx >= per) return;
@@ -304,6 +319,8 @@ __global__ void k_codec_qkv_rope(const float* qkv, int heads, int hd, int T, int
 // output dims 2l, 2l + 1 with the chunk's weights broadcast by shuffles.
 __global__ void k_codec_attention(const float* q, const float* k, const float* v, int heads,
                                   int T, int pos0, int cap, float scale, float* out) {
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  pdl_trigger();
   constexpr int HD = 64;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= heads * T) return;
@@ -362,6 +379,8 @@ __global__ void k_codec_attention(const float* q, const float* k, const float* v
 }
 
 __global__ void k_codec_exp(const float* x, int n, float* y) {
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) y[i] = expf(x[i]);
 }
@@ -370,23 +389,23 @@ inline unsigned blocks(long long n, int per) { return (unsigned)((n + per - 1) /
 
 }  // namespace
 
+// Every codec kernel is launched with programmatic dependent launch: it waits
+// for the previous kernel's completion before touching memory and lets the
+// next one launch right away, so a decode's ~350 launches do not each pay the
+// full launch latency.
 template <int BM>
 static cudaError_t codec_conv_bm(const CodecConvArgs& a, cudaStream_t stream) {
   const dim3 grid(blocks(a.lin, kTileT) * a.nphase, blocks(a.co, BM), 1);
-  if (a.act == CACT_SNAKE) {
-    k_codec_conv<CACT_SNAKE, 0, BM><<<grid, kConvThreads, 0, stream>>>(a);
-  } else if (a.act == CACT_SWIGLU) {
-    k_codec_conv<CACT_SWIGLU, 0, BM><<<grid, kConvThreads, 0, stream>>>(a);
-  } else {
-    switch (a.taps) {  // constant taps: the im2col index split is a multiply, not a divide
-      case 1: k_codec_conv<CACT_NONE, 1, BM><<<grid, kConvThreads, 0, stream>>>(a); break;
-      case 2: k_codec_conv<CACT_NONE, 2, BM><<<grid, kConvThreads, 0, stream>>>(a); break;
-      case 3: k_codec_conv<CACT_NONE, 3, BM><<<grid, kConvThreads, 0, stream>>>(a); break;
-      case 7: k_codec_conv<CACT_NONE, 7, BM><<<grid, kConvThreads, 0, stream>>>(a); break;
-      default: k_codec_conv<CACT_NONE, 0, BM><<<grid, kConvThreads, 0, stream>>>(a); break;
-    }
+  const dim3 block(kConvThreads);
+  if (a.act == CACT_SNAKE) return launch(k_codec_conv<CACT_SNAKE, 0, BM>, grid, block, 0, stream, a);
+  if (a.act == CACT_SWIGLU) return launch(k_codec_conv<CACT_SWIGLU, 0, BM>, grid, block, 0, stream, a);
+  switch (a.taps) {  // constant taps: the im2col index split is a multiply, not a divide
+    case 1: return launch(k_codec_conv<CACT_NONE, 1, BM>, grid, block, 0, stream, a);
+    case 2: return launch(k_codec_conv<CACT_NONE, 2, BM>, grid, block, 0, stream, a);
+    case 3: return launch(k_codec_conv<CACT_NONE, 3, BM>, grid, block, 0, stream, a);
+    case 7: return launch(k_codec_conv<CACT_NONE, 7, BM>, grid, block, 0, stream, a);
+    default: return launch(k_codec_conv<CACT_NONE, 0, BM>, grid, block, 0, stream, a);
   }
-  return cudaGetLastError();
 }
 
 cudaError_t codec_conv(const CodecConvArgs& a, cudaStream_t stream) {
@@ -408,54 +427,51 @@ cudaError_t codec_rvq(const int32_t* codes, int frames, int groups, int cb_size,
                       const float* cb_first, const float* cb_rest, const float* wf,
                       const float* wr, int out_dim, float* first, float* rest, float* y,
                       cudaStream_t stream) {
-  k_codec_rvq_gather<<<frames, 256, 0, stream>>>(codes, frames, groups, cb_size, cb_dim,
-                                                 cb_first, cb_rest, first, rest);
-  k_codec_rvq_project<<<blocks((long long)frames * out_dim * 32, 256), 256, 0, stream>>>(
-      first, rest, wf, wr, frames, cb_dim, out_dim, y);
-  return cudaGetLastError();
+  cudaError_t e = launch(k_codec_rvq_gather, dim3(frames), dim3(256), 0, stream, codes, frames,
+                         groups, cb_size, cb_dim, cb_first, cb_rest, first, rest);
+  if (e != cudaSuccess) return e;
+  return launch(k_codec_rvq_project, dim3(blocks((long long)frames * out_dim * 32, 256)),
+                dim3(256), 0, stream, (const float*)first, (const float*)rest, wf, wr, frames,
+                cb_dim, out_dim, y);
 }
 
 cudaError_t codec_chan_norm(const float* x, int C, int T, const float* gamma, const float* beta,
                             float eps, float* y, cudaStream_t stream) {
-  k_codec_chan_norm<<<blocks(T, 32), kNormWarps * 32, 0, stream>>>(x, C, T, gamma, beta, eps, y);
-  return cudaGetLastError();
+  return launch(k_codec_chan_norm, dim3(blocks(T, 32)), dim3(kNormWarps * 32), 0, stream, x, C,
+                T, gamma, beta, eps, y);
 }
 
 cudaError_t codec_dwconv(const float* x, int C, int T, int hist, const float* w, const float* b,
                          int K, float* y, cudaStream_t stream) {
   if (hist < 0 || hist > K - 1) return cudaErrorInvalidValue;
-  k_codec_dwconv<<<blocks((long long)C * T, 256), 256, 0, stream>>>(x, C, T, hist, w, b, K, y);
-  return cudaGetLastError();
+  return launch(k_codec_dwconv, dim3(blocks((long long)C * T, 256)), dim3(256), 0, stream, x, C,
+                T, hist, w, b, K, y);
 }
 
 cudaError_t codec_hist_cat(const float* state_cur, const float* x, int C, int H, int n,
                            float* cat, float* state_next, cudaStream_t stream) {
   if (C <= 0 || H <= 0 || n <= 0) return cudaErrorInvalidValue;
-  k_codec_hist_cat<<<blocks((long long)C * (H + n), 256), 256, 0, stream>>>(state_cur, x, C, H, n,
-                                                                            cat, state_next);
-  return cudaGetLastError();
+  return launch(k_codec_hist_cat, dim3(blocks((long long)C * (H + n), 256)), dim3(256), 0,
+                stream, state_cur, x, C, H, n, cat, state_next);
 }
 
 cudaError_t codec_qkv_rope(const float* qkv, int heads, int hd, int T, int pos0, int cap,
                            float theta, float* q, float* k, float* v, cudaStream_t stream) {
   if (pos0 < 0 || pos0 + T > cap) return cudaErrorInvalidValue;
-  k_codec_qkv_rope<<<blocks((long long)heads * T * hd, 256), 256, 0, stream>>>(
-      qkv, heads, hd, T, pos0, cap, theta, q, k, v);
-  return cudaGetLastError();
+  return launch(k_codec_qkv_rope, dim3(blocks((long long)heads * T * hd, 256)), dim3(256), 0,
+                stream, qkv, heads, hd, T, pos0, cap, theta, q, k, v);
 }
 
 cudaError_t codec_attention(const float* q, const float* k, const float* v, int heads, int hd,
                             int T, int pos0, int cap, float scale, float* out,
                             cudaStream_t stream) {
   if (hd != 64 || pos0 < 0 || pos0 + T > cap) return cudaErrorInvalidValue;
-  k_codec_attention<<<blocks((long long)heads * T * 32, 256), 256, 0, stream>>>(
-      q, k, v, heads, T, pos0, cap, scale, out);
-  return cudaGetLastError();
+  return launch(k_codec_attention, dim3(blocks((long long)heads * T * 32, 256)), dim3(256), 0,
+                stream, q, k, v, heads, T, pos0, cap, scale, out);
 }
 
 cudaError_t codec_exp(const float* x, int n, float* y, cudaStream_t stream) {
-  k_codec_exp<<<blocks(n, 256), 256, 0, stream>>>(x, n, y);
-  return cudaGetLastError();
+  return launch(k_codec_exp, dim3(blocks(n, 256)), dim3(256), 0, stream, x, n, y);
 }
 
 }  // namespace qtts

@@ -154,6 +154,10 @@ __global__ void __launch_bounds__(kCtThreads, 1)
     // K half h = bt / 128 (32 of the step's 64 channels)
     const int bt = threadIdx.x - 64;
     const int et = bt & (kCtCols - 1), h = bt >> 7;
+    // the activations (and the split-K workspace) come from the previous
+    // kernel; the weight tiles above did not wait for it
+    pdl_wait();
+    if (bt == 0) pdl_trigger();
     const int t = t0 + et;
     const long long ld = (long long)a.lin + a.hist;
     const float* xb = a.x + a.hist;
@@ -329,8 +333,8 @@ __global__ void k_split_hi_lo(const float* w, int rows, int ci, int taps, int ci
 template <int ACT>
 cudaError_t launch_ct(const CodecTcWeight& w, const CodecConvArgs& a, int* err,
                       const CodecTcSplit& sp, dim3 grid, cudaStream_t stream) {
-  k_codec_conv_tc<ACT><<<grid, kCtThreads, kCtSmem, stream>>>(w.mh, w.ml, a, w.cip, err, sp);
-  return cudaGetLastError();
+  return launch(k_codec_conv_tc<ACT>, grid, dim3(kCtThreads), kCtSmem, stream, w.mh, w.ml, a,
+                w.cip, err, sp);
 }
 
 template <int ACT>
