@@ -1485,6 +1485,7 @@ void Engine::build_cp_qkv_table() {
   const int V = C.vocab, H = cfg.talker.hidden, Hc = C.hidden, W = cp.qkv_w;
   const int n = C.groups - 2;  // heads 0 .. groups-3 feed groups 1 .. groups-2
   if (n <= 0 || (!has_proj() && H != Hc)) return;
+  if (W > kCpQkvTableMax || W % 4 != 0 || Hc > kCpXTableMax) return;  // widths the heads copy
   cp_qkv0 = arena.alloc<float>((size_t)n * V * W);
   if (has_proj()) cp_x0 = arena.alloc<float>((size_t)n * V * Hc);
   float* rows = arena.alloc<float>((size_t)V * H);

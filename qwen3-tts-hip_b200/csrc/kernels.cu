@@ -613,16 +613,23 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
       if (tok == a.eos_token) a.st->halt = 1;
     }
   } else if (cp) {
-    if (a.qkv_table) {
+    // Every read that depends on the token is issued before any store, so
+    // the table rows and the embedding row arrive in one memory round trip.
+    constexpr int kQIt = kCpQkvTableMax / (4 * kThreads), kXIt = kCpXTableMax / (4 * kThreads);
+    float4 qv[kQIt], xv[kXIt];
+    const int nq = a.qkv_table ? a.qkv_w / 4 : 0, nx = a.x_table ? a.x_w / 4 : 0;
+    if (nq) {
       // the next group's layer-0 projections: a row of the precomputed table
       const float4* src = reinterpret_cast<const float4*>(a.qkv_table + (long long)tok * a.qkv_w);
-      float4* dst = reinterpret_cast<float4*>(a.qkv_out);
-      for (int i = tid; i < a.qkv_w / 4; i += kThreads) dst[i] = __ldg(src + i);
-      if (a.x_table) {
-        const float4* xs4 = reinterpret_cast<const float4*>(a.x_table + (long long)tok * a.x_w);
-        float4* xd = reinterpret_cast<float4*>(a.x_out);
-        for (int i = tid; i < a.x_w / 4; i += kThreads) xd[i] = __ldg(xs4 + i);
-      }
+#pragma unroll
+      for (int it = 0; it < kQIt; ++it)
+        if (it * kThreads + tid < nq) qv[it] = __ldg(src + it * kThreads + tid);
+    }
+    if (nx) {
+      const float4* src = reinterpret_cast<const float4*>(a.x_table + (long long)tok * a.x_w);
+#pragma unroll
+      for (int it = 0; it < kXIt; ++it)
+        if (it * kThreads + tid < nx) xv[it] = __ldg(src + it * kThreads + tid);
     }
     const __nv_bfloat16* e = a.cp_emb + (long long)tok * H;
     uint2 ev[kIt];
@@ -631,6 +638,12 @@ __device__ __forceinline__ void head_select_act(const HeadArgs& a, const float* 
       const int i = (it * kThreads + tid) * 4;
       if (i < H) ev[it] = *reinterpret_cast<const uint2*>(e + i);
     }
+#pragma unroll
+    for (int it = 0; it < kQIt; ++it)
+      if (it * kThreads + tid < nq) reinterpret_cast<float4*>(a.qkv_out)[it * kThreads + tid] = qv[it];
+#pragma unroll
+    for (int it = 0; it < kXIt; ++it)
+      if (it * kThreads + tid < nx) reinterpret_cast<float4*>(a.x_out)[it * kThreads + tid] = xv[it];
 #pragma unroll
     for (int it = 0; it < kIt; ++it) {
       const int i = (it * kThreads + tid) * 4;

@@ -69,6 +69,11 @@ enum HeadRole : int {
   ROLE_LOGITS_ONLY = 3,     // debug: logits only
 };
 
+// Widest rows of the precomputed CodePredictor tables a token head copies
+// (layer-0 QKV row, projected input row), in floats.
+constexpr int kCpQkvTableMax = 4096;
+constexpr int kCpXTableMax = 2048;
+
 struct HeadArgs {
   LinearArgs lin;         // M = 1 projection to logits (lin.y = logits)
   unsigned* ticket;       // zero-initialised counter (reset by the last CTA)
