@@ -205,6 +205,49 @@ __global__ void __launch_bounds__(kThreads) k_linear(LinearArgs a) {
   linear_body<MT, RPW, EPI>(a, reinterpret_cast<float*>(dyn4), s_inv);
 }
 
+// CodePredictor attention (at most kCpFusedPositions positions) computed by
+// every CTA of the O projection while it stages its input: warp w handles kv
+// head w (and w + 8, ...) with its two q heads; lane l holds dims 4l..4l+3.
+// QK-RMSNorm, RoPE, the bf16 round of the new K/V row and the softmax follow
+// the standalone decode-attention kernel; CTA 0 appends the row to the cache.
+constexpr int kCpFusedPositions = 16;
+
+// The cached keys / values of kv head g (positions < pos) and the constant
+// norm and RoPE rows one lane needs. The cached rows were written by the
+// attention of earlier CodePredictor groups, at least four launches back;
+// a kernel only starts once the kernel two places before it has completed
+// (every launch triggers its dependents after its own dependency wait), so
+// these loads may be issued before this kernel's wait, overlapping its
+// predecessor, like the weight loads.
+struct CpAttnRows {
+  uint2 kc[kCpFusedPositions], vc[kCpFusedPositions];
+  float4 qg, kg, rc, rs;
+};
+
+__device__ __forceinline__ void load_cp_attention_rows(const AttnDecodeArgs& at, int g,
+                                                       CpAttnRows& r) {
+  const int lane = threadIdx.x & 31, pos = at.pos_const, d0 = 4 * lane;
+  // With a known page the cached rows are read without the table lookup.
+  const __nv_bfloat16* kbase =
+      at.page0 >= 0 ? at.kv.pool + (long long)at.page0 * at.kv.page_stride +
+                          (long long)at.layer * at.kv.layer_stride +
+                          ((long long)g << at.kv.page_shift) * kHeadDim
+                    : nullptr;
+  const long long vofs = ((long long)at.kv.kv_heads << at.kv.page_shift) * kHeadDim;
+#pragma unroll
+  for (int p = 0; p < kCpFusedPositions; ++p) {
+    if (p < pos) {
+      const __nv_bfloat16* kp = kbase ? kbase + (long long)p * kHeadDim : kv_ptr(at.kv, at.layer, 0, g, p);
+      const __nv_bfloat16* vp = kbase ? kbase + vofs + (long long)p * kHeadDim : kv_ptr(at.kv, at.layer, 1, g, p);
+      r.kc[p] = *reinterpret_cast<const uint2*>(kp + d0);
+      r.vc[p] = *reinterpret_cast<const uint2*>(vp + d0);
+    }
+  }
+  r.qg = __ldg(reinterpret_cast<const float4*>(at.q_gamma + d0));
+  r.kg = __ldg(reinterpret_cast<const float4*>(at.k_gamma + d0));
+  r.rc = __ldg(reinterpret_cast<const float4*>(at.rope_cos + pos * 64 + (d0 & 63)));
+  r.rs = __ldg(reinterpret_cast<const float4*>(at.rope_sin + pos * 64 + (d0 & 63)));
+}
 
 // ---------------------------------------------------------------------------
 // Decode GEMV (one activation row). Every lane owns KCH 16-byte chunks of
@@ -217,7 +260,8 @@ __global__ void __launch_bounds__(kThreads) k_linear(LinearArgs a) {
 // `xs` holds KCH * 256 floats + 32 words of reduction scratch.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, float* xs, int halted,
-                                                   int trace_id, unsigned long long tw);
+                                                   int trace_id, unsigned long long tw,
+                                                   CpAttnRows& r);
 
 template <int KCH, int NR, bool ATTN = false, int MR = 1>
 __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* xs,
@@ -242,6 +286,10 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
 #pragma unroll
     for (int j = 0; j < KCH; ++j) w[r][j] = ldg_stream(src + j * 256, pol);
   }
+  CpAttnRows attn_rows;
+  if constexpr (ATTN) {
+    if (warp < at->kv.kv_heads) load_cp_attention_rows(*at, warp, attn_rows);
+  }
   // A branch (never taken) between the weight loads and the dependency wait
   // keeps the two in separate basic blocks, so the SASS scheduler cannot sink
   // the loads past the wait: with both in one block the loads were issued
@@ -260,7 +308,7 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
   const int halted = a.halt ? __ldcg(a.halt) : 0;
   float* red = xs + MR * K;  // [MR][kWarps] partial sums of squares
   if (ATTN) {
-    stage_cp_attention(*at, xs, halted, a.trace_id, tw);
+    stage_cp_attention(*at, xs, halted, a.trace_id, tw, attn_rows);
   } else {
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
@@ -352,47 +400,26 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
   return true;
 }
 
-// CodePredictor attention (at most kCpFusedPositions positions) computed by
-// every CTA of the O projection while it stages its input: warp w handles kv
-// head w (and w + 8, ...) with its two q heads; lane l holds dims 4l..4l+3.
-// QK-RMSNorm, RoPE, the bf16 round of the new K/V row and the softmax follow
-// the standalone decode-attention kernel; CTA 0 appends the row to the cache.
-constexpr int kCpFusedPositions = 16;
-
+// `r` holds kv head `warp`'s rows, loaded before the dependency wait (and
+// is reloaded for any further head of the warp).
 __device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, float* xs, int halted,
-                                                   int trace_id, unsigned long long tw) {
+                                                   int trace_id, unsigned long long tw,
+                                                   CpAttnRows& r) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pos = at.pos_const, T = pos + 1;
   const int kvh = at.kv.kv_heads;
   const int q_out = at.q_heads * kHeadDim, kv_out = kvh * kHeadDim;
   const int d0 = 4 * lane;
   for (int g = warp; g < kvh; g += kWarps) {
-    uint2 kc[kCpFusedPositions], vc[kCpFusedPositions];
-    // With a known page the cached rows are read without the table lookup.
-    const __nv_bfloat16* kbase =
-        at.page0 >= 0 ? at.kv.pool + (long long)at.page0 * at.kv.page_stride +
-                            (long long)at.layer * at.kv.layer_stride +
-                            ((long long)g << at.kv.page_shift) * kHeadDim
-                      : nullptr;
-    const long long vofs = ((long long)at.kv.kv_heads << at.kv.page_shift) * kHeadDim;
-#pragma unroll
-    for (int p = 0; p < kCpFusedPositions; ++p) {
-      if (p < pos) {
-        const __nv_bfloat16* kp = kbase ? kbase + (long long)p * kHeadDim : kv_ptr(at.kv, at.layer, 0, g, p);
-        const __nv_bfloat16* vp = kbase ? kbase + vofs + (long long)p * kHeadDim : kv_ptr(at.kv, at.layer, 1, g, p);
-        kc[p] = *reinterpret_cast<const uint2*>(kp + d0);
-        vc[p] = *reinterpret_cast<const uint2*>(vp + d0);
-      }
-    }
+    if (g != warp) load_cp_attention_rows(at, g, r);
+    const uint2* kc = r.kc;
+    const uint2* vc = r.vc;
+    const float4 qg = r.qg, kg = r.kg, rc = r.rc, rs = r.rs;
     float4 q[2];
     q[0] = __ldcg(reinterpret_cast<const float4*>(at.qkv + (2 * g) * kHeadDim + d0));
     q[1] = __ldcg(reinterpret_cast<const float4*>(at.qkv + (2 * g + 1) * kHeadDim + d0));
     float4 kk = __ldcg(reinterpret_cast<const float4*>(at.qkv + q_out + g * kHeadDim + d0));
     const float4 vv = __ldcg(reinterpret_cast<const float4*>(at.qkv + q_out + kv_out + g * kHeadDim + d0));
-    const float4 qg = __ldg(reinterpret_cast<const float4*>(at.q_gamma + d0));
-    const float4 kg = __ldg(reinterpret_cast<const float4*>(at.k_gamma + d0));
-    const float4 rc = __ldg(reinterpret_cast<const float4*>(at.rope_cos + pos * 64 + (d0 & 63)));
-    const float4 rs = __ldg(reinterpret_cast<const float4*>(at.rope_sin + pos * 64 + (d0 & 63)));
     auto norm_rope = [&](float4 x, float4 gm) {
       const float ss = warp_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
       const float inv = rsqrtf(ss / (float)kHeadDim + at.eps);
@@ -478,7 +505,7 @@ __device__ __forceinline__ void stage_cp_attention(const AttnDecodeArgs& at, flo
 }
 
 template <int KCH>
-__global__ void __launch_bounds__(kThreads) k_gemv1_attn(LinearArgs a, AttnDecodeArgs at) {
+__global__ void __maxnreg__(200) k_gemv1_attn(LinearArgs a, AttnDecodeArgs at) {
   QTTS_CRUMB(0, 11);
   __shared__ __align__(16) float xs[KCH * 256 + 32];
   gemv1_body<KCH, 1, true>(a, EPI_RESID, xs, nullptr, &at);
