@@ -772,9 +772,13 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
   __shared__ float wm[NW][G], wl[NW][G];
   __shared__ float wacc[NW][G][kHeadDim];
   trace_mark(a.trace_id, 0);
-  pdl_wait();
-  trace_mark(a.trace_id, 1);
-  // halt, position and the projections are independent loads: issue together
+  // Before the dependency wait: the halt flag (written only by a frame's last
+  // kernel), the position (written by the CodePredictor's last head, at least
+  // two launches back), the first batch of cached rows (earlier positions,
+  // written by earlier steps) and the constant norm / RoPE rows. A kernel
+  // starts only after the kernel two places before it has completed, since
+  // every launch triggers its dependents after its own wait; only this
+  // step's projections come from the immediately preceding kernel.
   const int seq = blockIdx.y;
   const int halted = a.halt ? __ldcg(a.halt + seq * a.halt_stride) : 0;
   const int h = blockIdx.x, tid = threadIdx.x;
@@ -786,14 +790,6 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
   const int T = pos + 1;
   const int kvh = a.kv.kv_heads;
   const int q_out = a.q_heads * kHeadDim, kv_out = kvh * kHeadDim;
-
-  float qr[G], kr = 0.f, vr = 0.f;
-  if (tid < kHeadDim) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) qr[g] = __ldcg(a.qkv + (h * G + g) * kHeadDim + tid);
-    kr = __ldcg(a.qkv + q_out + h * kHeadDim + tid);
-    vr = __ldcg(a.qkv + q_out + kv_out + h * kHeadDim + tid);
-  }
   // Rows before `pos` come from the cache; the current row from shared memory.
   auto load = [&](int p0, uint2 (&ku)[kAttnBatch], uint2 (&vu)[kAttnBatch]) {
 #pragma unroll
@@ -817,6 +813,18 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(AttnDecodeArgs a) {
     rsn = a.rope_sin[pos * 64 + (tid & 63)];
     qgam = a.q_gamma[tid];
     kgam = a.k_gamma[tid];
+  }
+  // A branch (never taken) keeps the loads above in their own basic block,
+  // so the SASS scheduler cannot sink them past the wait.
+  if (a.layer < 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.qkv) : "memory");
+  pdl_wait();
+  trace_mark(a.trace_id, 1);
+  float qr[G], kr = 0.f, vr = 0.f;
+  if (tid < kHeadDim) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) qr[g] = __ldcg(a.qkv + (h * G + g) * kHeadDim + tid);
+    kr = __ldcg(a.qkv + q_out + h * kHeadDim + tid);
+    vr = __ldcg(a.qkv + q_out + kv_out + h * kHeadDim + tid);
   }
   if (halted) return;
   if (tid < kHeadDim) {
