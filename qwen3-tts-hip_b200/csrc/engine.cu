@@ -881,8 +881,9 @@ class Engine {
   // ---- launch helpers ----
   void linear(const __nv_bfloat16* W, const float* x, int ldx, const float* gamma, float eps,
               float* y, int ldy, const float* resid, int ldr, const float* bias, int M, int N,
-              int K, Epilogue epi, const int* halt) {
+              int K, Epilogue epi, const int* halt, bool resid_early = false) {
     LinearArgs a{W, x, ldx, gamma, eps, y, ldy, resid, ldr, bias, M, N, K, halt};
+    a.resid_early = resid_early;
     if (tc_scope && tc.tokens && tc_supported(a, epi, tc)) {
       QCK(launch_linear_tc(a, epi, tc, nullptr, tc_err, stream));  // tcgen05 GEMM
       launches += 1;
@@ -899,8 +900,9 @@ class Engine {
     const StackCfg& c = S.c;
     linear(S.wgu[l], B.h1, c.hidden, S.post_g[l], c.eps, B.act, c.intermediate, nullptr, 0,
            nullptr, 1, c.intermediate, c.hidden, EPI_SWIGLU, halt);
+    // B.h1 comes from the O projection, two launches back
     linear(S.wdown[l], B.act, c.intermediate, nullptr, 0.f, B.x, c.hidden, B.h1, c.hidden,
-           nullptr, 1, c.hidden, c.intermediate, EPI_RESID, halt);
+           nullptr, 1, c.hidden, c.intermediate, EPI_RESID, halt, true);
   }
 
   // ---- step trace (QTTS_STEP_TRACE=<file>, or qtts_step_trace_enable) ----
@@ -1375,6 +1377,11 @@ void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* 
                       B.attn,  halt};
     LinearArgs o{S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden,
                  nullptr, 1, c.hidden, S.q_out, halt};
+    // The O projection's residual B.x (the layer input) was written at least
+    // two launches back (previous layer's down projection, or the step input
+    // before this layer's QKV), except for layer 0 of a CodePredictor group
+    // whose QKV row came from the table: the preceding head wrote B.x.
+    o.resid_early = !(l == 0 && qkv0_given);
     if (fuse_attn_o && attn_o_fusable(da, o)) {
       if (&S == &cp) da.page0 = 0;  // the CodePredictor cache is one page (page 0)
       o.trace_id = trace_tag("attn+o+resid", c.hidden, S.q_out);
@@ -1385,7 +1392,7 @@ void Engine::stack_step(DevStack& S, StackBufs& B, const KvView& kv, const int* 
       QCK(launch_attn_decode(da, stream));
       ++launches;
       linear(S.wo[l], B.attn, S.q_out, nullptr, 0.f, B.h1, c.hidden, B.x, c.hidden, nullptr, 1,
-             c.hidden, S.q_out, EPI_RESID, halt);
+             c.hidden, S.q_out, EPI_RESID, halt, o.resid_early);
     }
     mlp(S, l, B, halt);
   }

@@ -286,6 +286,15 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
 #pragma unroll
     for (int j = 0; j < KCH; ++j) w[r][j] = ldg_stream(src + j * 256, pol);
   }
+  // residual values of this warp's outputs (lane 0), when known to be final
+  const bool early_r = epi == EPI_RESID && a.resid_early;
+  float rv[MR][NR];
+#pragma unroll
+  for (int m = 0; m < MR; ++m)
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+      rv[m][r] = early_r && lane == 0 && valid[r] ? __ldcg(a.resid + (long long)m * a.ldr + c0 + r)
+                                                  : 0.f;
   CpAttnRows attn_rows;
   if constexpr (ATTN) {
     if (warp < at->kv.kv_heads) load_cp_attention_rows(*at, warp, attn_rows);
@@ -388,7 +397,7 @@ __device__ __forceinline__ bool gemv1_body(const LinearArgs& a, int epi, float* 
           if (!valid[r]) continue;
           const int c = c0 + r;
           float out = acc[m][r] * sc[m];
-          if (epi == EPI_RESID) out += __ldcg(a.resid + (long long)m * a.ldr + c);
+          if (epi == EPI_RESID) out += early_r ? rv[m][r] : __ldcg(a.resid + (long long)m * a.ldr + c);
           if (epi == EPI_BIAS) out += a.bias[c];
           if (epi == EPI_BIAS_SILU) out = silu(out + a.bias[c]);
           y[c] = out;

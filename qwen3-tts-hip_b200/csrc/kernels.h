@@ -34,6 +34,10 @@ struct LinearArgs {
   int M, N, K;
   const int* halt;         // optional: kernel is a no-op while *halt != 0
   int trace_id;            // > 0: record entry / dependency-wait / exit times (step trace)
+  // EPI_RESID: the residual rows were written at least two launches back, so
+  // the kernel may read them before its dependency wait (a kernel starts only
+  // after the kernel two places before it has completed).
+  int resid_early;
 };
 
 // Sampling parameters of one token kind (talker or subtalker).
